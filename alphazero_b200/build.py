@@ -1,0 +1,102 @@
+"""Builds the package's native libraries in-tree (alphazero_b200/lib/).
+
+  libminigo_cuda.so  CUDA kernels for sm_100a + engine + C ABI
+                     (include/minigo_cuda.h); nvcc, static cudart.
+  libminigo_host.so  CPU-only helpers (include/minigo_host.h): position
+                     generator and ONNX reader; g++.
+
+Run as ``python -m alphazero_b200.build``.  Rebuilds a library only when one
+of its sources is newer than it.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+LIB = os.path.join(PKG, "lib")
+CSRC = os.path.join(PKG, "csrc")
+HOST = os.path.join(PKG, "host")
+INCLUDE = os.path.join(ROOT, "include")
+
+CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
+GENCODE = "-gencode=arch=compute_100a,code=sm_100a"
+
+CUDA_SOURCES = [
+    os.path.join(CSRC, "conv_tc.cu"),
+    os.path.join(CSRC, "conv_simt.cu"),
+    os.path.join(CSRC, "stage_heads.cu"),
+    os.path.join(CSRC, "engine.cu"),
+    os.path.join(HOST, "net_weights.cpp"),
+    os.path.join(HOST, "onnx_reader.cpp"),
+]
+CUDA_HEADERS = [
+    os.path.join(CSRC, "kernels.cuh"),
+    os.path.join(CSRC, "ptx_sm100.cuh"),
+    os.path.join(HOST, "net_weights.h"),
+    os.path.join(HOST, "onnx_reader.h"),
+    os.path.join(INCLUDE, "minigo_cuda.h"),
+]
+HOST_SOURCES = [
+    os.path.join(HOST, "go_positions.cpp"),
+    os.path.join(HOST, "onnx_reader.cpp"),
+    os.path.join(HOST, "c_api_host.cpp"),
+]
+HOST_HEADERS = [
+    os.path.join(HOST, "go_positions.h"),
+    os.path.join(HOST, "onnx_reader.h"),
+    os.path.join(INCLUDE, "minigo_host.h"),
+]
+
+CUDA_LIB = os.path.join(LIB, "libminigo_cuda.so")
+HOST_LIB = os.path.join(LIB, "libminigo_host.so")
+
+
+def _stale(target: str, deps: list[str]) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def _run(cmd: list[str]) -> None:
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("build failed:\n" + " ".join(cmd) + "\n" + r.stdout + r.stderr)
+
+
+def build_host(force: bool = False) -> str:
+    os.makedirs(LIB, exist_ok=True)
+    if force or _stale(HOST_LIB, HOST_SOURCES + HOST_HEADERS):
+        tmp = HOST_LIB + ".tmp"
+        _run(["g++", "-std=c++17", "-O3", "-fPIC", "-shared", "-Wall", "-Wextra",
+              "-o", tmp] + HOST_SOURCES + ["-lpthread"])
+        os.replace(tmp, HOST_LIB)
+    return HOST_LIB
+
+
+def build_cuda(force: bool = False) -> str:
+    os.makedirs(LIB, exist_ok=True)
+    if force or _stale(CUDA_LIB, CUDA_SOURCES + CUDA_HEADERS):
+        if not os.path.exists(NVCC) and shutil.which("nvcc") is None:
+            raise RuntimeError("nvcc not found; set CUDA_HOME")
+        nvcc = NVCC if os.path.exists(NVCC) else "nvcc"
+        tmp = CUDA_LIB + ".tmp"
+        _run([nvcc, GENCODE, "-O3", "-lineinfo", "-std=c++17", "-shared",
+              "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+              "-o", tmp] + CUDA_SOURCES)
+        os.replace(tmp, CUDA_LIB)
+    return CUDA_LIB
+
+
+def build_all(force: bool = False) -> list[str]:
+    return [build_host(force), build_cuda(force)]
+
+
+if __name__ == "__main__":
+    for p in build_all(force="--force" in sys.argv):
+        print(p)

@@ -1,0 +1,406 @@
+// 3x3 convolution as an implicit GEMM on the sm_100a tensor cores.
+//
+// GEMM view (the dominant cost of the reference forward pass,
+// src/eigen_engine.cpp:174-178, there one position at a time):
+//   M = positions * IS framed pixels, N = output channels,
+//   K = 9 taps * input channels.
+// Because of the framed layout, the A tile of tap (dy, dx) for output rows
+// [m0, m0 + 128) is simply rows [m0 + dy*RS + dx, ... + 128) of the input
+// activation matrix, so every K block is one 2-D TMA box (64 channels x 128
+// rows, 128-byte swizzle) with no gather and no im2col buffer.  Weights are
+// [cout][9][cin], so a K block of B is a (64 x bn) box at column
+// tap*cin + channel block.
+//
+// One persistent CTA per SM, warp-specialised:
+//   warp 0     TMA producer (one thread) filling a STAGES-deep smem ring;
+//   warp 1     TMEM allocator and MMA issuer (one thread): 4 x
+//              tcgen05.mma.kind::f16 (128 x bn x 16) per K block, fp32
+//              accumulators in TMEM, double-buffered across tiles;
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator, folded-BN bias,
+//              residual add, ReLU, frame masking, 16-bit store.
+// The epilogue of tile t overlaps the main loop of tile t+1.
+// Every mbarrier wait is bounded (ptx_sm100.cuh); on expiry the kernel
+// records an error code, drains its in-flight copies and frees TMEM.
+#include "kernels.cuh"
+#include "ptx_sm100.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <type_traits>
+
+namespace mgb {
+namespace {
+
+constexpr int kBM = 128;  // rows per tile (TMEM lanes)
+constexpr int kBK = 64;   // K elements per stage (128 bytes of 16-bit data)
+constexpr int kThreads = 192;
+
+template <int BN>
+struct TcConfig {
+    static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr uint32_t kABytes = kBM * kBK * 2;
+    static constexpr uint32_t kBBytes = BN * kBK * 2;
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr uint32_t kTmemCols = 2 * BN;
+    // ring + barriers + tmem slot + bias (256 floats) + 1 KB alignment slack
+    static constexpr int kSmem = kStages * kStageBytes + 256 + 1024 + 1024;
+};
+
+struct TcArgs {
+    int m_total;
+    int num_tiles;
+    int nsplit;  // cout / BN
+    int cin;
+    int cout;
+    int rs, is, board;
+    const float* bias;
+    const void* residual;
+    void* out;
+    int* err;
+};
+
+template <bool FP16>
+struct Act16;
+template <>
+struct Act16<false> {
+    using T = __nv_bfloat16;
+    static __device__ __forceinline__ uint32_t pack(float a, float b) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    static __device__ __forceinline__ float2 unpack(uint32_t u) {
+        __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
+        return __bfloat1622float2(h);
+    }
+};
+template <>
+struct Act16<true> {
+    using T = __half;
+    static __device__ __forceinline__ uint32_t pack(float a, float b) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    static __device__ __forceinline__ float2 unpack(uint32_t u) {
+        __half2 h = *reinterpret_cast<__half2*>(&u);
+        return __half22float2(h);
+    }
+};
+
+template <int BN, bool FP16>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv3x3_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
+    using Cfg = TcConfig<BN>;
+    using P = Act16<FP16>;
+    constexpr int S = Cfg::kStages;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + S * Cfg::kABytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + S;
+    uint64_t* tfull = bars + 2 * S;
+    uint64_t* tempty = bars + 2 * S + 2;
+    uint64_t* done = bars + 2 * S + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+    float* sbias = reinterpret_cast<float*>(tmem_slot + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&tfull[i]), 1);
+            mbar_init(smem_u32(&tempty[i]), 4);
+        }
+        mbar_init(smem_u32(done), 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    for (int i = threadIdx.x; i < a.cout; i += kThreads) sbias[i] = a.bias[i];
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int cblocks = a.cin / kBK;
+    const int kblocks = 9 * cblocks;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            prefetch_tensormap(&tmA);
+            prefetch_tensormap(&tmB);
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
+                const int mt = tile / a.nsplit;
+                const int n0 = (tile - mt * a.nsplit) * BN;
+                const int m0 = mt * kBM;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int tap = kb / cblocks;
+                    const int cb = kb - tap * cblocks;
+                    const int off = (tap / 3 - 1) * a.rs + (tap % 3 - 1);
+                    const int s = it % S;
+                    const uint32_t ph = ((it / S) & 1) ^ 1;
+                    if (!mbar_wait(smem_u32(&empty[s]), ph, a.err, kErrWaitProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = smem_u32(&full[s]);
+                    mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+                    tma_load_2d(smem_u32(sA + s * Cfg::kABytes), &tmA, fb, cb * kBK, m0 + off);
+                    tma_load_2d(smem_u32(sB + s * Cfg::kBBytes), &tmB, fb, tap * a.cin + cb * kBK,
+                                n0);
+                }
+            }
+            // Drain: every copy issued into the ring has landed before exit.
+            for (int j = (it > S ? it - S : 0); j < it; ++j)
+                mbar_wait(smem_u32(&full[j % S]), (j / S) & 1, a.err, kErrWaitDrain);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(kBM, BN, !FP16);
+            int it = 0, t = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++t) {
+                const int acc = t & 1;
+                if (!mbar_wait(smem_u32(&tempty[acc]), ((t >> 1) & 1) ^ 1, a.err, kErrWaitMma)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % S;
+                    if (!mbar_wait(smem_u32(&full[s]), (it / S) & 1, a.err, kErrWaitMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * Cfg::kABytes));
+                    const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * Cfg::kBBytes));
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k) {
+                        // advance 16 elements (32 bytes) along K inside the swizzle atom
+                        mma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                                (kb | k) != 0);
+                    }
+                    mma_commit(smem_u32(&empty[s]));
+                }
+                if (ok) mma_commit(smem_u32(&tfull[acc]));
+            }
+            // All MMAs complete before TMEM is released.
+            mma_commit(smem_u32(done));
+            mbar_wait(smem_u32(done), 0, a.err, kErrWaitDrain);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+        const int row = quarter * 32 + lane;
+        using T = typename P::T;
+        int t = 0;
+        for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++t) {
+            const int mt = tile / a.nsplit;
+            const int n0 = (tile - mt * a.nsplit) * BN;
+            const int acc = t & 1;
+            if (!mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, a.err, kErrWaitEpilogue)) break;
+            tc_fence_after();
+            const int m = mt * kBM + row;
+            const bool in_range = m < a.m_total;
+            bool board_px = false;
+            if (in_range) {
+                const int q = m % a.is;
+                const int y = q / a.rs;
+                const int x = q - y * a.rs;
+                board_px = (y < a.board) && (x < a.board);
+            }
+            T* out_row = reinterpret_cast<T*>(a.out) + (size_t)m * a.cout + n0;
+            const T* res_row = a.residual == nullptr
+                                   ? nullptr
+                                   : reinterpret_cast<const T*>(a.residual) + (size_t)m * a.cout + n0;
+            const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld_32cols(tbase + (uint32_t)c0, v);
+                tmem_ld_wait();
+                if (in_range) {
+                    float f[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + sbias[n0 + c0 + j];
+                    if (res_row != nullptr) {
+                        const uint4* rp = reinterpret_cast<const uint4*>(res_row + c0);
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            uint4 r = rp[q4];
+                            float2 r0 = P::unpack(r.x), r1 = P::unpack(r.y);
+                            float2 r2 = P::unpack(r.z), r3 = P::unpack(r.w);
+                            f[q4 * 8 + 0] += r0.x; f[q4 * 8 + 1] += r0.y;
+                            f[q4 * 8 + 2] += r1.x; f[q4 * 8 + 3] += r1.y;
+                            f[q4 * 8 + 4] += r2.x; f[q4 * 8 + 5] += r2.y;
+                            f[q4 * 8 + 6] += r3.x; f[q4 * 8 + 7] += r3.y;
+                        }
+                    }
+                    uint4* op = reinterpret_cast<uint4*>(out_row + c0);
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        float g[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            g[j] = board_px ? fmaxf(f[q4 * 8 + j], 0.0f) : 0.0f;
+                        uint4 w;
+                        w.x = P::pack(g[0], g[1]);
+                        w.y = P::pack(g[2], g[3]);
+                        w.z = P::pack(g[4], g[5]);
+                        w.w = P::pack(g[6], g[7]);
+                        op[q4] = w;
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+template <int BN, bool FP16>
+cudaError_t launch_bn(const ConvLayer& L, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                      int grid_limit, cudaStream_t stream) {
+    using Cfg = TcConfig<BN>;
+    TcArgs a;
+    a.m_total = L.m_total;
+    a.nsplit = L.cout / BN;
+    a.num_tiles = ((L.m_total + kBM - 1) / kBM) * a.nsplit;
+    a.cin = L.cin;
+    a.cout = L.cout;
+    a.rs = L.g.rs;
+    a.is = L.g.is;
+    a.board = L.g.board;
+    a.bias = L.bias;
+    a.residual = L.residual;
+    a.out = L.out;
+    a.err = L.err;
+    int grid = a.num_tiles < grid_limit ? a.num_tiles : grid_limit;
+    if (grid < 1) grid = 1;
+    conv3x3_tc_kernel<BN, FP16><<<grid, kThreads, Cfg::kSmem, stream>>>(tmA, tmB, a);
+    return cudaGetLastError();
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+bool encode_2d(CUtensorMap* map, bool fp16, const void* base, uint64_t inner, uint64_t rows,
+               uint32_t box_inner, uint32_t box_rows, const char** why) {
+    auto enc = tensor_map_encoder();
+    if (enc == nullptr) {
+        *why = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * 2};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                     2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        *why = "cuTensorMapEncodeTiled rejected the tensor map";
+        return false;
+    }
+    return true;
+}
+
+template <int BN, bool FP16>
+cudaError_t configure_one() {
+    return cudaFuncSetAttribute(conv3x3_tc_kernel<BN, FP16>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, TcConfig<BN>::kSmem);
+}
+
+}  // namespace
+
+cudaError_t configure_conv_tc() {
+    cudaError_t e;
+    if ((e = configure_one<64, false>()) != cudaSuccess) return e;
+    if ((e = configure_one<128, false>()) != cudaSuccess) return e;
+    if ((e = configure_one<256, false>()) != cudaSuccess) return e;
+    if ((e = configure_one<64, true>()) != cudaSuccess) return e;
+    if ((e = configure_one<128, true>()) != cudaSuccess) return e;
+    return configure_one<256, true>();
+}
+
+int conv_tc_smem_bytes(int bn) {
+    switch (bn) {
+        case 64: return TcConfig<64>::kSmem;
+        case 128: return TcConfig<128>::kSmem;
+        case 256: return TcConfig<256>::kSmem;
+        default: return -1;
+    }
+}
+
+bool make_conv_tensor_maps(const ConvLayer& L, int bn, bool fp16, CUtensorMap* tmA,
+                           CUtensorMap* tmB, const char** why) {
+    if (L.cin % kBK != 0 || L.cout % bn != 0 || bn % 64 != 0 || bn > 256) {
+        *why = "unsupported channel counts for the tensor-core convolution";
+        return false;
+    }
+    if (!encode_2d(tmA, fp16, L.in, (uint64_t)L.cin, (uint64_t)L.m_total, kBK, kBM, why))
+        return false;
+    return encode_2d(tmB, fp16, L.weight, (uint64_t)9 * L.cin, (uint64_t)L.cout, kBK,
+                     (uint32_t)bn, why);
+}
+
+cudaError_t launch_conv_tc(const ConvLayer& L, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                           int bn, bool fp16, int grid_limit, cudaStream_t stream) {
+    if (fp16) {
+        switch (bn) {
+            case 64: return launch_bn<64, true>(L, tmA, tmB, grid_limit, stream);
+            case 128: return launch_bn<128, true>(L, tmA, tmB, grid_limit, stream);
+            case 256: return launch_bn<256, true>(L, tmA, tmB, grid_limit, stream);
+        }
+    } else {
+        switch (bn) {
+            case 64: return launch_bn<64, false>(L, tmA, tmB, grid_limit, stream);
+            case 128: return launch_bn<128, false>(L, tmA, tmB, grid_limit, stream);
+            case 256: return launch_bn<256, false>(L, tmA, tmB, grid_limit, stream);
+        }
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace mgb

@@ -1,0 +1,740 @@
+// The network-evaluation engine behind the C ABI of include/minigo_cuda.h.
+//
+// Load time (src/eigen_engine.cpp:17-121 semantics): named fp32 tensors ->
+// HostNet (architecture inference + BN fold) -> device weights with the BN
+// scale folded into each conv's output channels, reordered to
+// [cout][tap][cin] with channels zero-padded to multiples of 64, in the
+// trunk's arithmetic type; heads stay fp32.
+//
+// Run time, per batch of n positions (n <= max batch):
+//   stage kernel (fp32 planes -> framed NHWC), then one CUDA graph per
+//   batch-size bucket holding 1 + 2*blocks convolution launches and the heads
+//   launch; host callers add one H2D copy before and D2H copies after, all on
+//   the engine's own stream.  Positions between n and the bucket size are
+//   computed on zero input and discarded.
+#include "../../include/minigo_cuda.h"
+#include "../host/net_weights.h"
+#include "../host/onnx_reader.h"
+#include "kernels.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <utility>
+#include <vector>
+
+using namespace mgb;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+constexpr int kStagedChannels = 64;  // input planes padded to one 64-channel K block
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+struct CudaFailure {
+    cudaError_t code;
+    std::string where;
+};
+
+void ck(cudaError_t e, const char* where) {
+    if (e != cudaSuccess) throw CudaFailure{e, where};
+}
+
+template <typename T>
+T* dalloc(size_t count, const char* what) {
+    void* p = nullptr;
+    if (count == 0) count = 1;
+    ck(cudaMalloc(&p, count * sizeof(T)), what);
+    return reinterpret_cast<T*>(p);
+}
+
+}  // namespace
+
+struct mg_engine {
+    int device = 0;
+    int flags = 0;
+    int precision = MG_PREC_BF16;
+    int max_batch = 1024;
+    int num_sms = 148;
+    int conv_bn_override = 0;
+    bool use_graphs = true;
+    cudaStream_t stream = nullptr;
+    std::string err;
+
+    bool loaded = false;
+    HostNet net;
+    FrameGeom g{};
+    int hw = 0, planes = 0, cpad = 0, actions = 0;
+    int n_convs = 0;
+
+    // Folded fp32 conv weights [cpad][9][cin_pad] and biases [cpad] (host).
+    std::vector<std::vector<float>> wf;
+    std::vector<int> wcin;  // cin_pad per conv
+    std::vector<std::vector<float>> bf;
+
+    // Device weights.
+    std::vector<void*> d_w16;  // current 16-bit type (w16_prec)
+    int w16_prec = -1;
+    std::vector<float*> d_w32;
+    std::vector<float*> d_bias;
+    float* d_head = nullptr;
+    HeadParams hp{};
+
+    // Device buffers for `alloc_batch` positions, element size `alloc_elem`.
+    int alloc_batch = 0;
+    int alloc_elem = 0;
+    void* d_stage = nullptr;
+    void* d_x = nullptr;
+    void* d_t = nullptr;
+    float* d_states = nullptr;
+    float* d_probs = nullptr;
+    float* d_logits = nullptr;
+    float* d_value = nullptr;
+    int* d_err = nullptr;
+    float* h_states = nullptr;  // pinned staging for pageable inputs
+    int* h_err = nullptr;       // pinned status word
+
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (bucket, precision)
+    int last_bucket = 0;
+
+    ~mg_engine() { release_all(); }
+
+    void drop_graphs() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        graphs.clear();
+    }
+
+    void free_buffers() {
+        drop_graphs();
+        for (void* p : {d_stage, d_x, d_t}) if (p) cudaFree(p);
+        for (void* p : {(void*)d_states, (void*)d_probs, (void*)d_logits, (void*)d_value, (void*)d_err})
+            if (p) cudaFree(p);
+        if (h_states) cudaFreeHost(h_states);
+        if (h_err) cudaFreeHost(h_err);
+        d_stage = d_x = d_t = nullptr;
+        d_states = d_probs = d_logits = d_value = nullptr;
+        d_err = nullptr;
+        h_states = nullptr;
+        h_err = nullptr;
+        alloc_batch = 0;
+        alloc_elem = 0;
+    }
+
+    void free_weights() {
+        drop_graphs();
+        for (void* p : d_w16) if (p) cudaFree(p);
+        for (float* p : d_w32) if (p) cudaFree(p);
+        for (float* p : d_bias) if (p) cudaFree(p);
+        if (d_head) cudaFree(d_head);
+        d_w16.clear();
+        d_w32.clear();
+        d_bias.clear();
+        d_head = nullptr;
+        w16_prec = -1;
+    }
+
+    void release_all() {
+        DeviceGuard dg(device);
+        free_buffers();
+        free_weights();
+        if (stream) cudaStreamDestroy(stream);
+        stream = nullptr;
+    }
+
+    int elem_bytes() const { return precision == MG_PREC_FP32 ? 4 : 2; }
+    ActType act_type() const {
+        return precision == MG_PREC_FP32 ? ActType::FP32
+                                         : (precision == MG_PREC_FP16 ? ActType::FP16 : ActType::BF16);
+    }
+
+    // ---- load ----------------------------------------------------------
+
+    void load(const std::vector<TensorView>& views) {
+        HostNet n = build_host_net(views);
+        if (n.input_channels > kStagedChannels)
+            throw std::runtime_error("input_conv.weight has " + std::to_string(n.input_channels) +
+                                     " input channels; at most 64 are supported");
+        if (n.filters > 256)
+            throw std::runtime_error("num_filters " + std::to_string(n.filters) +
+                                     " exceeds the supported maximum of 256");
+        if (n.board > 25) throw std::runtime_error("board sizes above 25 are not supported");
+        if (n.hidden > 1024) throw std::runtime_error("value_fc1 width above 1024 is not supported");
+        free_weights();
+        free_buffers();
+        net = std::move(n);
+        g = make_frame(net.board);
+        hw = net.board * net.board;
+        planes = net.input_channels;
+        cpad = round_up(net.filters, 64);
+        actions = net.actions;
+        n_convs = 1 + 2 * net.blocks;
+
+        // Fold the BN scale into output channels; [cout][cin][3][3] ->
+        // [cpad][tap][cin_pad].
+        wf.assign(n_convs, {});
+        bf.assign(n_convs, {});
+        wcin.assign(n_convs, 0);
+        auto fold = [&](int li, const HostConv& c, int cin_pad) {
+            std::vector<float>& w = wf[li];
+            w.assign((size_t)cpad * 9 * cin_pad, 0.0f);
+            for (int co = 0; co < c.cout; ++co)
+                for (int ci = 0; ci < c.cin; ++ci)
+                    for (int tap = 0; tap < 9; ++tap)
+                        w[((size_t)co * 9 + tap) * cin_pad + ci] =
+                            c.w[((size_t)co * c.cin + ci) * 9 + tap] * c.bn.scale[co];
+            bf[li].assign(cpad, 0.0f);
+            for (int co = 0; co < c.cout; ++co) bf[li][co] = c.bn.bias[co];
+            wcin[li] = cin_pad;
+        };
+        fold(0, net.input, kStagedChannels);
+        for (int b = 0; b < net.blocks; ++b) {
+            fold(1 + 2 * b, net.conv1[b], cpad);
+            fold(2 + 2 * b, net.conv2[b], cpad);
+        }
+
+        DeviceGuard dg(device);
+        d_bias.resize(n_convs, nullptr);
+        for (int li = 0; li < n_convs; ++li) {
+            d_bias[li] = dalloc<float>(cpad, "cudaMalloc(bias)");
+            ck(cudaMemcpy(d_bias[li], bf[li].data(), cpad * sizeof(float), cudaMemcpyHostToDevice),
+               "cudaMemcpy(bias)");
+        }
+        upload_heads();
+        loaded = true;
+        prepare_weights();
+    }
+
+    void upload_heads() {
+        const int A = actions, H = net.hidden, C = cpad;
+        // Policy features are read in c*hw + p order; with eigen_compat the
+        // FC columns are permuted from the column-major flatten c + 2p
+        // (src/eigen_engine.cpp:242) so the kernel is the same.
+        std::vector<float> pfc((size_t)A * 2 * hw);
+        const bool eig = (flags & MG_FLAG_EIGEN_COMPAT) != 0;
+        for (int a = 0; a < A; ++a)
+            for (int c = 0; c < 2; ++c)
+                for (int p = 0; p < hw; ++p) {
+                    const int src = eig ? (c + 2 * p) : (c * hw + p);
+                    pfc[(size_t)a * 2 * hw + c * hw + p] = net.pfc_w[(size_t)a * 2 * hw + src];
+                }
+        std::vector<float> pcw((size_t)2 * C, 0.0f), vcw(C, 0.0f);
+        for (int c = 0; c < 2; ++c)
+            for (int k = 0; k < net.filters; ++k)
+                pcw[(size_t)c * C + k] = net.pconv_w[(size_t)c * net.filters + k] * net.pbn.scale[c];
+        for (int k = 0; k < net.filters; ++k) vcw[k] = net.vconv_w[k] * net.vbn.scale[0];
+        std::vector<std::pair<const float*, size_t>> parts = {
+            {pcw.data(), pcw.size()},          {net.pbn.bias.data(), 2},
+            {vcw.data(), vcw.size()},          {net.vbn.bias.data(), 1},
+            {pfc.data(), pfc.size()},          {net.pfc_b.data(), (size_t)A},
+            {net.v1_w.data(), (size_t)H * hw}, {net.v1_b.data(), (size_t)H},
+            {net.v2_w.data(), (size_t)H},      {net.v2_b.data(), 1}};
+        std::vector<size_t> offs;
+        size_t total = 0;
+        for (auto& pr : parts) {
+            offs.push_back(total);
+            total += (pr.second + 63) / 64 * 64;  // 256-byte aligned pieces
+        }
+        std::vector<float> packed(total, 0.0f);
+        for (size_t i = 0; i < parts.size(); ++i)
+            std::memcpy(packed.data() + offs[i], parts[i].first, parts[i].second * sizeof(float));
+        d_head = dalloc<float>(total, "cudaMalloc(heads)");
+        ck(cudaMemcpy(d_head, packed.data(), total * sizeof(float), cudaMemcpyHostToDevice),
+           "cudaMemcpy(heads)");
+        hp.board = net.board;
+        hp.hw = hw;
+        hp.c = C;
+        hp.actions = A;
+        hp.hidden = H;
+        hp.g = g;
+        hp.pconv_w = d_head + offs[0];
+        hp.pconv_b = d_head + offs[1];
+        hp.vconv_w = d_head + offs[2];
+        hp.vconv_b = d_head + offs[3];
+        hp.pfc_w = d_head + offs[4];
+        hp.pfc_b = d_head + offs[5];
+        hp.v1_w = d_head + offs[6];
+        hp.v1_b = d_head + offs[7];
+        hp.v2_w = d_head + offs[8];
+        hp.v2_b = d_head + offs[9];
+        const size_t smem = heads_smem_bytes(hp);
+        if (smem > 48 * 1024)
+            throw std::runtime_error("board / value-head sizes exceed the heads kernel's shared memory");
+    }
+
+    // Device weights in the current precision's type (16-bit for the tensor
+    // cores, fp32 for the SIMT path).
+    void prepare_weights() {
+        DeviceGuard dg(device);
+        if (precision == MG_PREC_FP32) {
+            if (d_w32.empty()) {
+                d_w32.resize(n_convs, nullptr);
+                for (int li = 0; li < n_convs; ++li) {
+                    d_w32[li] = dalloc<float>(wf[li].size(), "cudaMalloc(w32)");
+                    ck(cudaMemcpy(d_w32[li], wf[li].data(), wf[li].size() * sizeof(float),
+                                  cudaMemcpyHostToDevice),
+                       "cudaMemcpy(w32)");
+                }
+            }
+            return;
+        }
+        if (w16_prec == precision) return;
+        drop_graphs();  // captured graphs hold the old weight pointers
+        for (void* p : d_w16) if (p) cudaFree(p);
+        d_w16.assign(n_convs, nullptr);
+        for (int li = 0; li < n_convs; ++li) {
+            const size_t cnt = wf[li].size();
+            std::vector<uint16_t> h(cnt);
+            if (precision == MG_PREC_BF16) {
+                for (size_t i = 0; i < cnt; ++i) {
+                    __nv_bfloat16 v = __float2bfloat16_rn(wf[li][i]);
+                    std::memcpy(&h[i], &v, 2);
+                }
+            } else {
+                for (size_t i = 0; i < cnt; ++i) {
+                    __half v = __float2half_rn(wf[li][i]);
+                    std::memcpy(&h[i], &v, 2);
+                }
+            }
+            d_w16[li] = dalloc<uint16_t>(cnt, "cudaMalloc(w16)");
+            ck(cudaMemcpy(d_w16[li], h.data(), cnt * 2, cudaMemcpyHostToDevice), "cudaMemcpy(w16)");
+        }
+        w16_prec = precision;
+    }
+
+    // ---- buffers ---------------------------------------------------------
+
+    void ensure_buffers() {
+        const int elem = elem_bytes();
+        if (alloc_batch == max_batch && alloc_elem >= elem) return;
+        DeviceGuard dg(device);
+        free_buffers();
+        const size_t rows = (size_t)max_batch * g.is;
+        d_stage = dalloc<uint8_t>(rows * kStagedChannels * elem, "cudaMalloc(stage)");
+        d_x = dalloc<uint8_t>(rows * cpad * elem, "cudaMalloc(act x)");
+        d_t = dalloc<uint8_t>(rows * cpad * elem, "cudaMalloc(act t)");
+        d_states = dalloc<float>((size_t)max_batch * planes * hw, "cudaMalloc(states)");
+        ck(cudaMemset(d_states, 0, (size_t)max_batch * planes * hw * sizeof(float)),
+           "cudaMemset(states)");
+        d_probs = dalloc<float>((size_t)max_batch * actions, "cudaMalloc(probs)");
+        d_logits = dalloc<float>((size_t)max_batch * actions, "cudaMalloc(logits)");
+        d_value = dalloc<float>((size_t)max_batch, "cudaMalloc(value)");
+        d_err = dalloc<int>(1, "cudaMalloc(err)");
+        ck(cudaMemset(d_err, 0, sizeof(int)), "cudaMemset(err)");
+        ck(cudaMallocHost(reinterpret_cast<void**>(&h_states),
+                          (size_t)max_batch * planes * hw * sizeof(float)),
+           "cudaMallocHost(states)");
+        ck(cudaMallocHost(reinterpret_cast<void**>(&h_err), sizeof(int)), "cudaMallocHost(err)");
+        alloc_batch = max_batch;
+        alloc_elem = elem;
+    }
+
+    int bucket_for(int n) const {
+        static const int kBuckets[] = {1,   2,   4,   8,   16,   32,   64,   96,   128,  192, 256,
+                                       320, 384, 448, 512, 640, 768, 896, 1024, 1536, 2048};
+        for (int b : kBuckets)
+            if (b >= n) return std::min(b, max_batch);
+        return max_batch;
+    }
+
+    int choose_bn(int m_total) const {
+        if (conv_bn_override > 0 && cpad % conv_bn_override == 0) return conv_bn_override;
+        int bn = std::min(cpad, 256);
+        while (cpad % bn != 0) bn -= 64;
+        const int mt = (m_total + 127) / 128;
+        while (bn > 64 && (long)mt * (cpad / bn) < 2L * num_sms && cpad % (bn / 2) == 0 &&
+               (bn / 2) % 64 == 0)
+            bn /= 2;
+        return bn;
+    }
+
+    // ---- kernels ---------------------------------------------------------
+
+    ConvLayer layer_desc(int li, int bucket) const {
+        ConvLayer L;
+        L.m_total = bucket * g.is;
+        L.cin = wcin[li];
+        L.cout = cpad;
+        L.g = g;
+        L.bias = d_bias[li];
+        L.err = d_err;
+        L.weight = precision == MG_PREC_FP32 ? (const void*)d_w32[li] : (const void*)d_w16[li];
+        if (li == 0) {
+            L.in = d_stage;
+            L.residual = nullptr;
+            L.out = d_x;
+        } else if (li % 2 == 1) {  // conv1 of a block: x -> t
+            L.in = d_x;
+            L.residual = nullptr;
+            L.out = d_t;
+        } else {  // conv2: t (+ x) -> x, in place over the residual rows
+            L.in = d_t;
+            L.residual = d_x;
+            L.out = d_x;
+        }
+        return L;
+    }
+
+    void launch_conv(int li, int bucket) {
+        ConvLayer L = layer_desc(li, bucket);
+        if (precision == MG_PREC_FP32) {
+            ck(launch_conv_simt(L, stream), "conv3x3_simt launch");
+            return;
+        }
+        const bool fp16 = precision == MG_PREC_FP16;
+        const int bn = choose_bn(L.m_total);
+        CUtensorMap ta, tb;
+        const char* why = "";
+        if (!make_conv_tensor_maps(L, bn, fp16, &ta, &tb, &why)) throw std::runtime_error(why);
+        ck(launch_conv_tc(L, ta, tb, bn, fp16, num_sms, stream), "conv3x3_tc launch");
+    }
+
+    void enqueue_trunk_heads(int bucket) {
+        for (int li = 0; li < n_convs; ++li) launch_conv(li, bucket);
+        ck(launch_heads(d_x, act_type(), hp, bucket, d_probs, d_logits, d_value, stream),
+           "heads launch");
+    }
+
+    void run_graph(int bucket) {
+        if (!use_graphs) {
+            enqueue_trunk_heads(bucket);
+            return;
+        }
+        auto key = std::make_pair(bucket, precision);
+        auto it = graphs.find(key);
+        if (it == graphs.end()) {
+            cudaGraph_t graph = nullptr;
+            ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal),
+               "cudaStreamBeginCapture");
+            try {
+                enqueue_trunk_heads(bucket);
+            } catch (...) {
+                cudaStreamEndCapture(stream, &graph);
+                if (graph) cudaGraphDestroy(graph);
+                throw;
+            }
+            ck(cudaStreamEndCapture(stream, &graph), "cudaStreamEndCapture");
+            cudaGraphExec_t exec = nullptr;
+            cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            ck(e, "cudaGraphInstantiate");
+            it = graphs.emplace(key, exec).first;
+        }
+        ck(cudaGraphLaunch(it->second, stream), "cudaGraphLaunch");
+    }
+
+    // Stage + trunk + heads for n <= max_batch positions at d_src (device).
+    void forward_core(const float* d_src, int n) {
+        const int bucket = bucket_for(n);
+        ck(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "cudaMemsetAsync(err)");
+        ck(launch_stage_input(d_src, n, bucket, planes, g, kStagedChannels,
+                              (flags & MG_FLAG_EIGEN_COMPAT) != 0, act_type(), d_stage, stream),
+           "stage launch");
+        run_graph(bucket);
+        last_bucket = bucket;
+    }
+
+    void check_ready() const {
+        if (!loaded) throw std::logic_error("no model loaded");
+    }
+};
+
+namespace {
+
+int fail(mg_engine* e, int code, const std::string& msg) {
+    if (e) e->err = msg;
+    return code;
+}
+
+// Runs `fn` with the engine's device current, mapping exceptions to codes.
+template <typename F>
+int guarded(mg_engine* e, F&& fn) {
+    if (e == nullptr) return MG_E_ARG;
+    DeviceGuard dg(e->device);
+    try {
+        fn();
+        e->err.clear();
+        return MG_OK;
+    } catch (const CudaFailure& f) {
+        return fail(e, MG_E_CUDA, f.where + ": " + cudaGetErrorString(f.code));
+    } catch (const std::invalid_argument& x) {
+        return fail(e, MG_E_ARG, x.what());
+    } catch (const std::logic_error& x) {
+        return fail(e, MG_E_STATE, x.what());
+    } catch (const std::runtime_error& x) {
+        return fail(e, MG_E_MODEL, x.what());
+    } catch (const std::exception& x) {
+        return fail(e, MG_E_MODEL, x.what());
+    }
+}
+
+bool is_pinned(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+}  // namespace
+
+extern "C" {
+
+mg_engine* mg_create(int device, int flags) {
+    g_create_error.clear();
+    int count = 0;
+    cudaError_t ce = cudaGetDeviceCount(&count);
+    if (ce != cudaSuccess || count == 0) {
+        g_create_error = std::string("no CUDA device: ") + cudaGetErrorString(ce);
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (device < 0 || device >= count) {
+        g_create_error = "device index out of range";
+        return nullptr;
+    }
+    std::unique_ptr<mg_engine> e(new mg_engine());
+    e->device = device;
+    e->flags = flags;
+    DeviceGuard dg(device);
+    cudaDeviceProp prop;
+    if ((ce = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) {
+        g_create_error = std::string("cudaGetDeviceProperties: ") + cudaGetErrorString(ce);
+        return nullptr;
+    }
+    if (prop.major != 10) {
+        g_create_error = "this backend needs an sm_100 (B200-class) GPU; device " +
+                         std::to_string(device) + " is sm_" + std::to_string(prop.major) +
+                         std::to_string(prop.minor);
+        return nullptr;
+    }
+    e->num_sms = prop.multiProcessorCount;
+    if ((ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (ce = configure_conv_tc()) != cudaSuccess) {
+        g_create_error = std::string("CUDA setup failed: ") + cudaGetErrorString(ce);
+        return nullptr;
+    }
+    if (const char* s = std::getenv("MG_CONV_BN")) e->conv_bn_override = std::atoi(s);
+    if (const char* s = std::getenv("MG_NO_GRAPHS")) e->use_graphs = std::atoi(s) == 0;
+    return e.release();
+}
+
+const char* mg_create_error(void) { return g_create_error.c_str(); }
+
+void mg_destroy(mg_engine* e) { delete e; }
+
+const char* mg_last_error(const mg_engine* e) { return e ? e->err.c_str() : "null engine"; }
+
+int mg_load_onnx(mg_engine* e, const char* path) {
+    if (path == nullptr) return fail(e, MG_E_ARG, "null path");
+    return guarded(e, [&] {
+        std::vector<NamedTensor> ts = read_onnx_initializers(path);
+        std::vector<std::vector<float>> vals(ts.size());
+        std::vector<TensorView> views(ts.size());
+        for (size_t i = 0; i < ts.size(); ++i) {
+            views[i].name = ts[i].name;
+            views[i].dims = ts[i].dims;
+            // Non-FLOAT tensors (e.g. num_batches_tracked) are kept without
+            // values; reading one as a weight fails its size check.
+            if (ts[i].data_type == 0 || ts[i].data_type == 1) vals[i] = ts[i].floats();
+            views[i].data = vals[i].data();
+            views[i].count = vals[i].size();
+        }
+        e->load(views);
+    });
+}
+
+int mg_load_weights(mg_engine* e, const mg_tensor* tensors, int count) {
+    if (count < 0 || (count > 0 && tensors == nullptr)) return fail(e, MG_E_ARG, "bad tensor list");
+    return guarded(e, [&] {
+        std::vector<TensorView> views(count);
+        for (int i = 0; i < count; ++i) {
+            const mg_tensor& t = tensors[i];
+            if (t.name == nullptr || t.ndims < 0 || (t.ndims > 0 && t.dims == nullptr))
+                throw std::invalid_argument("tensor " + std::to_string(i) + " is malformed");
+            views[i].name = t.name;
+            views[i].dims.assign(t.dims, t.dims + t.ndims);
+            size_t cnt = t.ndims > 0 ? 1 : 0;
+            for (int d = 0; d < t.ndims; ++d) cnt *= (size_t)std::max<int64_t>(t.dims[d], 0);
+            views[i].data = t.data;
+            views[i].count = t.data ? cnt : 0;
+        }
+        e->load(views);
+    });
+}
+
+int mg_get_info(const mg_engine* e, int* board_size, int* input_channels, int* num_filters,
+                int* num_res_blocks, int* action_size) {
+    if (e == nullptr) return MG_E_ARG;
+    if (!e->loaded) return MG_E_STATE;
+    if (board_size) *board_size = e->net.board;
+    if (input_channels) *input_channels = e->net.input_channels;
+    if (num_filters) *num_filters = e->net.filters;
+    if (num_res_blocks) *num_res_blocks = e->net.blocks;
+    if (action_size) *action_size = e->net.actions;
+    return MG_OK;
+}
+
+int mg_set_precision(mg_engine* e, int precision) {
+    if (e == nullptr) return MG_E_ARG;
+    if (precision != MG_PREC_BF16 && precision != MG_PREC_FP16 && precision != MG_PREC_FP32)
+        return fail(e, MG_E_ARG, "unknown precision");
+    return guarded(e, [&] {
+        e->precision = precision;
+        if (e->loaded) e->prepare_weights();
+    });
+}
+
+int mg_set_max_batch(mg_engine* e, int max_batch) {
+    if (e == nullptr) return MG_E_ARG;
+    if (max_batch < 1 || max_batch > 65536) return fail(e, MG_E_ARG, "max batch out of range");
+    return guarded(e, [&] {
+        e->max_batch = max_batch;
+        e->free_buffers();
+    });
+}
+
+int mg_forward(mg_engine* e, const float* states, int n, float* policy_out, float* value_out,
+               float* logits_out) {
+    if (e == nullptr) return MG_E_ARG;
+    if (n < 0) return fail(e, MG_E_ARG, "negative batch size");
+    if (n == 0) return MG_OK;
+    if (states == nullptr || policy_out == nullptr || value_out == nullptr)
+        return fail(e, MG_E_ARG, "null buffer");
+    int dev_err = 0;
+    int rc = guarded(e, [&] {
+        e->check_ready();
+        e->prepare_weights();
+        e->ensure_buffers();
+        const size_t in_per = (size_t)e->planes * e->hw;
+        const int A = e->actions;
+        const bool pinned = is_pinned(states);
+        for (int base = 0; base < n; base += e->max_batch) {
+            const int m = std::min(e->max_batch, n - base);
+            const float* src = states + (size_t)base * in_per;
+            if (pinned) {
+                ck(cudaMemcpyAsync(e->d_states, src, (size_t)m * in_per * sizeof(float),
+                                   cudaMemcpyHostToDevice, e->stream),
+                   "cudaMemcpyAsync(H2D states)");
+            } else {
+                // The pinned staging buffer may still feed the previous chunk's copy.
+                ck(cudaStreamSynchronize(e->stream), "cudaStreamSynchronize");
+                std::memcpy(e->h_states, src, (size_t)m * in_per * sizeof(float));
+                ck(cudaMemcpyAsync(e->d_states, e->h_states, (size_t)m * in_per * sizeof(float),
+                                   cudaMemcpyHostToDevice, e->stream),
+                   "cudaMemcpyAsync(H2D states)");
+            }
+            e->forward_core(e->d_states, m);
+            ck(cudaMemcpyAsync(policy_out + (size_t)base * A, e->d_probs, (size_t)m * A * sizeof(float),
+                               cudaMemcpyDeviceToHost, e->stream),
+               "cudaMemcpyAsync(D2H policy)");
+            ck(cudaMemcpyAsync(value_out + base, e->d_value, (size_t)m * sizeof(float),
+                               cudaMemcpyDeviceToHost, e->stream),
+               "cudaMemcpyAsync(D2H value)");
+            if (logits_out)
+                ck(cudaMemcpyAsync(logits_out + (size_t)base * A, e->d_logits,
+                                   (size_t)m * A * sizeof(float), cudaMemcpyDeviceToHost, e->stream),
+                   "cudaMemcpyAsync(D2H logits)");
+            ck(cudaMemcpyAsync(e->h_err, e->d_err, sizeof(int), cudaMemcpyDeviceToHost, e->stream),
+               "cudaMemcpyAsync(D2H status)");
+            if (base + m < n) {
+                // Later chunks reuse the device buffers: keep results ordered.
+                ck(cudaStreamSynchronize(e->stream), "cudaStreamSynchronize");
+                dev_err |= *e->h_err;
+            }
+        }
+        ck(cudaStreamSynchronize(e->stream), "cudaStreamSynchronize");
+        dev_err |= *e->h_err;
+    });
+    if (rc == MG_OK && dev_err != 0)
+        return fail(e, MG_E_DEVICE, "a kernel gave up waiting (device status " +
+                                        std::to_string(dev_err) + ")");
+    return rc;
+}
+
+int mg_forward_device(mg_engine* e, const float* d_states, int n, float* d_policy, float* d_value,
+                      float* d_logits) {
+    if (e == nullptr) return MG_E_ARG;
+    if (n < 0) return fail(e, MG_E_ARG, "negative batch size");
+    if (n == 0) return MG_OK;
+    if (d_states == nullptr || d_policy == nullptr || d_value == nullptr)
+        return fail(e, MG_E_ARG, "null buffer");
+    if (n > e->max_batch) return fail(e, MG_E_ARG, "batch exceeds the max batch");
+    return guarded(e, [&] {
+        e->check_ready();
+        e->prepare_weights();
+        e->ensure_buffers();
+        const int A = e->actions;
+        e->forward_core(d_states, n);
+        ck(cudaMemcpyAsync(d_policy, e->d_probs, (size_t)n * A * sizeof(float),
+                           cudaMemcpyDeviceToDevice, e->stream),
+           "cudaMemcpyAsync(policy)");
+        ck(cudaMemcpyAsync(d_value, e->d_value, (size_t)n * sizeof(float), cudaMemcpyDeviceToDevice,
+                           e->stream),
+           "cudaMemcpyAsync(value)");
+        if (d_logits)
+            ck(cudaMemcpyAsync(d_logits, e->d_logits, (size_t)n * A * sizeof(float),
+                               cudaMemcpyDeviceToDevice, e->stream),
+               "cudaMemcpyAsync(logits)");
+    });
+}
+
+int mg_synchronize(mg_engine* e) {
+    if (e == nullptr) return MG_E_ARG;
+    int dev_err = 0;
+    int rc = guarded(e, [&] {
+        ck(cudaStreamSynchronize(e->stream), "cudaStreamSynchronize");
+        if (e->d_err) {
+            ck(cudaMemcpy(&dev_err, e->d_err, sizeof(int), cudaMemcpyDeviceToHost),
+               "cudaMemcpy(status)");
+        }
+    });
+    if (rc == MG_OK && dev_err != 0)
+        return fail(e, MG_E_DEVICE, "a kernel gave up waiting (device status " +
+                                        std::to_string(dev_err) + ")");
+    return rc;
+}
+
+void* mg_stream(mg_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+int mg_launch_conv(mg_engine* e, int n, int layer, int reps) {
+    if (e == nullptr) return MG_E_ARG;
+    return guarded(e, [&] {
+        e->check_ready();
+        if (e->last_bucket == 0 || e->alloc_batch == 0)
+            throw std::logic_error("run a forward pass before mg_launch_conv");
+        if (layer < 0 || layer >= 2 * e->net.blocks || reps < 0 || n < 1 || n > e->max_batch)
+            throw std::invalid_argument("bad layer, n or reps");
+        const int bucket = e->bucket_for(n);
+        for (int r = 0; r < reps; ++r) e->launch_conv(1 + layer, bucket);
+    });
+}
+
+int mg_launches_per_forward(mg_engine* e, int n) {
+    if (e == nullptr || !e->loaded) return 0;
+    (void)n;
+    return 1 /* stage */ + e->n_convs + 1 /* heads */;
+}
+
+}  // extern "C"

@@ -1,0 +1,102 @@
+// Launch interfaces of the device kernels of the network-evaluation path.
+//
+// Activation layout ("framed NHWC"): a batch of positions on a board of side
+// B is stored as rows of channel vectors, one row per pixel of a
+// (B+1) x (B+1) frame per position: row = n*IS + y*RS + x with RS = B + 1,
+// IS = RS * RS.  Column x = B and row y = B of every frame are zero, so the
+// 3x3 neighbour (y+dy, x+dx) of any board pixel is the row
+// row + dy*RS + dx and reads zero whenever it falls off the board (the
+// zero padding of src/eigen_engine.cpp:139-168); the rows before the first
+// frame read as zero through TMA out-of-bounds fill.  Every kernel that
+// writes activations writes zeros on frame pixels.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace mgb {
+
+struct FrameGeom {
+    int board;  // B
+    int rs;     // B + 1
+    int is;     // (B + 1)^2
+};
+
+inline FrameGeom make_frame(int board) {
+    FrameGeom g;
+    g.board = board;
+    g.rs = board + 1;
+    g.is = (board + 1) * (board + 1);
+    return g;
+}
+
+// One 3x3 convolution layer, stride 1, zero padding 1, with folded
+// BatchNorm bias, optional residual add and ReLU:
+//   out[r, co] = relu(sum_{tap, ci} in[r + off(tap), ci] * W[co, tap, ci]
+//                     + bias[co] (+ residual[r, co]))      on board pixels,
+//   out[r, co] = 0                                          on frame pixels.
+struct ConvLayer {
+    int m_total;            // rows = positions * IS
+    int cin;                // input channels (multiple of 64)
+    int cout;               // output channels (multiple of 64)
+    FrameGeom g;
+    const void* in;         // [m_total][cin]
+    const void* weight;     // [cout][9][cin]
+    const float* bias;      // [cout]
+    const void* residual;   // [m_total][cout] or nullptr (may equal out)
+    void* out;              // [m_total][cout]
+    int* err;               // device status word
+};
+
+// Tensor-core path (bf16 or fp16 operands, fp32 accumulation in TMEM).
+// tmA / tmB must describe layer.in / layer.weight (see make_conv_tensor_maps).
+// bn = output channels per tile (64, 128 or 256; must divide cout).
+cudaError_t launch_conv_tc(const ConvLayer& layer, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                           int bn, bool fp16, int grid_limit, cudaStream_t stream);
+
+// Host-side encoding of the two TMA descriptors of a layer.
+bool make_conv_tensor_maps(const ConvLayer& layer, int bn, bool fp16, CUtensorMap* tmA,
+                           CUtensorMap* tmB, const char** why);
+
+// Shared-memory bytes the tensor-core kernel needs for a tile width bn.
+int conv_tc_smem_bytes(int bn);
+
+// Sets the shared-memory opt-in of every tensor-core kernel instantiation on
+// the current device (a per-device attribute; call once per device before
+// launching or capturing).
+cudaError_t configure_conv_tc();
+
+// fp32 SIMT path used by the fp32 verification mode.
+cudaError_t launch_conv_simt(const ConvLayer& layer, cudaStream_t stream);
+
+// Input staging: n_valid positions of plane-major fp32 states (17 planes of
+// B*B, src/game.cpp:229-256) -> framed NHWC rows of `cpad` channels of type
+// T for `n_pos` positions (positions >= n_valid are zero).  With
+// eigen_order, state element (c, p) is read from c + p*planes instead of
+// c*B*B + p, the column-major reading of src/eigen_engine.cpp:211.
+enum class ActType { BF16 = 0, FP16 = 1, FP32 = 2 };
+cudaError_t launch_stage_input(const float* states, int n_valid, int n_pos, int planes,
+                               const FrameGeom& g, int cpad, bool eigen_order, ActType t,
+                               void* out, cudaStream_t stream);
+
+// Policy / value heads over the trunk output (framed NHWC, `c` channels).
+struct HeadParams {
+    int board, hw, c, actions, hidden;
+    FrameGeom g;
+    const float* pconv_w;  // [2][c]  (BatchNorm folded)
+    const float* pconv_b;  // [2]
+    const float* vconv_w;  // [c]
+    const float* vconv_b;  // [1]
+    const float* pfc_w;    // [actions][2*hw], column c*hw + p
+    const float* pfc_b;    // [actions]
+    const float* v1_w;     // [hidden][hw]
+    const float* v1_b;     // [hidden]
+    const float* v2_w;     // [hidden]
+    const float* v2_b;     // [1]
+};
+cudaError_t launch_heads(const void* trunk, ActType t, const HeadParams& h, int n_pos,
+                         float* probs, float* logits, float* value, cudaStream_t stream);
+size_t heads_smem_bytes(const HeadParams& h);
+
+}  // namespace mgb

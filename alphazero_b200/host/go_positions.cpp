@@ -1,0 +1,203 @@
+#include "go_positions.h"
+
+#include <cstring>
+#include <random>
+
+namespace mgb {
+
+GoPosition::GoPosition(int board_size, float komi) : n_(board_size), komi_(komi) {
+    reset();
+}
+
+void GoPosition::reset() {
+    std::memset(cells_, 0, sizeof(cells_));
+    std::memset(prev_, 0, sizeof(prev_));
+    std::memset(hist_, 0, sizeof(hist_));
+    has_prev_ = false;
+    to_move_ = 1;
+    passes_ = 0;
+    over_ = false;
+    winner_ = 0;
+    moves_ = 0;
+    hist_len_ = 0;
+    hist_top_ = kHistory - 1;
+    push_history();
+}
+
+int GoPosition::neighbours(int p, int* out) const {
+    int r = p / n_, c = p % n_, k = 0;
+    if (r > 0) out[k++] = p - n_;
+    if (r < n_ - 1) out[k++] = p + n_;
+    if (c > 0) out[k++] = p - 1;
+    if (c < n_ - 1) out[k++] = p + 1;
+    return k;
+}
+
+int GoPosition::chain_liberties(const int8_t* b, int p, int* chain, int* len) const {
+    const int8_t colour = b[p];
+    uint8_t seen[kMaxBoard * kMaxBoard];
+    std::memset(seen, 0, sizeof(seen));
+    // bit 0: in chain, bit 1: counted as a liberty
+    int head = 0, tail = 0, libs = 0;
+    chain[tail++] = p;
+    seen[p] = 1;
+    while (head < tail) {
+        int q = chain[head++];
+        int nb[4];
+        int k = neighbours(q, nb);
+        for (int i = 0; i < k; ++i) {
+            int t = nb[i];
+            if (b[t] == 0) {
+                if (!(seen[t] & 2)) { seen[t] |= 2; ++libs; }
+            } else if (b[t] == colour && !(seen[t] & 1)) {
+                seen[t] |= 1;
+                chain[tail++] = t;
+            }
+        }
+    }
+    *len = tail;
+    return libs;
+}
+
+bool GoPosition::legal(int action) const {
+    if (over_) return false;
+    const int nn = n_ * n_;
+    if (action == nn) return true;
+    if (action < 0 || action > nn) return false;
+    if (cells_[action] != 0) return false;
+    int nb[4];
+    int k = neighbours(action, nb);
+    for (int i = 0; i < k; ++i)
+        if (cells_[nb[i]] == 0) return true;
+
+    // Every neighbour is occupied: resolve captures on a scratch board.
+    int8_t trial[kMaxBoard * kMaxBoard];
+    std::memcpy(trial, cells_, sizeof(trial));
+    trial[action] = (int8_t)to_move_;
+    const int8_t them = (int8_t)(3 - to_move_);
+    int chain[kMaxBoard * kMaxBoard];
+    int len = 0;
+    for (int i = 0; i < k; ++i) {
+        if (trial[nb[i]] != them) continue;
+        if (chain_liberties(trial, nb[i], chain, &len) == 0)
+            for (int j = 0; j < len; ++j) trial[chain[j]] = 0;
+    }
+    if (chain_liberties(trial, action, chain, &len) == 0) return false;  // suicide
+    if (has_prev_) {
+        bool same = true;
+        for (int q = 0; q < nn && same; ++q) same = (trial[q] == prev_[q]);
+        if (same) return false;  // recreates the previous board
+    }
+    return true;
+}
+
+void GoPosition::play(int action) {
+    const int nn = n_ * n_;
+    std::memcpy(prev_, cells_, sizeof(cells_));
+    has_prev_ = true;
+    if (action == nn || action < 0) {
+        if (++passes_ >= 2) {
+            over_ = true;
+            decide_winner();
+        }
+    } else {
+        passes_ = 0;
+        cells_[action] = (int8_t)to_move_;
+        const int8_t them = (int8_t)(3 - to_move_);
+        int nb[4];
+        int k = neighbours(action, nb);
+        int chain[kMaxBoard * kMaxBoard];
+        int len = 0;
+        for (int i = 0; i < k; ++i) {
+            if (cells_[nb[i]] != them) continue;
+            if (chain_liberties(cells_, nb[i], chain, &len) == 0)
+                for (int j = 0; j < len; ++j) cells_[chain[j]] = 0;
+        }
+    }
+    ++moves_;
+    to_move_ = 3 - to_move_;
+    push_history();
+}
+
+void GoPosition::push_history() {
+    hist_top_ = (hist_top_ + 1) % kHistory;
+    std::memcpy(hist_[hist_top_], cells_, sizeof(cells_));
+    if (hist_len_ < kHistory) ++hist_len_;
+}
+
+void GoPosition::encode(float* out) const {
+    const int nn = n_ * n_;
+    std::memset(out, 0, sizeof(float) * (size_t)kInputPlanes * nn);
+    const int8_t us = (int8_t)to_move_, them = (int8_t)(3 - to_move_);
+    for (int i = 0; i < hist_len_; ++i) {
+        const int8_t* snap = hist_[(hist_top_ - i + kHistory) % kHistory];
+        float* mine = out + (size_t)i * nn;
+        float* theirs = out + (size_t)(kHistory + i) * nn;
+        for (int q = 0; q < nn; ++q) {
+            if (snap[q] == us) mine[q] = 1.0f;
+            else if (snap[q] == them) theirs[q] = 1.0f;
+        }
+    }
+    if (to_move_ == 1) {
+        float* colour = out + (size_t)2 * kHistory * nn;
+        for (int q = 0; q < nn; ++q) colour[q] = 1.0f;
+    }
+}
+
+void GoPosition::decide_winner() {
+    const int nn = n_ * n_;
+    float area[3] = {0.f, 0.f, 0.f};
+    for (int q = 0; q < nn; ++q) area[cells_[q]] += 1.0f;
+    uint8_t seen[kMaxBoard * kMaxBoard];
+    std::memset(seen, 0, sizeof(seen));
+    int region[kMaxBoard * kMaxBoard];
+    for (int s = 0; s < nn; ++s) {
+        if (cells_[s] != 0 || seen[s]) continue;
+        int head = 0, tail = 0;
+        bool touch[3] = {false, false, false};
+        region[tail++] = s;
+        seen[s] = 1;
+        while (head < tail) {
+            int q = region[head++];
+            int nb[4];
+            int k = neighbours(q, nb);
+            for (int i = 0; i < k; ++i) {
+                int t = nb[i];
+                if (cells_[t] == 0) {
+                    if (!seen[t]) { seen[t] = 1; region[tail++] = t; }
+                } else {
+                    touch[cells_[t]] = true;
+                }
+            }
+        }
+        if (touch[1] && !touch[2]) area[1] += (float)tail;
+        else if (touch[2] && !touch[1]) area[2] += (float)tail;
+    }
+    const float black = area[1], white = area[2] + komi_;
+    winner_ = black > white ? 1 : (white > black ? 2 : 0);
+}
+
+uint32_t draw_below(uint32_t r, uint32_t range) {
+    return (uint32_t)(((uint64_t)r * (uint64_t)range) >> 32);
+}
+
+void random_positions(int board, int n, uint32_t seed, int max_moves, float* out) {
+    std::mt19937 rng(seed);
+    const int nn = board * board;
+    std::vector<int> legal_list;
+    legal_list.reserve(nn + 1);
+    for (int i = 0; i < n; ++i) {
+        GoPosition g(board);
+        const int k = (int)draw_below(rng(), (uint32_t)max_moves + 1u);
+        for (int m = 0; m < k && !g.over(); ++m) {
+            legal_list.clear();
+            for (int a = 0; a < nn; ++a)
+                if (g.legal(a)) legal_list.push_back(a);
+            legal_list.push_back(nn);
+            g.play(legal_list[draw_below(rng(), (uint32_t)legal_list.size())]);
+        }
+        g.encode(out + (size_t)i * kInputPlanes * nn);
+    }
+}
+
+}  // namespace mgb

@@ -1,0 +1,82 @@
+// Go rules, input-plane encoder and seeded random-playout position generator.
+//
+// This is the synthetic-input producer for the network-evaluation path: it
+// yields the same 17 binary planes the reference encoder writes
+// (src/game.cpp:229-256, GoGame::encode) for positions reached by uniformly
+// random legal moves from the empty board.  The rules follow the reference's
+// GoGame exactly where they decide which moves are legal:
+//   - pass is always legal unless the game is over (src/game.cpp:164-168);
+//   - a point with an empty neighbour is always legal (src/game.cpp:189-194);
+//   - otherwise captures are resolved, suicide is illegal and a move that
+//     recreates the previous board is illegal (simple ko,
+//     src/game.cpp:199-233);
+//   - two consecutive passes end the game and area scoring decides the winner
+//     (src/game.cpp:247-256, :258-315).
+// History planes use the last 8 boards, most recent first, coloured relative
+// to the player to move; plane 16 is all ones when black is to move.
+#pragma once
+
+#include <cstdint>
+#include <vector>
+
+namespace mgb {
+
+constexpr int kMaxBoard = 19;
+constexpr int kHistory = 8;
+constexpr int kInputPlanes = 2 * kHistory + 1;  // 17
+
+class GoPosition {
+public:
+    explicit GoPosition(int board_size = 19, float komi = 7.5f);
+
+    void reset();
+    bool legal(int action) const;  // action in [0, n*n]; n*n = pass
+    void play(int action);         // caller guarantees legal(action)
+    void encode(float* out) const; // kInputPlanes * n * n floats, plane-major
+
+    int size() const { return n_; }
+    bool over() const { return over_; }
+    int to_move() const { return to_move_; }  // 1 black, 2 white
+    int winner() const { return winner_; }    // 0 draw/none, 1, 2
+    int moves() const { return moves_; }
+    const int8_t* board() const { return cells_; }
+
+private:
+    int n_;
+    float komi_;
+    int8_t cells_[kMaxBoard * kMaxBoard];
+    int8_t prev_[kMaxBoard * kMaxBoard];
+    bool has_prev_;
+    int to_move_;
+    int passes_;
+    bool over_;
+    int winner_;
+    int moves_;
+    // Circular store of the last kHistory boards; hist_len_ valid entries
+    // ending at hist_top_ (the current board).
+    int8_t hist_[kHistory][kMaxBoard * kMaxBoard];
+    int hist_len_;
+    int hist_top_;
+
+    int neighbours(int p, int* out) const;
+    // Flood-fills the chain through p on `b`; returns its liberty count and
+    // writes its points to `chain` (length in *len).
+    int chain_liberties(const int8_t* b, int p, int* chain, int* len) const;
+    void push_history();
+    void decide_winner();
+};
+
+// Uniform draw in [0, range) from a 32-bit Mersenne Twister word by the
+// multiply-shift map floor(r * range / 2^32): fully specified, so a harness
+// around any other Go implementation can reproduce the same choices.
+uint32_t draw_below(uint32_t r, uint32_t range);
+
+// Writes n positions (kInputPlanes * board^2 floats each) to out.  Position i
+// plays k_i = draw_below(rng(), max_moves + 1) random legal moves (pass
+// included, stopping early if the game ends), drawing each move as
+// legal_list[draw_below(rng(), legal_count)] where legal_list is the legal
+// points in increasing index order followed by pass; rng is one
+// std::mt19937 seeded with `seed` shared by all n positions.
+void random_positions(int board, int n, uint32_t seed, int max_moves, float* out);
+
+}  // namespace mgb

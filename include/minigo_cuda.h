@@ -1,0 +1,130 @@
+/*
+ * minigo_cuda.h - C ABI of the B200 network-evaluation backend.
+ *
+ * One handle = one network resident on one GPU, evaluated on that GPU's own
+ * stream.  Calls on one handle must be serialised by the caller, exactly as
+ * the reference's engines require (include/opencl_engine.h:24: one
+ * NNEvaluator server thread drives one engine).  Every call returns 0 on
+ * success or a negative MG_E* code; mg_last_error() then holds a message.
+ * Nothing throws across this boundary.
+ *
+ * Semantics follow the reference interface include/inference_engine.h:
+ * input states are 17 planes x board^2 fp32 values per position, plane-major
+ * (src/game.cpp:229-256); outputs are softmax probabilities over
+ * board^2 + 1 actions and a tanh value in [-1, 1] per position.
+ */
+#ifndef MINIGO_CUDA_H
+#define MINIGO_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mg_engine mg_engine;
+
+/* Error codes. */
+#define MG_OK 0
+#define MG_E_ARG (-1)      /* bad argument (null pointer, size out of range)  */
+#define MG_E_MODEL (-2)    /* model file or tensor set rejected                */
+#define MG_E_CUDA (-3)     /* CUDA runtime or driver call failed               */
+#define MG_E_STATE (-4)    /* call not valid in this state (no model loaded)   */
+#define MG_E_DEVICE (-5)   /* a kernel reported an error (bounded wait expired) */
+
+/* Arithmetic of the trunk (mg_set_precision). */
+#define MG_PREC_BF16 0     /* bf16 operands, fp32 accumulate (tcgen05)        */
+#define MG_PREC_FP16 1     /* fp16 operands, fp32 accumulate (tcgen05)        */
+#define MG_PREC_FP32 2     /* fp32 SIMT verification path                     */
+
+/* mg_create flags. */
+#define MG_FLAG_EIGEN_COMPAT 1 /* read inputs and flatten the policy features
+                                  the way src/eigen_engine.cpp:211,242 do
+                                  (column-major Map), instead of the NCHW
+                                  semantics of scripts/model.py:48-62        */
+
+/* A named fp32 host tensor, as produced by any ONNX initializer parser
+ * (replaces onnx_parser::OnnxTensor, include/onnx_loader.h:13-30). */
+typedef struct mg_tensor {
+    const char* name;
+    const int64_t* dims;
+    int ndims;
+    const float* data; /* product(dims) little-endian fp32 values */
+} mg_tensor;
+
+/* Creates an engine on CUDA device `device`.  Replaces the backend
+ * constructor called by create_engine() (src/inference_engine.cpp:16-24);
+ * the device index is new (one engine per GPU).  Returns NULL on failure;
+ * mg_create_error() then describes why. */
+mg_engine* mg_create(int device, int flags);
+const char* mg_create_error(void);
+
+/* Releases every device and pinned host allocation of the engine. */
+void mg_destroy(mg_engine* e);
+
+/* Message describing the last failed call on this handle ("" if none). */
+const char* mg_last_error(const mg_engine* e);
+
+/* Loads weights from an ONNX file (initializers only).  Replaces
+ * InferenceEngine::load_model (include/inference_engine.h:19) as implemented
+ * by EigenEngine::load_from_onnx (src/eigen_engine.cpp:17-121): the
+ * architecture is inferred from tensor names and shapes and BatchNorm is
+ * folded with eps = 1e-5.  Errors name the file or the missing tensor. */
+int mg_load_onnx(mg_engine* e, const char* path);
+
+/* Same as mg_load_onnx for tensors already parsed by the caller (for example
+ * by the reference's onnx_parser::parse_onnx_file, src/onnx_loader.cpp:183). */
+int mg_load_weights(mg_engine* e, const mg_tensor* tensors, int count);
+
+/* Model metadata, set by a successful load (include/inference_engine.h:36-40).
+ * Any output pointer may be NULL. */
+int mg_get_info(const mg_engine* e, int* board_size, int* input_channels,
+                int* num_filters, int* num_res_blocks, int* action_size);
+
+/* Selects MG_PREC_*.  Default MG_PREC_BF16. */
+int mg_set_precision(mg_engine* e, int precision);
+
+/* Largest positions per device launch (default 1024).  Larger batches are
+ * evaluated in chunks.  Must be called before the first forward. */
+int mg_set_max_batch(mg_engine* e, int max_batch);
+
+/* Evaluates n positions held in HOST memory.  Replaces predict_batch
+ * (include/inference_engine.h:25-32; src/opencl_engine.cpp:722-857) and, for
+ * n = 1, predict (include/inference_engine.h:21-23).
+ *   states      n x input_channels x board^2 fp32, position-major
+ *   policy_out  n x action_size softmax probabilities
+ *   value_out   n tanh values
+ *   logits_out  n x action_size pre-softmax logits, or NULL
+ * n == 0 is valid and does nothing (src/opencl_engine.cpp:724).
+ * Blocks until the results are in the output buffers.  Pinned (page-locked)
+ * host buffers are copied by DMA directly; pageable ones are staged. */
+int mg_forward(mg_engine* e, const float* states, int n, float* policy_out,
+               float* value_out, float* logits_out);
+
+/* As mg_forward, with every pointer in this engine's device memory.
+ * Enqueues on the engine's stream and returns without waiting; pair with
+ * mg_synchronize.  n must not exceed the max batch. */
+int mg_forward_device(mg_engine* e, const float* d_states, int n, float* d_policy,
+                      float* d_value, float* d_logits);
+
+/* Waits for all work on the engine's stream and reports device-side errors. */
+int mg_synchronize(mg_engine* e);
+
+/* The engine's cudaStream_t, for callers that time its work with events. */
+void* mg_stream(mg_engine* e);
+
+/* Launches `reps` back-to-back passes of one residual-block 3x3 convolution
+ * layer (layer index 0 .. 2*blocks-1) over the activations left by the last
+ * mg_forward_device of n positions.  A measurement hook: it lets a caller
+ * time the trunk's convolution kernel alone with events on mg_stream(). */
+int mg_launch_conv(mg_engine* e, int n, int layer, int reps);
+
+/* Number of kernel launches one mg_forward_device of n positions makes. */
+int mg_launches_per_forward(mg_engine* e, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINIGO_CUDA_H */

@@ -1,0 +1,164 @@
+"""GPU parity: the CUDA engine (through the C ABI) against the golden
+fixtures of the reference network and against the oracle.
+
+Tolerances (max |difference| of pre-softmax logits and of values):
+  fp32 verification mode   1e-4
+  bf16 / fp16 modes        2e-2
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from alphazero_b200 import host_lib, weights
+from conftest import golden_cases, load_golden
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp32": 1e-4, "bf16": 2e-2, "fp16": 2e-2}
+
+
+def softmax(l):
+    e = np.exp(l - l.max(1, keepdims=True))
+    return e / e.sum(1, keepdims=True)
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16", "fp16"])
+@pytest.mark.parametrize("case", golden_cases())
+def test_engine_matches_reference_golden(gpu_engine_factory, case, precision):
+    z, sd = load_golden(case)
+    e = gpu_engine_factory(sd, precision)
+    x = z["positions"].astype(np.float32)
+    p, v, l = e.forward(x)
+    tol = TOL[precision]
+    assert np.isfinite(l).all() and np.isfinite(v).all()
+    assert np.abs(l - z["logits"]).max() < tol
+    assert np.abs(v - z["value"]).max() < tol
+    assert np.abs(p - softmax(z["logits"])).max() < tol
+    assert np.abs(p.sum(1) - 1).max() < 1e-5
+    # the engine's probabilities are the softmax of its own logits
+    assert np.abs(p - softmax(l.astype(np.float64))).max() < 1e-5
+
+
+@pytest.mark.parametrize("precision", ["fp32", "bf16"])
+@pytest.mark.parametrize("case", ["b9c64x6_pert", "b19c128x10_pert", "b5c32x3_pert"])
+def test_eigen_compat_matches_literal_semantics(gpu_engine_factory, case, precision):
+    z, sd = load_golden(case)
+    e = gpu_engine_factory(sd, precision, eigen_compat=True)
+    p, v, l = e.forward(z["positions"].astype(np.float32))
+    assert np.abs(l - z["logits_literal"]).max() < TOL[precision]
+    assert np.abs(v - z["value_literal"]).max() < TOL[precision]
+
+
+def _oracle_rows(sd, x, rows):
+    orc = oracle.EigenOracle(sd)
+    return orc.predict_batch(x[rows], oracle.CANONICAL, threads=min(32, os.cpu_count() or 1))
+
+
+@pytest.mark.parametrize("board,filters,blocks,n,max_moves", [
+    (9, 128, 10, 256, 60),     # 9x9 b10c128, batch 256
+    (19, 128, 10, 512, 250),   # 19x19 b10c128, batch 512
+    (19, 256, 20, 1024, 250),  # 19x19 b20c256, batch 1024
+])
+def test_full_size_batches(gpu_engine_factory, board, filters, blocks, n, max_moves):
+    sd = weights.make_state_dict(board, filters, blocks, seed=11, variant="perturbed")
+    e = gpu_engine_factory(sd, "bf16")
+    x = host_lib.random_positions(board, n, 2024, max_moves)
+    p, v, l = e.forward(x)
+    # size-independent properties over the whole batch
+    assert np.isfinite(l).all() and np.isfinite(v).all()
+    assert np.abs(p.sum(1) - 1).max() < 1e-5
+    assert (np.abs(v) <= 1).all()
+    # a sample of rows against the oracle
+    rows = np.random.default_rng(0).choice(n, 12, replace=False)
+    rows[:2] = [0, n - 1]
+    _, ov, ol = _oracle_rows(sd, x, rows)
+    assert np.abs(l[rows] - ol).max() < TOL["bf16"]
+    assert np.abs(v[rows] - ov).max() < TOL["bf16"]
+    # positions are independent: permuting the batch permutes the results
+    perm = np.random.default_rng(1).permutation(n)
+    p2, v2, l2 = e.forward(x[perm])
+    assert np.array_equal(l2, l[perm]) and np.array_equal(v2, v[perm])
+
+
+def test_ragged_and_chunked_batches(gpu_engine_factory):
+    z, sd = load_golden("b19c128x10_pert")
+    e = gpu_engine_factory(sd, "bf16", max_batch=64)
+    x = host_lib.random_positions(19, 150, 77, 250)
+    _, v_all, l_all = e.forward(x)  # 150 > max batch 64: three chunks
+    for n in (1, 3, 17, 64, 65, 129):
+        _, v, l = e.forward(x[:n])
+        assert np.array_equal(l, l_all[:n]) and np.array_equal(v, v_all[:n]), n
+    rows = np.array([0, 63, 64, 127, 128, 149])
+    _, ov, ol = _oracle_rows(sd, x, rows)
+    assert np.abs(l_all[rows] - ol).max() < TOL["bf16"]
+
+
+def test_duplicate_positions_identical(gpu_engine_factory):
+    _, sd = load_golden("b9c64x6_pert")
+    e = gpu_engine_factory(sd, "bf16")
+    x = np.repeat(host_lib.random_positions(9, 1, 5, 60), 37, axis=0)
+    _, v, l = e.forward(x)
+    assert (l == l[0]).all() and (v == v[0]).all()
+
+
+def test_interface_semantics(gpu_engine_factory, tmp_path):
+    z, sd = load_golden("b9c64x6_init")
+    path = weights.write_onnx(str(tmp_path / "m.onnx"), sd)
+    from alphazero_b200.engine import CudaEngine
+
+    e = CudaEngine(0, precision="fp32")
+    try:
+        with pytest.raises(RuntimeError, match="no model loaded"):
+            e.predict(np.zeros(17 * 81, np.float32))
+        e.load_model(path)
+        assert (e.board_size, e.input_channels, e.num_filters, e.num_res_blocks) == (9, 17, 64, 6)
+        assert e.backend_name() == "cuda"
+        assert e.predict_batch([]) == []
+        x = z["positions"].astype(np.float32)
+        batch = e.predict_batch(list(x))
+        for i in range(len(x)):
+            pol, val = e.predict(x[i])
+            assert np.allclose(pol, batch[i][0], atol=1e-6) and abs(val - batch[i][1]) < 1e-6
+            assert abs(val - z["value"][i]) < 1e-4
+        with pytest.raises(RuntimeError, match="Cannot open model file"):
+            e.load_model(str(tmp_path / "missing.onnx"))
+        bad = dict(sd)
+        del bad["res_blocks.0.bn2.running_var"]
+        with pytest.raises(RuntimeError, match="Missing tensor: res_blocks.0.bn2.running_var"):
+            e.load_state_dict(bad)
+    finally:
+        e.close()
+
+
+def test_pinned_pageable_and_device_inputs_agree(gpu_engine_factory):
+    import torch
+
+    z, sd = load_golden("b19c128x10_pert")
+    e = gpu_engine_factory(sd, "bf16")
+    x = host_lib.random_positions(19, 40, 9, 250)
+    _, v0, l0 = e.forward(x)
+    pinned = torch.from_numpy(x).pin_memory()
+    _, v1, l1 = e.forward(pinned.numpy())
+    assert np.array_equal(l0, l1) and np.array_equal(v0, v1)
+    dx = torch.from_numpy(x).cuda()
+    dp = torch.empty((40, 362), device="cuda")
+    dv = torch.empty((40,), device="cuda")
+    dl = torch.empty((40, 362), device="cuda")
+    e.forward_device(dx.data_ptr(), 40, dp.data_ptr(), dv.data_ptr(), dl.data_ptr())
+    e.synchronize()
+    assert np.array_equal(dl.cpu().numpy(), l0) and np.array_equal(dv.cpu().numpy(), v0)
+
+
+def test_precision_switch_round_trip(gpu_engine_factory):
+    z, sd = load_golden("b9c128x10_pert")
+    x = z["positions"].astype(np.float32)
+    e = gpu_engine_factory(sd, "bf16")
+    _, _, l_bf = e.forward(x)
+    e.set_precision("fp32")
+    _, _, l_32 = e.forward(x)
+    e.set_precision("bf16")
+    _, _, l_bf2 = e.forward(x)
+    assert np.array_equal(l_bf, l_bf2)
+    assert np.abs(l_32 - z["logits"]).max() < TOL["fp32"]
