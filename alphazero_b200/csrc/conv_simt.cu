@@ -59,8 +59,8 @@ __global__ void __launch_bounds__(256) conv3x3_simt_kernel(ConvLayer L) {
         }
     }
 
-    float* out = reinterpret_cast<float*>(L.out);
-    const float* res = reinterpret_cast<const float*>(L.residual);
+    float* out = L.out32;
+    const float* res = L.res32;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int m = m0 + ty * 4 + i;

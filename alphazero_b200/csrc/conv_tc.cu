@@ -17,7 +17,10 @@
 //              tcgen05.mma.kind::f16 (128 x bn x 16) per K block, fp32
 //              accumulators in TMEM, double-buffered across tiles;
 //   warps 2-5  epilogue: tcgen05.ld of the accumulator, folded-BN bias,
-//              residual add, ReLU, frame masking, 16-bit store.
+//              fp32 residual add, ReLU, frame masking, fp32 and/or 16-bit
+//              stores, and optionally the fused policy/value 1x1 head
+//              projection (one thread owns one pixel row, so when a tile
+//              spans all output channels it sees the whole channel vector).
 // The epilogue of tile t overlaps the main loop of tile t+1.
 // Every mbarrier wait is bounded (ptx_sm100.cuh); on expiry the kernel
 // records an error code, drains its in-flight copies and frees TMEM.
@@ -36,7 +39,7 @@ namespace {
 
 constexpr int kBM = 128;  // rows per tile (TMEM lanes)
 constexpr int kBK = 64;   // K elements per stage (128 bytes of 16-bit data)
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
 
 template <int BN>
 struct TcConfig {
@@ -45,8 +48,9 @@ struct TcConfig {
     static constexpr uint32_t kBBytes = BN * kBK * 2;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr uint32_t kTmemCols = 2 * BN;
-    // ring + barriers + tmem slot + bias (256 floats) + 1 KB alignment slack
-    static constexpr int kSmem = kStages * kStageBytes + 256 + 1024 + 1024;
+    // ring + barriers + tmem slot + bias (256 floats) + head weights
+    // (3 x 256 floats) + head exchange (2 x 128 x 3 floats) + 1 KB alignment slack
+    static constexpr int kSmem = kStages * kStageBytes + 256 + 1024 + 3072 + 3072 + 1024;
 };
 
 struct TcArgs {
@@ -57,8 +61,12 @@ struct TcArgs {
     int cout;
     int rs, is, board;
     const float* bias;
-    const void* residual;
-    void* out;
+    const float* res32;
+    float* out32;
+    void* out16;
+    const float* head_w;
+    const float* head_b;
+    float* feat;
     int* err;
 };
 
@@ -110,6 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* done = bars + 2 * S + 4;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
     float* sbias = reinterpret_cast<float*>(tmem_slot + 4);
+    float* shead = sbias + 256;  // [3][cout] fused head projection weights
+    float* sxchg = shead + 768;  // [2][128][3] head partial-sum exchange
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -121,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&tfull[i]), 1);
-            mbar_init(smem_u32(&tempty[i]), 4);
+            mbar_init(smem_u32(&tempty[i]), 8);
         }
         mbar_init(smem_u32(done), 1);
         fence_barrier_init();
@@ -131,6 +141,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_relinquish();
     }
     for (int i = threadIdx.x; i < a.cout; i += kThreads) sbias[i] = a.bias[i];
+    if (a.head_w != nullptr)
+        for (int i = threadIdx.x; i < 3 * a.cout; i += kThreads) shead[i] = a.head_w[i];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -211,67 +223,121 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+        // ---------------- epilogue (warps 2..9) ----------------
+        // Two warps per TMEM lane quarter: warp w reads lanes
+        // [32*(w%4), +32) (the lane-access rule of tcgen05.ld) and column half
+        // (w-2)/4 of the tile, so one thread owns one pixel row's half.
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        constexpr int kCols = BN / 2;
+        constexpr int kChunks = kCols / 32;
         const int row = quarter * 32 + lane;
         using T = typename P::T;
         int t = 0;
         for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++t) {
             const int mt = tile / a.nsplit;
             const int n0 = (tile - mt * a.nsplit) * BN;
+            const int cbase = n0 + half * kCols;
             const int acc = t & 1;
-            if (!mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, a.err, kErrWaitEpilogue)) break;
-            tc_fence_after();
             const int m = mt * kBM + row;
             const bool in_range = m < a.m_total;
             bool board_px = false;
+            int pos = 0, pix = 0;
             if (in_range) {
-                const int q = m % a.is;
+                pos = m / a.is;
+                const int q = m - pos * a.is;
                 const int y = q / a.rs;
                 const int x = q - y * a.rs;
                 board_px = (y < a.board) && (x < a.board);
+                pix = y * a.board + x;
             }
-            T* out_row = reinterpret_cast<T*>(a.out) + (size_t)m * a.cout + n0;
-            const T* res_row = a.residual == nullptr
-                                   ? nullptr
-                                   : reinterpret_cast<const T*>(a.residual) + (size_t)m * a.cout + n0;
-            const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+            const size_t off = (size_t)m * a.cout + cbase;
+            const bool has_res = a.res32 != nullptr && in_range;
+            // The first chunk's residual is requested before the accumulator
+            // is ready; each later chunk's is requested one chunk ahead.
+            float4 r[8];
+            if (has_res) {
+                const float4* rp = reinterpret_cast<const float4*>(a.res32 + off);
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4) r[q4] = rp[q4];
+            }
+            const bool ok = mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, a.err, kErrWaitEpilogue);
+            // Leave together: no epilogue warp may be left at a named barrier.
+            if (bar_any(1, 256, !ok)) break;
+            tc_fence_after();
+            float h0 = 0.f, h1 = 0.f, h2 = 0.f;  // fused head projection partial sums
+            const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                   (uint32_t)(acc * BN + half * kCols);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c = 0; c < kChunks; ++c) {
+                const int c0 = c * 32;
                 uint32_t v[32];
                 tmem_ld_32cols(tbase + (uint32_t)c0, v);
                 tmem_ld_wait();
-                if (in_range) {
-                    float f[32];
+                if (!in_range) continue;
+                float f[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + sbias[n0 + c0 + j];
-                    if (res_row != nullptr) {
-                        const uint4* rp = reinterpret_cast<const uint4*>(res_row + c0);
+                for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + sbias[cbase + c0 + j];
+                if (has_res) {
 #pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) {
-                            uint4 r = rp[q4];
-                            float2 r0 = P::unpack(r.x), r1 = P::unpack(r.y);
-                            float2 r2 = P::unpack(r.z), r3 = P::unpack(r.w);
-                            f[q4 * 8 + 0] += r0.x; f[q4 * 8 + 1] += r0.y;
-                            f[q4 * 8 + 2] += r1.x; f[q4 * 8 + 3] += r1.y;
-                            f[q4 * 8 + 4] += r2.x; f[q4 * 8 + 5] += r2.y;
-                            f[q4 * 8 + 6] += r3.x; f[q4 * 8 + 7] += r3.y;
-                        }
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        f[q4 * 4 + 0] += r[q4].x;
+                        f[q4 * 4 + 1] += r[q4].y;
+                        f[q4 * 4 + 2] += r[q4].z;
+                        f[q4 * 4 + 3] += r[q4].w;
                     }
-                    uint4* op = reinterpret_cast<uint4*>(out_row + c0);
+                    if (c + 1 < kChunks) {
+                        const float4* rp = reinterpret_cast<const float4*>(a.res32 + off + c0 + 32);
+#pragma unroll
+                        for (int q4 = 0; q4 < 8; ++q4) r[q4] = rp[q4];
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) f[j] = board_px ? fmaxf(f[j], 0.0f) : 0.0f;
+                if (a.out32 != nullptr) {
+                    float4* op = reinterpret_cast<float4*>(a.out32 + off + c0);
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4)
+                        op[q4] = make_float4(f[q4 * 4], f[q4 * 4 + 1], f[q4 * 4 + 2], f[q4 * 4 + 3]);
+                }
+                if (a.out16 != nullptr) {
+                    uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out16) + off + c0);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
-                        float g[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            g[j] = board_px ? fmaxf(f[q4 * 8 + j], 0.0f) : 0.0f;
                         uint4 w;
-                        w.x = P::pack(g[0], g[1]);
-                        w.y = P::pack(g[2], g[3]);
-                        w.z = P::pack(g[4], g[5]);
-                        w.w = P::pack(g[6], g[7]);
+                        w.x = P::pack(f[q4 * 8 + 0], f[q4 * 8 + 1]);
+                        w.y = P::pack(f[q4 * 8 + 2], f[q4 * 8 + 3]);
+                        w.z = P::pack(f[q4 * 8 + 4], f[q4 * 8 + 5]);
+                        w.w = P::pack(f[q4 * 8 + 6], f[q4 * 8 + 7]);
                         op[q4] = w;
                     }
+                }
+                if (a.head_w != nullptr) {
+                    const float* w0 = shead + cbase + c0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        h0 = fmaf(f[j], w0[j], h0);
+                        h1 = fmaf(f[j], w0[a.cout + j], h1);
+                        h2 = fmaf(f[j], w0[2 * a.cout + j], h2);
+                    }
+                }
+            }
+            if (a.head_w != nullptr) {
+                // Half 1 hands its partial sums to half 0 through a
+                // double-buffered exchange (indexed by accumulator).
+                float* xs = sxchg + acc * (kBM * 3) + row * 3;
+                if (half == 1) {
+                    xs[0] = h0;
+                    xs[1] = h1;
+                    xs[2] = h2;
+                }
+                named_barrier_sync(1, 256);
+                if (half == 0 && board_px) {
+                    const int hw = a.board * a.board;
+                    float* fr = a.feat + (size_t)pos * 3 * hw;
+                    fr[pix] = fmaxf(h0 + xs[0] + a.head_b[0], 0.f);
+                    fr[hw + pix] = fmaxf(h1 + xs[1] + a.head_b[1], 0.f);
+                    fr[2 * hw + pix] = fmaxf(h2 + xs[2] + a.head_b[2], 0.f);
                 }
             }
             tc_fence_before();
@@ -292,6 +358,8 @@ template <int BN, bool FP16>
 cudaError_t launch_bn(const ConvLayer& L, const CUtensorMap& tmA, const CUtensorMap& tmB,
                       int grid_limit, cudaStream_t stream) {
     using Cfg = TcConfig<BN>;
+    // The fused head projection needs every output channel of a row in one tile.
+    if (L.head_w != nullptr && L.cout != BN) return cudaErrorInvalidValue;
     TcArgs a;
     a.m_total = L.m_total;
     a.nsplit = L.cout / BN;
@@ -302,8 +370,12 @@ cudaError_t launch_bn(const ConvLayer& L, const CUtensorMap& tmA, const CUtensor
     a.is = L.g.is;
     a.board = L.g.board;
     a.bias = L.bias;
-    a.residual = L.residual;
-    a.out = L.out;
+    a.res32 = L.res32;
+    a.out32 = L.out32;
+    a.out16 = L.out16;
+    a.head_w = L.head_w;
+    a.head_b = L.head_b;
+    a.feat = L.feat;
     a.err = L.err;
     int grid = a.num_tiles < grid_limit ? a.num_tiles : grid_limit;
     if (grid < 1) grid = 1;

@@ -98,15 +98,20 @@ struct mg_engine {
     int w16_prec = -1;
     std::vector<float*> d_w32;
     std::vector<float*> d_bias;
-    float* d_head = nullptr;
-    HeadParams hp{};
+    float* d_head = nullptr;  // packed head parameters
+    const float* d_head_w = nullptr;
+    const float* d_head_b = nullptr;
+    HeadFc fc{};
 
     // Device buffers for `alloc_batch` positions, element size `alloc_elem`.
     int alloc_batch = 0;
     int alloc_elem = 0;
-    void* d_stage = nullptr;
-    void* d_x = nullptr;
-    void* d_t = nullptr;
+    void* d_stage = nullptr;  // staged input rows, operand type
+    float* d_x = nullptr;     // fp32 residual stream
+    void* d_x16 = nullptr;    // 16-bit copy of d_x (tensor-core operand)
+    void* d_t = nullptr;      // block-internal activation, operand type
+    float* d_feat = nullptr;  // head features [positions][3*hw]
+    float* d_fc = nullptr;    // FC outputs [positions][actions + hidden]
     float* d_states = nullptr;
     float* d_probs = nullptr;
     float* d_logits = nullptr;
@@ -127,12 +132,13 @@ struct mg_engine {
 
     void free_buffers() {
         drop_graphs();
-        for (void* p : {d_stage, d_x, d_t}) if (p) cudaFree(p);
+        for (void* p : {d_stage, (void*)d_x, d_x16, d_t, (void*)d_feat, (void*)d_fc}) if (p) cudaFree(p);
         for (void* p : {(void*)d_states, (void*)d_probs, (void*)d_logits, (void*)d_value, (void*)d_err})
             if (p) cudaFree(p);
         if (h_states) cudaFreeHost(h_states);
         if (h_err) cudaFreeHost(h_err);
-        d_stage = d_x = d_t = nullptr;
+        d_stage = d_x16 = d_t = nullptr;
+        d_x = d_feat = d_fc = nullptr;
         d_states = d_probs = d_logits = d_value = nullptr;
         d_err = nullptr;
         h_states = nullptr;
@@ -227,28 +233,37 @@ struct mg_engine {
 
     void upload_heads() {
         const int A = actions, H = net.hidden, C = cpad;
-        // Policy features are read in c*hw + p order; with eigen_compat the
-        // FC columns are permuted from the column-major flatten c + 2p
-        // (src/eigen_engine.cpp:242) so the kernel is the same.
-        std::vector<float> pfc((size_t)A * 2 * hw);
+        // Head projection: folded 1x1 convs [3][C] (policy 0, policy 1, value).
+        std::vector<float> hw3((size_t)3 * C, 0.0f), hb3(3);
+        for (int c = 0; c < 2; ++c)
+            for (int k = 0; k < net.filters; ++k)
+                hw3[(size_t)c * C + k] = net.pconv_w[(size_t)c * net.filters + k] * net.pbn.scale[c];
+        for (int k = 0; k < net.filters; ++k) hw3[(size_t)2 * C + k] = net.vconv_w[k] * net.vbn.scale[0];
+        hb3[0] = net.pbn.bias[0];
+        hb3[1] = net.pbn.bias[1];
+        hb3[2] = net.vbn.bias[0];
+        // FC block matrix over feat = [policy c*hw + p | value p]:
+        // rows < A are policy_fc (its columns permuted from the column-major
+        // flatten c + 2p of src/eigen_engine.cpp:242 under eigen_compat),
+        // rows >= A are value_fc1.
+        const int K = 3 * hw;
+        std::vector<float> wcat((size_t)(A + H) * K, 0.0f), bcat(A + H);
         const bool eig = (flags & MG_FLAG_EIGEN_COMPAT) != 0;
-        for (int a = 0; a < A; ++a)
+        for (int a = 0; a < A; ++a) {
             for (int c = 0; c < 2; ++c)
                 for (int p = 0; p < hw; ++p) {
                     const int src = eig ? (c + 2 * p) : (c * hw + p);
-                    pfc[(size_t)a * 2 * hw + c * hw + p] = net.pfc_w[(size_t)a * 2 * hw + src];
+                    wcat[(size_t)a * K + c * hw + p] = net.pfc_w[(size_t)a * 2 * hw + src];
                 }
-        std::vector<float> pcw((size_t)2 * C, 0.0f), vcw(C, 0.0f);
-        for (int c = 0; c < 2; ++c)
-            for (int k = 0; k < net.filters; ++k)
-                pcw[(size_t)c * C + k] = net.pconv_w[(size_t)c * net.filters + k] * net.pbn.scale[c];
-        for (int k = 0; k < net.filters; ++k) vcw[k] = net.vconv_w[k] * net.vbn.scale[0];
+            bcat[a] = net.pfc_b[a];
+        }
+        for (int j = 0; j < H; ++j) {
+            for (int p = 0; p < hw; ++p) wcat[(size_t)(A + j) * K + 2 * hw + p] = net.v1_w[(size_t)j * hw + p];
+            bcat[A + j] = net.v1_b[j];
+        }
         std::vector<std::pair<const float*, size_t>> parts = {
-            {pcw.data(), pcw.size()},          {net.pbn.bias.data(), 2},
-            {vcw.data(), vcw.size()},          {net.vbn.bias.data(), 1},
-            {pfc.data(), pfc.size()},          {net.pfc_b.data(), (size_t)A},
-            {net.v1_w.data(), (size_t)H * hw}, {net.v1_b.data(), (size_t)H},
-            {net.v2_w.data(), (size_t)H},      {net.v2_b.data(), 1}};
+            {hw3.data(), hw3.size()},   {hb3.data(), 3},           {wcat.data(), wcat.size()},
+            {bcat.data(), bcat.size()}, {net.v2_w.data(), (size_t)H}, {net.v2_b.data(), 1}};
         std::vector<size_t> offs;
         size_t total = 0;
         for (auto& pr : parts) {
@@ -261,25 +276,15 @@ struct mg_engine {
         d_head = dalloc<float>(total, "cudaMalloc(heads)");
         ck(cudaMemcpy(d_head, packed.data(), total * sizeof(float), cudaMemcpyHostToDevice),
            "cudaMemcpy(heads)");
-        hp.board = net.board;
-        hp.hw = hw;
-        hp.c = C;
-        hp.actions = A;
-        hp.hidden = H;
-        hp.g = g;
-        hp.pconv_w = d_head + offs[0];
-        hp.pconv_b = d_head + offs[1];
-        hp.vconv_w = d_head + offs[2];
-        hp.vconv_b = d_head + offs[3];
-        hp.pfc_w = d_head + offs[4];
-        hp.pfc_b = d_head + offs[5];
-        hp.v1_w = d_head + offs[6];
-        hp.v1_b = d_head + offs[7];
-        hp.v2_w = d_head + offs[8];
-        hp.v2_b = d_head + offs[9];
-        const size_t smem = heads_smem_bytes(hp);
-        if (smem > 48 * 1024)
-            throw std::runtime_error("board / value-head sizes exceed the heads kernel's shared memory");
+        d_head_w = d_head + offs[0];
+        d_head_b = d_head + offs[1];
+        fc.hw = hw;
+        fc.actions = A;
+        fc.hidden = H;
+        fc.w = d_head + offs[2];
+        fc.b = d_head + offs[3];
+        fc.v2_w = d_head + offs[4];
+        fc.v2_b = d_head + offs[5];
     }
 
     // Device weights in the current precision's type (16-bit for the tensor
@@ -331,8 +336,11 @@ struct mg_engine {
         free_buffers();
         const size_t rows = (size_t)max_batch * g.is;
         d_stage = dalloc<uint8_t>(rows * kStagedChannels * elem, "cudaMalloc(stage)");
-        d_x = dalloc<uint8_t>(rows * cpad * elem, "cudaMalloc(act x)");
+        d_x = dalloc<float>(rows * cpad, "cudaMalloc(act x)");
+        d_x16 = dalloc<uint16_t>(rows * cpad, "cudaMalloc(act x16)");
         d_t = dalloc<uint8_t>(rows * cpad * elem, "cudaMalloc(act t)");
+        d_feat = dalloc<float>((size_t)max_batch * 3 * hw, "cudaMalloc(feat)");
+        d_fc = dalloc<float>((size_t)max_batch * (actions + net.hidden), "cudaMalloc(fc)");
         d_states = dalloc<float>((size_t)max_batch * planes * hw, "cudaMalloc(states)");
         ck(cudaMemset(d_states, 0, (size_t)max_batch * planes * hw * sizeof(float)),
            "cudaMemset(states)");
@@ -370,27 +378,43 @@ struct mg_engine {
 
     // ---- kernels ---------------------------------------------------------
 
+    // Whether the last trunk layer computes the head projection in its
+    // epilogue (tensor-core path with one tile spanning all channels).
+    bool fused_heads(int bucket) const {
+        return precision != MG_PREC_FP32 && choose_bn(bucket * g.is) == cpad;
+    }
+
     ConvLayer layer_desc(int li, int bucket) const {
-        ConvLayer L;
+        ConvLayer L{};
         L.m_total = bucket * g.is;
         L.cin = wcin[li];
         L.cout = cpad;
         L.g = g;
         L.bias = d_bias[li];
         L.err = d_err;
-        L.weight = precision == MG_PREC_FP32 ? (const void*)d_w32[li] : (const void*)d_w16[li];
-        if (li == 0) {
+        const bool f32 = precision == MG_PREC_FP32;
+        L.weight = f32 ? (const void*)d_w32[li] : (const void*)d_w16[li];
+        if (li == 0) {  // input conv: staged planes -> x
             L.in = d_stage;
-            L.residual = nullptr;
-            L.out = d_x;
+            L.out32 = d_x;
+            L.out16 = f32 ? nullptr : d_x16;
         } else if (li % 2 == 1) {  // conv1 of a block: x -> t
-            L.in = d_x;
-            L.residual = nullptr;
-            L.out = d_t;
+            L.in = f32 ? (const void*)d_x : (const void*)d_x16;
+            if (f32) L.out32 = reinterpret_cast<float*>(d_t);
+            else L.out16 = d_t;
         } else {  // conv2: t (+ x) -> x, in place over the residual rows
             L.in = d_t;
-            L.residual = d_x;
-            L.out = d_x;
+            L.res32 = d_x;
+            L.out32 = d_x;
+            L.out16 = f32 ? nullptr : d_x16;
+        }
+        if (li == n_convs - 1 && fused_heads(bucket)) {
+            // The trunk output is consumed only by the heads.
+            L.out32 = nullptr;
+            L.out16 = nullptr;
+            L.head_w = d_head_w;
+            L.head_b = d_head_b;
+            L.feat = d_feat;
         }
         return L;
     }
@@ -411,7 +435,10 @@ struct mg_engine {
 
     void enqueue_trunk_heads(int bucket) {
         for (int li = 0; li < n_convs; ++li) launch_conv(li, bucket);
-        ck(launch_heads(d_x, act_type(), hp, bucket, d_probs, d_logits, d_value, stream),
+        if (!fused_heads(bucket))
+            ck(launch_head_projection(d_x, bucket, cpad, g, d_head_w, d_head_b, d_feat, stream),
+               "head projection launch");
+        ck(launch_heads_fc(d_feat, fc, bucket, d_fc, d_probs, d_logits, d_value, stream),
            "heads launch");
     }
 
@@ -734,7 +761,8 @@ int mg_launch_conv(mg_engine* e, int n, int layer, int reps) {
 int mg_launches_per_forward(mg_engine* e, int n) {
     if (e == nullptr || !e->loaded) return 0;
     (void)n;
-    return 1 /* stage */ + e->n_convs + 1 /* heads */;
+    const int bucket = e->bucket_for(std::max(1, std::min(n, e->max_batch)));
+    return 1 /* stage */ + e->n_convs + (e->fused_heads(bucket) ? 0 : 1) + 2 /* FC, finish */;
 }
 
 }  // extern "C"

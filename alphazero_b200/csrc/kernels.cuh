@@ -33,19 +33,34 @@ inline FrameGeom make_frame(int board) {
 
 // One 3x3 convolution layer, stride 1, zero padding 1, with folded
 // BatchNorm bias, optional residual add and ReLU:
-//   out[r, co] = relu(sum_{tap, ci} in[r + off(tap), ci] * W[co, tap, ci]
-//                     + bias[co] (+ residual[r, co]))      on board pixels,
-//   out[r, co] = 0                                          on frame pixels.
+//   y[r, co] = relu(sum_{tap, ci} in[r + off(tap), ci] * W[co, tap, ci]
+//                   + bias[co] (+ res32[r, co]))     on board pixels,
+//   y[r, co] = 0                                     on frame pixels,
+// written as fp32 to out32 and/or as the 16-bit operand type to out16.
+// The residual stream is kept in fp32 (res32 / out32) so 16-bit rounding
+// enters only through the tensor-core operands, not the running sum.
+//
+// Optional fused head projection (tensor-core path, when one tile spans all
+// output channels): for each board pixel p of position n,
+//   feat[n][c*hw + p] = relu(sum_co y[r, co] * head_w[c][co] + head_b[c])
+// for c = 0, 1 (policy) and c = 2 (value): the policy and value 1x1
+// convolutions with folded BN and ReLU (src/eigen_engine.cpp:237-241,
+// :257-260), laid out as the policy features in c*hw + p order followed by
+// the value features.
 struct ConvLayer {
     int m_total;            // rows = positions * IS
     int cin;                // input channels (multiple of 64)
     int cout;               // output channels (multiple of 64)
     FrameGeom g;
-    const void* in;         // [m_total][cin]
-    const void* weight;     // [cout][9][cin]
+    const void* in;         // [m_total][cin], operand type
+    const void* weight;     // [cout][9][cin], operand type
     const float* bias;      // [cout]
-    const void* residual;   // [m_total][cout] or nullptr (may equal out)
-    void* out;              // [m_total][cout]
+    const float* res32;     // [m_total][cout] fp32 or nullptr (may equal out32)
+    float* out32;           // [m_total][cout] fp32 or nullptr
+    void* out16;            // [m_total][cout] 16-bit or nullptr (tensor-core path)
+    const float* head_w;    // [3][cout] or nullptr: fused head projection
+    const float* head_b;    // [3]
+    float* feat;            // [positions][3*B*B]
     int* err;               // device status word
 };
 
@@ -80,23 +95,29 @@ cudaError_t launch_stage_input(const float* states, int n_valid, int n_pos, int 
                                const FrameGeom& g, int cpad, bool eigen_order, ActType t,
                                void* out, cudaStream_t stream);
 
-// Policy / value heads over the trunk output (framed NHWC, `c` channels).
-struct HeadParams {
-    int board, hw, c, actions, hidden;
-    FrameGeom g;
-    const float* pconv_w;  // [2][c]  (BatchNorm folded)
-    const float* pconv_b;  // [2]
-    const float* vconv_w;  // [c]
-    const float* vconv_b;  // [1]
-    const float* pfc_w;    // [actions][2*hw], column c*hw + p
-    const float* pfc_b;    // [actions]
-    const float* v1_w;     // [hidden][hw]
-    const float* v1_b;     // [hidden]
-    const float* v2_w;     // [hidden]
-    const float* v2_b;     // [1]
+// Head projection as a separate pass (fp32 SIMT path, or when the
+// tensor-core tile does not span all channels): the 1x1 policy / value
+// convolutions over an fp32 trunk [positions * IS][c] -> feat (see
+// ConvLayer for the formula).
+cudaError_t launch_head_projection(const float* trunk, int positions, int c, const FrameGeom& g,
+                                   const float* head_w, const float* head_b, float* feat,
+                                   cudaStream_t stream);
+
+// Policy FC and value FC1 as one fp32 GEMM over the features
+// feat[n] = [policy (2*hw) | value (hw)]:
+//   out[n][o] = sum_k feat[n][k] * W[o][k] + b[o],  o < actions + hidden,
+// where W = [[policy_fc.weight, 0], [0, value_fc1.weight]] (the zero blocks
+// are skipped), then per position a max-subtracted softmax over the
+// `actions` logits and value = tanh(value_fc2(relu(hidden))) (src/eigen_engine.cpp:243-269).
+struct HeadFc {
+    int hw, actions, hidden;
+    const float* w;     // [actions + hidden][3*hw]
+    const float* b;     // [actions + hidden]
+    const float* v2_w;  // [hidden]
+    const float* v2_b;  // [1]
 };
-cudaError_t launch_heads(const void* trunk, ActType t, const HeadParams& h, int n_pos,
-                         float* probs, float* logits, float* value, cudaStream_t stream);
-size_t heads_smem_bytes(const HeadParams& h);
+cudaError_t launch_heads_fc(const float* feat, const HeadFc& h, int positions,
+                            float* scratch /* [positions][actions + hidden] */, float* probs,
+                            float* logits, float* value, cudaStream_t stream);
 
 }  // namespace mgb

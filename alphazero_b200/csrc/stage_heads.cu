@@ -1,4 +1,4 @@
-// Input staging and the fused policy / value heads.
+// Input staging and the policy / value heads.
 #include "kernels.cuh"
 
 #include <cuda_bf16.h>
@@ -7,43 +7,54 @@
 namespace mgb {
 namespace {
 
-template <typename T>
-__device__ __forceinline__ T from_float(float v);
-template <>
-__device__ __forceinline__ float from_float<float>(float v) { return v; }
-template <>
-__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
-    return __float2bfloat16_rn(v);
+__device__ __forceinline__ uint32_t pack2(float a, float b, ActType t) {
+    if (t == ActType::BF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
 }
-template <>
-__device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
 
-__device__ __forceinline__ float to_float(float v) { return v; }
-__device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
-__device__ __forceinline__ float to_float(__half v) { return __half2float(v); }
-
-// One thread per framed row: gathers the row's `planes` input values
-// (strided across planes, coalesced across threads) and writes cpad
-// channels, zero beyond `planes` and on frame pixels / absent positions.
-template <typename T>
+// One thread per (framed row, group of 8 channels): gathers up to 8 input
+// planes of the row's pixel (strided across planes, coalesced across rows)
+// and writes them as one 16-byte (16-bit types) or 32-byte (fp32) vector;
+// channels >= planes, frame pixels and absent positions are zero.
+template <ActType T>
 __global__ void stage_input_kernel(const float* __restrict__ states, int n_valid, int rows,
                                    int planes, FrameGeom g, int cpad, int eigen_order,
-                                   T* __restrict__ out) {
-    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+                                   void* __restrict__ out) {
+    const int groups = cpad >> 3;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    const int m = idx / groups;
+    const int c8 = (idx - m * groups) * 8;
     if (m >= rows) return;
     const int n = m / g.is;
     const int q = m - n * g.is;
     const int y = q / g.rs;
     const int x = q - y * g.rs;
-    T* o = out + (size_t)m * cpad;
     const bool live = (n < n_valid) && (y < g.board) && (x < g.board);
     const int hw = g.board * g.board;
     const int p = y * g.board + x;
     const float* s = states + (size_t)n * planes * hw;
-    for (int c = 0; c < cpad; ++c) {
-        float v = 0.0f;
-        if (live && c < planes) v = eigen_order ? s[c + (size_t)p * planes] : s[(size_t)c * hw + p];
-        o[c] = from_float<T>(v);
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int c = c8 + j;
+        v[j] = (live && c < planes) ? (eigen_order ? s[c + (size_t)p * planes] : s[(size_t)c * hw + p])
+                                    : 0.0f;
+    }
+    if (T == ActType::FP32) {
+        float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)m * cpad + c8);
+        o[0] = make_float4(v[0], v[1], v[2], v[3]);
+        o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint4 w;
+        w.x = pack2(v[0], v[1], T);
+        w.y = pack2(v[2], v[3], T);
+        w.z = pack2(v[4], v[5], T);
+        w.w = pack2(v[6], v[7], T);
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + (size_t)m * cpad + c8) = w;
     }
 }
 
@@ -59,118 +70,132 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-constexpr int kHeadPos = 4;  // positions per CTA (shares the FC weight reads)
-constexpr int kHeadWarps = 8;
-
-// Fused heads for kHeadPos positions per CTA (src/eigen_engine.cpp:236-270):
-//  1. policy 1x1 conv (c -> 2) and value 1x1 conv (c -> 1) with folded BN
-//     and ReLU, one warp per pixel, lanes across channels;
-//  2. policy FC (2*hw -> actions) and value FC1 (hw -> hidden) + ReLU, one
-//     warp per output row, lanes across inputs, all positions of the CTA at
-//     once so each weight row is read once per CTA;
-//  3. per position: max-subtracted softmax over the logits, value FC2 and
-//     tanh.  All arithmetic is fp32.
-template <typename T>
-__global__ void __launch_bounds__(kHeadWarps * 32)
-    heads_kernel(const T* __restrict__ trunk, HeadParams h, int n_pos, float* __restrict__ probs,
-                 float* __restrict__ logits, float* __restrict__ value) {
-    extern __shared__ float sm[];
-    const int c = h.c, hw = h.hw, A = h.actions, V = h.hidden;
-    float* sw = sm;                         // 3*c
-    float* pf = sw + 3 * c;                 // kHeadPos * 2*hw
-    float* vf = pf + kHeadPos * 2 * hw;     // kHeadPos * hw
-    float* lg = vf + kHeadPos * hw;         // kHeadPos * A
-    float* hid = lg + kHeadPos * A;         // kHeadPos * V
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos0 = blockIdx.x * kHeadPos;
-
-    for (int i = threadIdx.x; i < c; i += blockDim.x) {
-        sw[i] = h.pconv_w[i];
-        sw[c + i] = h.pconv_w[c + i];
-        sw[2 * c + i] = h.vconv_w[i];
+// One warp per board pixel: the three 1x1 head convolutions over the fp32
+// trunk row, lanes across channels.
+__global__ void head_projection_kernel(const float* __restrict__ trunk, int positions, int c,
+                                       FrameGeom g, const float* __restrict__ hw3,
+                                       const float* __restrict__ hb, float* __restrict__ feat) {
+    const int hw = g.board * g.board;
+    const int job = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (job >= positions * hw) return;
+    const int n = job / hw, p = job - n * hw;
+    const int y = p / g.board, x = p - y * g.board;
+    const float* t = trunk + ((size_t)n * g.is + (size_t)y * g.rs + x) * c;
+    float d0 = 0.f, d1 = 0.f, d2 = 0.f;
+    for (int ch = lane; ch < c; ch += 32) {
+        const float v = t[ch];
+        d0 = fmaf(v, hw3[ch], d0);
+        d1 = fmaf(v, hw3[c + ch], d1);
+        d2 = fmaf(v, hw3[2 * c + ch], d2);
     }
-    __syncthreads();
+    d0 = warp_sum(d0);
+    d1 = warp_sum(d1);
+    d2 = warp_sum(d2);
+    if (lane == 0) {
+        float* fr = feat + (size_t)n * 3 * hw;
+        fr[p] = fmaxf(d0 + hb[0], 0.f);
+        fr[hw + p] = fmaxf(d1 + hb[1], 0.f);
+        fr[2 * hw + p] = fmaxf(d2 + hb[2], 0.f);
+    }
+}
 
-    const float pb0 = h.pconv_b[0], pb1 = h.pconv_b[1], vb = h.vconv_b[0];
-    for (int job = warp; job < kHeadPos * hw; job += kHeadWarps) {
-        const int pp = job / hw, p = job - pp * hw;
-        const int n = pos0 + pp;
-        float d0 = 0.f, d1 = 0.f, d2 = 0.f;
-        if (n < n_pos) {
-            const int y = p / h.board, x = p - y * h.board;
-            const T* t = trunk + ((size_t)n * h.g.is + (size_t)y * h.g.rs + x) * c;
-            for (int ch = lane; ch < c; ch += 32) {
-                const float v = to_float(t[ch]);
-                d0 = fmaf(v, sw[ch], d0);
-                d1 = fmaf(v, sw[c + ch], d1);
-                d2 = fmaf(v, sw[2 * c + ch], d2);
-            }
-        }
-        d0 = warp_sum(d0);
-        d1 = warp_sum(d1);
-        d2 = warp_sum(d2);
-        if (lane == 0) {
-            pf[pp * 2 * hw + p] = fmaxf(d0 + pb0, 0.f);
-            pf[pp * 2 * hw + hw + p] = fmaxf(d1 + pb1, 0.f);
-            vf[pp * hw + p] = fmaxf(d2 + vb, 0.f);
-        }
-    }
-    __syncthreads();
+constexpr int kFcTM = 32;  // positions per tile
+constexpr int kFcTO = 32;  // outputs per tile
+constexpr int kFcTK = 64;  // K slice
 
-    for (int a = warp; a < A; a += kHeadWarps) {
-        float acc[kHeadPos];
+// out[n][o] = sum_k feat[n][k] * W[o][k] + b[o] for a 32 x 32 tile, each of
+// 256 threads owning 2 positions x 2 outputs.  K slices of 64 are staged in
+// shared memory while the next slice is already being fetched into
+// registers.  Output tiles that lie wholly in the policy (o < actions) or
+// value (o >= actions) rows only walk their own K block.
+__global__ void __launch_bounds__(256) heads_fc_kernel(const float* __restrict__ feat, HeadFc h,
+                                                       int positions, float* __restrict__ out) {
+    __shared__ float sF[kFcTK][kFcTM + 1];
+    __shared__ float sW[kFcTK][kFcTO + 1];
+    const int K = 3 * h.hw;
+    const int O = h.actions + h.hidden;
+    const int n0 = blockIdx.x * kFcTM;
+    const int o0 = blockIdx.y * kFcTO;
+    const int kbeg = (o0 >= h.actions) ? 2 * h.hw : 0;
+    const int kend = (o0 + kFcTO <= h.actions) ? 2 * h.hw : K;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    // Each thread stages 8 feature and 8 weight values per slice: element
+    // (row r = idx / 64, k = idx % 64) for idx = threadIdx.x + i * 256.
+    float pF[8], pW[8];
+    auto fetch = [&](int k0) {
 #pragma unroll
-        for (int pp = 0; pp < kHeadPos; ++pp) acc[pp] = 0.f;
-        const float* wr = h.pfc_w + (size_t)a * 2 * hw;
-        for (int k = lane; k < 2 * hw; k += 32) {
-            const float wv = wr[k];
-#pragma unroll
-            for (int pp = 0; pp < kHeadPos; ++pp) acc[pp] = fmaf(wv, pf[pp * 2 * hw + k], acc[pp]);
+        for (int i = 0; i < 8; ++i) {
+            const int idx = threadIdx.x + i * 256;
+            const int r = idx >> 6, k = idx & 63;
+            const int kk = k0 + k;
+            const bool kin = kk < kend;
+            const int n = n0 + r, o = o0 + r;
+            pF[i] = (kin && n < positions) ? feat[(size_t)n * K + kk] : 0.f;
+            pW[i] = (kin && o < O) ? h.w[(size_t)o * K + kk] : 0.f;
         }
+    };
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    fetch(kbeg);
+    for (int k0 = kbeg; k0 < kend; k0 += kFcTK) {
 #pragma unroll
-        for (int pp = 0; pp < kHeadPos; ++pp) {
-            const float s = warp_sum(acc[pp]);
-            if (lane == 0) lg[pp * A + a] = s + h.pfc_b[a];
+        for (int i = 0; i < 8; ++i) {
+            const int idx = threadIdx.x + i * 256;
+            const int r = idx >> 6, k = idx & 63;
+            sF[k][r] = pF[i];
+            sW[k][r] = pW[i];
+        }
+        __syncthreads();
+        if (k0 + kFcTK < kend) fetch(k0 + kFcTK);
+#pragma unroll 16
+        for (int k = 0; k < kFcTK; ++k) {
+            const float a0 = sF[k][ty * 2], a1 = sF[k][ty * 2 + 1];
+            const float w0 = sW[k][tx * 2], w1 = sW[k][tx * 2 + 1];
+            acc[0][0] = fmaf(a0, w0, acc[0][0]);
+            acc[0][1] = fmaf(a0, w1, acc[0][1]);
+            acc[1][0] = fmaf(a1, w0, acc[1][0]);
+            acc[1][1] = fmaf(a1, w1, acc[1][1]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int n = n0 + ty * 2 + i;
+        if (n >= positions) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int o = o0 + tx * 2 + j;
+            if (o < O) out[(size_t)n * O + o] = acc[i][j] + h.b[o];
         }
     }
-    for (int j = warp; j < V; j += kHeadWarps) {
-        float acc[kHeadPos];
-#pragma unroll
-        for (int pp = 0; pp < kHeadPos; ++pp) acc[pp] = 0.f;
-        const float* wr = h.v1_w + (size_t)j * hw;
-        for (int k = lane; k < hw; k += 32) {
-            const float wv = wr[k];
-#pragma unroll
-            for (int pp = 0; pp < kHeadPos; ++pp) acc[pp] = fmaf(wv, vf[pp * hw + k], acc[pp]);
-        }
-#pragma unroll
-        for (int pp = 0; pp < kHeadPos; ++pp) {
-            const float s = warp_sum(acc[pp]);
-            if (lane == 0) hid[pp * V + j] = fmaxf(s + h.v1_b[j], 0.f);
-        }
-    }
-    __syncthreads();
+}
 
-    for (int pp = warp; pp < kHeadPos; pp += kHeadWarps) {
-        const int n = pos0 + pp;
-        if (n >= n_pos) continue;
-        const float* l = lg + pp * A;
-        float mx = -INFINITY;
-        for (int a = lane; a < A; a += 32) mx = fmaxf(mx, l[a]);
-        mx = warp_max(mx);
-        float sum = 0.f;
-        for (int a = lane; a < A; a += 32) sum += expf(l[a] - mx);
-        sum = warp_sum(sum);
-        const float inv = 1.0f / sum;
-        for (int a = lane; a < A; a += 32) {
-            probs[(size_t)n * A + a] = expf(l[a] - mx) * inv;
-            if (logits != nullptr) logits[(size_t)n * A + a] = l[a];
-        }
-        float v = 0.f;
-        for (int j = lane; j < V; j += 32) v = fmaf(hid[pp * V + j], h.v2_w[j], v);
-        v = warp_sum(v);
-        if (lane == 0) value[n] = tanhf(v + h.v2_b[0]);
+// One warp per position: softmax of the logits and the value head's last
+// two steps (ReLU of FC1, FC2, tanh).
+__global__ void heads_finish_kernel(const float* __restrict__ fc, HeadFc h, int positions,
+                                    float* __restrict__ probs, float* __restrict__ logits,
+                                    float* __restrict__ value) {
+    const int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (n >= positions) return;
+    const int A = h.actions, O = h.actions + h.hidden;
+    const float* l = fc + (size_t)n * O;
+    float mx = -INFINITY;
+    for (int a = lane; a < A; a += 32) mx = fmaxf(mx, l[a]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int a = lane; a < A; a += 32) sum += expf(l[a] - mx);
+    sum = warp_sum(sum);
+    const float inv = 1.0f / sum;
+    for (int a = lane; a < A; a += 32) {
+        const float la = l[a];
+        probs[(size_t)n * A + a] = expf(la - mx) * inv;
+        logits[(size_t)n * A + a] = la;
     }
+    float v = 0.f;
+    for (int j = lane; j < h.hidden; j += 32) v = fmaf(fmaxf(l[A + j], 0.f), h.v2_w[j], v);
+    v = warp_sum(v);
+    if (lane == 0) value[n] = tanhf(v + h.v2_b[0]);
 }
 
 }  // namespace
@@ -178,54 +203,52 @@ __global__ void __launch_bounds__(kHeadWarps * 32)
 cudaError_t launch_stage_input(const float* states, int n_valid, int n_pos, int planes,
                                const FrameGeom& g, int cpad, bool eigen_order, ActType t,
                                void* out, cudaStream_t stream) {
-    const int rows = n_pos * g.is;
-    const int threads = 128;
-    const int blocks = (rows + threads - 1) / threads;
+    if (cpad % 8 != 0) return cudaErrorInvalidValue;
+    const long threads_total = (long)n_pos * g.is * (cpad / 8);
+    const int threads = 256;
+    const long blocks = (threads_total + threads - 1) / threads;
     if (blocks == 0) return cudaSuccess;
+    const int rows = n_pos * g.is;
+    const int eo = eigen_order ? 1 : 0;
     switch (t) {
         case ActType::BF16:
-            stage_input_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(
-                states, n_valid, rows, planes, g, cpad, eigen_order ? 1 : 0,
-                reinterpret_cast<__nv_bfloat16*>(out));
+            stage_input_kernel<ActType::BF16><<<(unsigned)blocks, threads, 0, stream>>>(
+                states, n_valid, rows, planes, g, cpad, eo, out);
             break;
         case ActType::FP16:
-            stage_input_kernel<__half><<<blocks, threads, 0, stream>>>(
-                states, n_valid, rows, planes, g, cpad, eigen_order ? 1 : 0,
-                reinterpret_cast<__half*>(out));
+            stage_input_kernel<ActType::FP16><<<(unsigned)blocks, threads, 0, stream>>>(
+                states, n_valid, rows, planes, g, cpad, eo, out);
             break;
         case ActType::FP32:
-            stage_input_kernel<float><<<blocks, threads, 0, stream>>>(
-                states, n_valid, rows, planes, g, cpad, eigen_order ? 1 : 0,
-                reinterpret_cast<float*>(out));
+            stage_input_kernel<ActType::FP32><<<(unsigned)blocks, threads, 0, stream>>>(
+                states, n_valid, rows, planes, g, cpad, eo, out);
             break;
     }
     return cudaGetLastError();
 }
 
-size_t heads_smem_bytes(const HeadParams& h) {
-    return sizeof(float) *
-           (size_t)(3 * h.c + kHeadPos * (2 * h.hw + h.hw + h.actions + h.hidden));
+cudaError_t launch_head_projection(const float* trunk, int positions, int c, const FrameGeom& g,
+                                   const float* head_w, const float* head_b, float* feat,
+                                   cudaStream_t stream) {
+    const int jobs = positions * g.board * g.board;
+    const int warps_per_block = 8;
+    const int blocks = (jobs + warps_per_block - 1) / warps_per_block;
+    if (blocks == 0) return cudaSuccess;
+    head_projection_kernel<<<blocks, warps_per_block * 32, 0, stream>>>(trunk, positions, c, g,
+                                                                        head_w, head_b, feat);
+    return cudaGetLastError();
 }
 
-cudaError_t launch_heads(const void* trunk, ActType t, const HeadParams& h, int n_pos,
-                         float* probs, float* logits, float* value, cudaStream_t stream) {
-    const int blocks = (n_pos + kHeadPos - 1) / kHeadPos;
-    if (blocks == 0) return cudaSuccess;
-    const size_t smem = heads_smem_bytes(h);
-    switch (t) {
-        case ActType::BF16:
-            heads_kernel<__nv_bfloat16><<<blocks, kHeadWarps * 32, smem, stream>>>(
-                reinterpret_cast<const __nv_bfloat16*>(trunk), h, n_pos, probs, logits, value);
-            break;
-        case ActType::FP16:
-            heads_kernel<__half><<<blocks, kHeadWarps * 32, smem, stream>>>(
-                reinterpret_cast<const __half*>(trunk), h, n_pos, probs, logits, value);
-            break;
-        case ActType::FP32:
-            heads_kernel<float><<<blocks, kHeadWarps * 32, smem, stream>>>(
-                reinterpret_cast<const float*>(trunk), h, n_pos, probs, logits, value);
-            break;
-    }
+cudaError_t launch_heads_fc(const float* feat, const HeadFc& h, int positions, float* scratch,
+                            float* probs, float* logits, float* value, cudaStream_t stream) {
+    if (positions == 0) return cudaSuccess;
+    dim3 grid((positions + kFcTM - 1) / kFcTM, (h.actions + h.hidden + kFcTO - 1) / kFcTO);
+    heads_fc_kernel<<<grid, 256, 0, stream>>>(feat, h, positions, scratch);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const int warps_per_block = 8;
+    heads_finish_kernel<<<(positions + warps_per_block - 1) / warps_per_block, warps_per_block * 32,
+                          0, stream>>>(scratch, h, positions, probs, logits, value);
     return cudaGetLastError();
 }
 

@@ -1,0 +1,368 @@
+"""Throughput benchmark of the batched policy/value evaluation
+(InferenceEngine::predict_batch, include/inference_engine.h:25-32) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload b19c128x10_bs512|b19c256x20_bs1024|b9c128x10_bs256|b9c64x6_bs16]
+
+A step is one forward pass of the network over one batch of seeded random-
+playout positions.  Under torchrun each rank drives its own GPU with its own
+batch (weights replicated, no collective on the data path); rank 0 prints one
+JSON line.  Numbers:
+  value      positions/s over all ranks, inputs resident in HBM, L2 flushed
+             (256 MB write) before every timed step, CUDA-event timed on the
+             engine's stream, max over ranks;
+  e2e        the same through the host API (mg_forward with pinned host
+             inputs): H2D of the inputs, forward, D2H of policy and value,
+             wall-clock timed, max over ranks;
+  roofline   the 3x3 convolution kernel (the dominant kernel) timed alone with
+             CUDA events: algorithmic FLOPs per launch / average launch time,
+             against the measured dense bf16 peak;
+  cpu_baseline  the oracle (C restatement of src/eigen_engine.cpp) on the
+             host cores over a bounded sample (rank 0, N = 1 only).
+--impl reference times that CPU implementation alone as the reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (board, filters, blocks, batch per GPU, max random moves)
+    "b19c128x10_bs512": (19, 128, 10, 512, 250),
+    "b19c256x20_bs1024": (19, 256, 20, 1024, 250),
+    "b9c128x10_bs256": (9, 128, 10, 256, 60),
+    "b9c64x6_bs16": (9, 64, 6, 16, 60),
+}
+DEFAULT_WORKLOAD = "b19c128x10_bs512"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def flops_per_position(board, filters, blocks, inputs=17, hidden=64):
+    """Algorithmic FLOPs of one forward pass (2 per multiply-add)."""
+    hw = board * board
+    a = hw + 1
+    c = filters
+    trunk = 2 * hw * (9 * inputs * c + blocks * 2 * 9 * c * c)
+    heads = 2 * hw * 3 * c + 2 * 2 * hw * a + 2 * hw * hidden + 2 * hidden
+    return trunk + heads
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"]))}, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS, bf16_tflops_sustained=FALLBACK_PEAKS["bf16_tflops"]), "fallback"
+
+
+def profiled_traffic(workload):
+    """DRAM bytes per conv launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", f"conv3x3_tc_{workload}.md")
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = str(gpu_index)
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", self.gpu], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, nm in enumerate(names):
+                if len(r) > 5 + i and r[5 + i].lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(self.rows)}
+
+
+def cpu_baseline(sd, x, target_s=12.0):
+    """The oracle on all host cores over a bounded sample of the workload
+    (about target_s seconds of wall time)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    threads = os.cpu_count() or 1
+    orc = oracle.EigenOracle(sd)
+    t0 = time.perf_counter()
+    orc.predict_batch(x[:1], oracle.CANONICAL, threads=1)
+    per_pos = time.perf_counter() - t0
+    sample = int(target_s / max(per_pos, 1e-9)) * threads
+    sample = max(min(threads, len(x)), min(sample, len(x)))
+    t0 = time.perf_counter()
+    orc.predict_batch(x[:sample], oracle.CANONICAL, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt, "unit": "positions/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} positions of the same workload; oracle C restatement of "
+                      f"src/eigen_engine.cpp on {threads} threads ({dt:.1f} s)"}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_reference(args, wl):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    board, filters, blocks, batch, max_moves = WORKLOADS[wl]
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from alphazero_b200 import host_lib, weights
+
+    sd = weights.make_state_dict(board, filters, blocks, seed=0, variant="init")
+    x = host_lib.random_positions(board, batch, 1000, max_moves)
+    threads = os.cpu_count() or 1
+    orc = oracle.EigenOracle(sd)
+    t0 = time.perf_counter()
+    orc.predict_batch(x[:1], oracle.CANONICAL, threads=1)
+    per_pos = time.perf_counter() - t0
+    # each step: a bounded sample (about 0.5 s of work on all threads)
+    sample = max(1, min(batch, int(0.5 * threads / max(per_pos, 1e-9))))
+    for _ in range(args.warmup):
+        orc.predict_batch(x[:sample], oracle.CANONICAL, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.predict_batch(x[:sample], oracle.CANONICAL, threads=threads)
+    dt = time.perf_counter() - t0
+    v = sample * args.steps / dt
+    line = {
+        "impl": "reference", "metric": metric_name(wl), "value": v, "unit": "positions/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(wl),
+        "cpu_baseline": {"value": v, "unit": "positions/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} positions per step of the same workload; oracle C "
+                                   "restatement of src/eigen_engine.cpp (Eigen3 is absent, so the "
+                                   "reference engine itself does not compile)"},
+        "e2e": {"value": v, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def metric_name(wl):
+    board, filters, blocks, batch, _ = WORKLOADS[wl]
+    return f"positions/sec ({board}x{board} b{blocks}c{filters}, batch {batch} per GPU)"
+
+
+def workload_config(wl):
+    board, filters, blocks, batch, max_moves = WORKLOADS[wl]
+    return {"workload": f"predict_batch {board}x{board} b{blocks}c{filters} batch {batch} per GPU",
+            "board": board, "filters": filters, "blocks": blocks, "batch_per_gpu": batch,
+            "positions": f"seeded random playouts of 0-{max_moves} legal moves",
+            "weights": "seeded random init (export_onnx --init distributions)",
+            "l2": "flushed by a 256 MB write before each timed step",
+            "parallelism": "replicas; positions sharded per GPU, no collective"}
+
+
+def run_b200(args, wl):
+    import torch
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    board, filters, blocks, batch, max_moves = WORKLOADS[wl]
+    hw = board * board
+    actions = hw + 1
+    from alphazero_b200 import host_lib, weights
+    from alphazero_b200.engine import CudaEngine
+
+    sd = weights.make_state_dict(board, filters, blocks, seed=0, variant="init")
+    tmp = tempfile.mkdtemp(prefix="mgb_bench_")
+    model = weights.write_onnx(os.path.join(tmp, "model.onnx"), sd)
+    eng = CudaEngine(local, precision="bf16", max_batch=batch)
+    eng.load_model(model)
+    x = host_lib.random_positions(board, batch, 1000 + rank, max_moves)
+
+    stream = torch.cuda.ExternalStream(eng.stream_handle())
+    d_x = torch.from_numpy(x).cuda()
+    d_p = torch.empty((batch, actions), device="cuda")
+    d_v = torch.empty((batch,), device="cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if pg is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- value: device-resident inputs, L2 flushed before each step ----
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            flush.zero_()
+            eng.forward_device(d_x.data_ptr(), batch, d_p.data_ptr(), d_v.data_ptr(), None)
+    eng.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                flush.zero_()
+                starts[i].record(stream)
+                eng.forward_device(d_x.data_ptr(), batch, d_p.data_ptr(), d_v.data_ptr(), None)
+                ends[i].record(stream)
+        eng.synchronize()
+    barrier()
+    dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    dev_ms = max_over_ranks(dev_ms)
+    value = world * batch * args.steps / (dev_ms / 1e3)
+    launches = eng.launches_per_forward(batch) * args.steps
+
+    # ---- e2e: host API, pinned inputs, H2D + forward + D2H per step ----
+    pinned = torch.from_numpy(x).pin_memory()
+    xin = pinned.numpy()
+    for _ in range(args.warmup):
+        eng.forward(xin, want_logits=False)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.forward(xin, want_logits=False)
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    e2e_s = max_over_ranks(e2e_s)
+    e2e = world * batch * args.steps / e2e_s
+
+    # ---- roofline: the 3x3 conv kernel alone (conv1 of block 0) ----
+    reps = 50
+    eng.forward_device(d_x.data_ptr(), batch, d_p.data_ptr(), d_v.data_ptr(), None)
+    eng.launch_conv(batch, 0, 5)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    eng.launch_conv(batch, 0, reps)
+    c1.record(stream)
+    eng.synchronize()
+    conv_ms = c0.elapsed_time(c1) / reps
+    conv_flops = 2.0 * batch * hw * 9 * filters * filters
+    peaks, peak_src = load_peaks()
+    achieved = conv_flops / (conv_ms / 1e3) / 1e12
+    traffic = profiled_traffic(wl)
+
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base = cpu_baseline(sd, x)
+
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": metric_name(wl), "value": value, "unit": "positions/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": workload_config(wl),
+        "e2e": {"value": e2e, "unit": "positions/s",
+                "h2d_bytes_per_step": batch * 17 * hw * 4,
+                "d2h_bytes_per_step": batch * (actions + 1) * 4},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                     "traffic": traffic, "kernel": "conv3x3_tc_kernel (residual-block conv)",
+                     "flops_per_launch": conv_flops, "launch_ms": conv_ms,
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
+        "tflops_whole_forward": value * flops_per_position(board, filters, blocks) / 1e12,
+        "clocks": clocks.summary(),
+    }
+    if base is not None:
+        line["cpu_baseline"] = base
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
+    if args.impl == "reference":
+        run_reference(args, args.workload)
+    else:
+        run_b200(args, args.workload)
+
+
+if __name__ == "__main__":
+    main()
