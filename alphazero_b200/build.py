@@ -28,6 +28,7 @@ GENCODE = "-gencode=arch=compute_100a,code=sm_100a"
 
 CUDA_SOURCES = [
     os.path.join(CSRC, "conv_tc.cu"),
+    os.path.join(CSRC, "conv_pix.cu"),
     os.path.join(CSRC, "conv_simt.cu"),
     os.path.join(CSRC, "stage_heads.cu"),
     os.path.join(CSRC, "engine.cu"),

@@ -1,0 +1,494 @@
+// 3x3 convolution with 128 output channels as an implicit GEMM on the
+// sm_100a tensor cores, pixels on the MMA's N side.
+//
+//   D[co][px] = sum_{cb, tap, k} W[co][tap][cb*64 + k] * X[px + off(tap)][cb*64 + k]
+//
+// A = weights (M = 128 output channels), B = pixels (N = up to 256 framed
+// pixels per tile), K = 9 taps x input channels.  Per 64-channel block the
+// producer loads ONE activation slab of N + 2*(RS+1) rows (the tile's rows
+// plus a halo of one frame row and one pixel on each side) and every one of
+// the 9 taps reads it through a descriptor whose start row is shifted by
+// dy*RS + dx, so activations cross L2 -> SMEM once per block instead of
+// nine times.  (The MMA derives the 128-byte swizzle phase from the absolute
+// shared-memory address, as TMA does when it writes the slab, so a start
+// address moved by whole 128-byte rows needs no descriptor base offset.)
+// Weight K blocks (128 x 64) stream through a 6-deep ring.
+//
+// The accumulator is [co lanes][px columns] in TMEM, double-buffered across
+// tiles (2 x 256 columns).  The epilogue moves activations only through
+// TMA: per 16-pixel chunk the fp32 residual rows arrive by a TMA load into
+// shared memory (issued one chunk ahead), each thread (= one channel) adds
+// bias and residual and applies ReLU and the frame mask, and the results are
+// staged in shared memory and leave as TMA bulk stores (fp32 and/or 16-bit).
+// In the last trunk layer the staged chunk instead feeds the policy / value
+// 1x1 head projection.
+//
+// Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
+// issuer, warps 2-9 epilogue in two groups of four (group g takes chunks
+// g, g+2, ...; warp w of a group reads TMEM lanes [32*(w%4), +32)).  All
+// waits are bounded.
+#include "kernels.cuh"
+#include "ptx_sm100.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+namespace mgb {
+namespace {
+
+constexpr int kCo = 128;        // output channels (MMA M)
+constexpr int kBK = 64;         // K per stage / slab channel block
+constexpr int kMaxPx = 256;     // MMA N limit
+constexpr int kStages = 6;      // weight ring depth
+constexpr int kThreads = 320;
+constexpr int kChunk = 16;      // pixels per epilogue chunk
+constexpr uint32_t kWBytes = kCo * kBK * 2;            // 16 KB weight stage
+constexpr uint32_t kStage32 = kChunk * kCo * 4;        // 8 KB fp32 chunk
+constexpr uint32_t kStage16 = kChunk * kCo * 2;        // 4 KB 16-bit chunk
+
+struct PixArgs {
+    int m_total;
+    int num_tiles;
+    int npx;        // pixels per tile (multiple of 16, <= 256)
+    int cin;
+    int rs, is, board;
+    int slab_rows;  // rows per slab (multiple of 16)
+    int has_res, has_out32, has_out16;
+    const float* bias;
+    const float* head_w;  // [3][128] or nullptr (fused head projection)
+    const float* head_b;
+    float* feat;
+    int* err;
+};
+
+template <bool FP16>
+__device__ __forceinline__ uint16_t to16(float v);
+template <>
+__device__ __forceinline__ uint16_t to16<false>(float v) {
+    __nv_bfloat16 h = __float2bfloat16_rn(v);
+    return *reinterpret_cast<uint16_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint16_t to16<true>(float v) {
+    __half h = __float2half_rn(v);
+    return *reinterpret_cast<uint16_t*>(&h);
+}
+
+template <bool FP16>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv3x3_pix_kernel(const __grid_constant__ CUtensorMap tmW,
+                       const __grid_constant__ CUtensorMap tmX,
+                       const __grid_constant__ CUtensorMap tmR,
+                       const __grid_constant__ CUtensorMap tmO32,
+                       const __grid_constant__ CUtensorMap tmO16, const PixArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t slab_bytes = (uint32_t)a.slab_rows * 128u;
+    uint8_t* wring = smem;                                   // kStages x 16 KB
+    uint8_t* slab0 = wring + kStages * kWBytes;              // 2 slabs
+    float* st32 = reinterpret_cast<float*>(slab0 + 2 * slab_bytes);        // [2 groups][16][128]
+    uint16_t* st16 = reinterpret_cast<uint16_t*>(st32 + 2 * kChunk * kCo);  // [2][16][128]
+    float* stres = reinterpret_cast<float*>(st16 + 2 * kChunk * kCo);      // [2][16][128]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stres + 2 * kChunk * kCo);
+    uint64_t* wfull = bars;
+    uint64_t* wempty = bars + kStages;
+    uint64_t* sfull = bars + 2 * kStages;
+    uint64_t* sempty = sfull + 2;
+    uint64_t* tfull = sempty + 2;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* rfull = tempty + 2;
+    uint64_t* done = rfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    float* sbias = reinterpret_cast<float*>(tmem_slot + 4);  // [128]
+    float* shead = sbias + kCo;                              // [3][128]
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&wfull[s]), 1);
+            mbar_init(smem_u32(&wempty[s]), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&sfull[i]), 1);
+            mbar_init(smem_u32(&sempty[i]), 1);
+            mbar_init(smem_u32(&tfull[i]), 1);
+            mbar_init(smem_u32(&tempty[i]), 8);
+            mbar_init(smem_u32(&rfull[i]), 1);
+        }
+        mbar_init(smem_u32(done), 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), 512);
+        tmem_relinquish();
+    }
+    for (int i = threadIdx.x; i < kCo; i += kThreads) sbias[i] = a.bias[i];
+    if (a.head_w != nullptr)
+        for (int i = threadIdx.x; i < 3 * kCo; i += kThreads) shead[i] = a.head_w[i];
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int cblocks = a.cin / kBK;
+    const int halo = a.rs + 1;
+    const int half_rows = a.slab_rows / 2;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            prefetch_tensormap(&tmW);
+            prefetch_tensormap(&tmX);
+            int iw = 0, is = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
+                const int m0 = tile * a.npx;
+                for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
+                    const int sb = is & 1;
+                    if (!mbar_wait(smem_u32(&sempty[sb]), ((is >> 1) & 1) ^ 1, a.err,
+                                   kErrWaitProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sfb = smem_u32(&sfull[sb]);
+                    uint8_t* slab = slab0 + sb * slab_bytes;
+                    mbar_arrive_expect_tx(sfb, slab_bytes);
+                    tma_load_2d(smem_u32(slab), &tmX, sfb, cb * kBK, m0 - halo);
+                    tma_load_2d(smem_u32(slab + half_rows * 128), &tmX, sfb, cb * kBK,
+                                m0 - halo + half_rows);
+                    for (int tap = 0; tap < 9; ++tap, ++iw) {
+                        const int s = iw % kStages;
+                        if (!mbar_wait(smem_u32(&wempty[s]), ((iw / kStages) & 1) ^ 1, a.err,
+                                       kErrWaitProducer)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t wfb = smem_u32(&wfull[s]);
+                        mbar_arrive_expect_tx(wfb, kWBytes);
+                        tma_load_2d(smem_u32(wring + s * kWBytes), &tmW, wfb, tap * a.cin + cb * kBK,
+                                    0);
+                    }
+                }
+            }
+            // Drain every copy still in flight before the CTA exits.
+            for (int j = (iw > kStages ? iw - kStages : 0); j < iw; ++j)
+                mbar_wait(smem_u32(&wfull[j % kStages]), (j / kStages) & 1, a.err, kErrWaitDrain);
+            for (int j = (is > 2 ? is - 2 : 0); j < is; ++j)
+                mbar_wait(smem_u32(&sfull[j & 1]), (j >> 1) & 1, a.err, kErrWaitDrain);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(kCo, a.npx, !FP16);
+            int iw = 0, is = 0, t = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++t) {
+                const int acc = t & 1;
+                if (!mbar_wait(smem_u32(&tempty[acc]), ((t >> 1) & 1) ^ 1, a.err, kErrWaitMma)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * kMaxPx);
+                for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
+                    const int sb = is & 1;
+                    if (!mbar_wait(smem_u32(&sfull[sb]), (is >> 1) & 1, a.err, kErrWaitMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t slab = smem_u32(slab0 + sb * slab_bytes);
+                    for (int tap = 0; tap < 9; ++tap, ++iw) {
+                        const int s = iw % kStages;
+                        if (!mbar_wait(smem_u32(&wfull[s]), (iw / kStages) & 1, a.err, kErrWaitMma)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const int r0 = halo + (tap / 3 - 1) * a.rs + (tap % 3 - 1);
+                        const uint64_t ad = smem_desc_sw128(smem_u32(wring + s * kWBytes));
+#pragma unroll
+                        for (int k = 0; k < kBK / 16; ++k) {
+                            // row-shifted start, base offset 0 (see file comment)
+                            const uint64_t bd = smem_desc_sw128(slab + (uint32_t)r0 * 128u + 32u * k);
+                            mma_f16(d, ad + (uint64_t)(2 * k), bd, idesc, (cb | tap | k) != 0);
+                        }
+                        mma_commit(smem_u32(&wempty[s]));
+                    }
+                    if (ok) mma_commit(smem_u32(&sempty[sb]));
+                }
+                if (ok) mma_commit(smem_u32(&tfull[acc]));
+            }
+            mma_commit(smem_u32(done));
+            mbar_wait(smem_u32(done), 0, a.err, kErrWaitDrain);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue (warps 2..9, two groups) ----------------
+        const int quarter = warp & 3;                   // channels [32*quarter, +32)
+        const int grp = (warp - 2) >> 2;                // chunks grp, grp+2, ...
+        const int gtid = ((warp - 2) & 3) * 32 + lane;  // 0..127 within the group
+        const bool leader = gtid == 0;
+        const int bar_a = 2 + 2 * grp, bar_b = 3 + 2 * grp;
+        const int co = quarter * 32 + lane;
+        const float bias = sbias[co];
+        const int hw = a.board * a.board;
+        const int nchunks = a.npx / kChunk;
+        float* s32 = st32 + grp * (kChunk * kCo);
+        uint16_t* s16 = st16 + grp * (kChunk * kCo);
+        float* sres = stres + grp * (kChunk * kCo);
+        const uint32_t rbar = smem_u32(&rfull[grp]);
+        const bool store_out = (a.has_out32 | a.has_out16) != 0;
+        int rissued = 0;  // residual loads issued (leader)
+        if (a.has_res && leader && blockIdx.x < a.num_tiles && grp < nchunks) {
+            // residual of this group's first chunk of its first tile
+            mbar_arrive_expect_tx(rbar, kStage32);
+            tma_load_2d(smem_u32(sres), &tmR, rbar, 0, blockIdx.x * a.npx + grp * kChunk);
+            ++rissued;
+        }
+        int rseq = 0;  // residual loads consumed
+        int t = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++t) {
+            const int acc = t & 1;
+            const int m0 = tile * a.npx;
+            ok = mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, a.err, kErrWaitEpilogue);
+            if (bar_any(bar_a, 128, !ok)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tcol =
+                tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kMaxPx);
+#pragma unroll 1
+            for (int c = grp; c < nchunks; c += 2) {
+                const int px0 = m0 + c * kChunk;
+                uint32_t v[16];
+                tmem_ld_16cols(tcol + (uint32_t)(c * kChunk), v);
+                // lanes 0..15 classify pixels px0 + lane
+                const int mj = px0 + (lane & 15);
+                bool onb = false;
+                if (mj < a.m_total) {
+                    const int q = mj % a.is;
+                    const int y = q / a.rs;
+                    onb = (y < a.board) && (q - y * a.rs < a.board);
+                }
+                const uint32_t board_mask = __ballot_sync(0xffffffffu, onb) & 0xffffu;
+                float f[16];
+                tmem_ld_wait();
+                if (a.has_res) {
+                    const bool rok = mbar_wait(rbar, rseq & 1, a.err, kErrWaitEpilogue);
+                    ++rseq;
+                    if (bar_any(bar_b, 128, !rok)) {
+                        ok = false;
+                        break;
+                    }
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j) f[j] = sres[j * kCo + co];
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j) f[j] = 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    const float x = __uint_as_float(v[j]) + bias + f[j];
+                    f[j] = ((board_mask >> j) & 1) ? fmaxf(x, 0.f) : 0.f;
+                }
+                // The staging buffers and the residual buffer are free once the
+                // previous bulk store has read them and every thread of the
+                // group has read its residual.
+                if (leader && store_out) bulk_wait_read();
+                named_barrier_sync(bar_a, 128);
+                if (a.has_res && leader) {
+                    // Residual of this group's next chunk (this tile or the next).
+                    int nt = tile, nc = c + 2;
+                    if (nc >= nchunks) {
+                        nt = tile + gridDim.x;
+                        nc = grp;
+                    }
+                    if (nt < a.num_tiles) {
+                        mbar_arrive_expect_tx(rbar, kStage32);
+                        tma_load_2d(smem_u32(sres), &tmR, rbar, 0, nt * a.npx + nc * kChunk);
+                        ++rissued;
+                    }
+                }
+                if (a.has_out32 || a.head_w != nullptr) {
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j) s32[j * kCo + co] = f[j];
+                }
+                if (a.has_out16) {
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j) s16[j * kCo + co] = to16<FP16>(f[j]);
+                }
+                if (store_out) fence_proxy_async_smem();
+                named_barrier_sync(bar_b, 128);
+                if (store_out) {
+                    if (leader && px0 < a.m_total) {  // rows past the end are clipped
+                        if (a.has_out32) tma_store_2d(&tmO32, smem_u32(s32), 0, px0);
+                        if (a.has_out16) tma_store_2d(&tmO16, smem_u32(s16), 0, px0);
+                        bulk_commit();
+                    }
+                } else if (a.head_w != nullptr) {
+                    // Policy / value 1x1 convs of the 16 staged pixels: thread
+                    // (pixel gtid/8, channel segment gtid%8) sums 16 channels,
+                    // then the 8 segments of a pixel combine by shuffles.
+                    const int p = gtid >> 3, seg = gtid & 7;
+                    const float* row = s32 + p * kCo + seg * 16;
+                    const float* hw0 = shead + seg * 16;
+                    float d0 = 0.f, d1 = 0.f, d2 = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int k = (i + 2 * seg) & 15;  // rotate to spread banks
+                        const float xv = row[k];
+                        d0 = fmaf(xv, hw0[k], d0);
+                        d1 = fmaf(xv, hw0[kCo + k], d1);
+                        d2 = fmaf(xv, hw0[2 * kCo + k], d2);
+                    }
+#pragma unroll
+                    for (int o = 1; o < 8; o <<= 1) {
+                        d0 += __shfl_xor_sync(0xffffffffu, d0, o);
+                        d1 += __shfl_xor_sync(0xffffffffu, d1, o);
+                        d2 += __shfl_xor_sync(0xffffffffu, d2, o);
+                    }
+                    if (seg == 0 && ((board_mask >> p) & 1)) {
+                        const int m = px0 + p;
+                        const int pos = m / a.is;
+                        const int q = m - pos * a.is;
+                        const int y = q / a.rs, x = q - y * a.rs;
+                        float* fr = a.feat + (size_t)pos * 3 * hw + y * a.board + x;
+                        fr[0] = fmaxf(d0 + a.head_b[0], 0.f);
+                        fr[hw] = fmaxf(d1 + a.head_b[1], 0.f);
+                        fr[2 * hw] = fmaxf(d2 + a.head_b[2], 0.f);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+        }
+        if (leader) {
+            // Every bulk store complete and every issued residual load landed
+            // before the CTA's shared memory is released.
+            if (store_out) bulk_wait_all();
+            for (int j = rseq; j < rissued; ++j) mbar_wait(rbar, j & 1, a.err, kErrWaitDrain);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+int slab_rows_for(int npx, int rs) {
+    const int need = npx + 2 * (rs + 1);
+    return (need + 15) / 16 * 16;
+}
+
+size_t pix_smem_bytes(int npx, int rs) {
+    const size_t slab = (size_t)slab_rows_for(npx, rs) * 128;
+    return (size_t)kStages * kWBytes + 2 * slab + 2 * (kStage32 + kStage16 + kStage32) +
+           (2 * kStages + 11) * 8 + 16 + (kCo + 3 * kCo) * 4 + 1024;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D tensor map [rows][inner] of `esize`-byte elements.
+bool encode(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, uint64_t inner,
+            uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
+    auto enc = encoder();
+    if (enc == nullptr) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * (uint64_t)esize};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t configure_conv_pix() {
+    const int smem = 227 * 1024;
+    cudaError_t e = cudaFuncSetAttribute(conv3x3_pix_kernel<false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(conv3x3_pix_kernel<true>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
+bool conv_pix_supported(const ConvLayer& L, int npx) {
+    return L.cout == kCo && L.cin % kBK == 0 && npx % kChunk == 0 && npx >= 32 &&
+           npx <= kMaxPx && pix_smem_bytes(npx, L.g.rs) <= 227 * 1024;
+}
+
+cudaError_t launch_conv_pix(const ConvLayer& L, int npx, bool fp16, int grid_limit,
+                            cudaStream_t stream) {
+    if (!conv_pix_supported(L, npx)) return cudaErrorInvalidValue;
+    PixArgs a;
+    a.m_total = L.m_total;
+    a.npx = npx;
+    a.num_tiles = (L.m_total + npx - 1) / npx;
+    a.cin = L.cin;
+    a.rs = L.g.rs;
+    a.is = L.g.is;
+    a.board = L.g.board;
+    a.slab_rows = slab_rows_for(npx, L.g.rs);
+    a.has_res = L.res32 != nullptr;
+    a.has_out32 = L.out32 != nullptr;
+    a.has_out16 = L.out16 != nullptr;
+    a.bias = L.bias;
+    a.head_w = L.head_w;
+    a.head_b = L.head_b;
+    a.feat = L.feat;
+    a.err = L.err;
+    const CUtensorMapDataType t16 =
+        fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap tmW, tmX, tmR, tmO32, tmO16;
+    // Epilogue maps of absent buffers describe a valid dummy (the first 16
+    // rows' worth of the weight buffer, at least 147 KB) and are never used.
+    const void* r = L.res32 ? (const void*)L.res32 : L.weight;
+    const void* o32 = L.out32 ? (const void*)L.out32 : L.weight;
+    const void* o16 = L.out16 ? (const void*)L.out16 : L.weight;
+    const uint64_t rows = (uint64_t)L.m_total;
+    if (!encode(&tmW, t16, 2, L.weight, (uint64_t)9 * L.cin, (uint64_t)kCo, kBK, kCo,
+                CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode(&tmX, t16, 2, L.in, (uint64_t)L.cin, rows, kBK, (uint32_t)(a.slab_rows / 2),
+                CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode(&tmR, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, r, kCo, L.res32 ? rows : kChunk, kCo,
+                kChunk, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(&tmO32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, o32, kCo, L.out32 ? rows : kChunk, kCo,
+                kChunk, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(&tmO16, t16, 2, o16, kCo, L.out16 ? rows : kChunk, kCo, kChunk,
+                CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    int grid = a.num_tiles < grid_limit ? a.num_tiles : grid_limit;
+    if (grid < 1) grid = 1;
+    const size_t smem = pix_smem_bytes(npx, L.g.rs);
+    if (fp16)
+        conv3x3_pix_kernel<true><<<grid, kThreads, smem, stream>>>(tmW, tmX, tmR, tmO32, tmO16, a);
+    else
+        conv3x3_pix_kernel<false><<<grid, kThreads, smem, stream>>>(tmW, tmX, tmR, tmO32, tmO16, a);
+    return cudaGetLastError();
+}
+
+}  // namespace mgb

@@ -78,6 +78,8 @@ struct mg_engine {
     int max_batch = 1024;
     int num_sms = 148;
     int conv_bn_override = 0;
+    int pix_mode = 1;      // 1: pixels-on-N kernel for 128-channel layers
+    int pix_npx = 0;       // pixels per tile override (0 = heuristic)
     bool use_graphs = true;
     cudaStream_t stream = nullptr;
     std::string err;
@@ -378,10 +380,32 @@ struct mg_engine {
 
     // ---- kernels ---------------------------------------------------------
 
+    // 128-channel layers run the pixels-on-N kernel (conv_pix.cu).
+    bool use_pix() const { return precision != MG_PREC_FP32 && cpad == 128 && pix_mode != 0; }
+
+    // Pixels per tile: the largest tile whose last wave is not much emptier
+    // than a smaller tile's (critical path ~ waves x (npx + weight reload)).
+    int choose_npx(int m_total) const {
+        if (pix_npx > 0) return pix_npx;
+        int best = 256;
+        long best_cost = -1;
+        for (int npx = 256; npx >= 128; npx -= 16) {
+            const long tiles = (m_total + npx - 1) / npx;
+            const long waves = (tiles + num_sms - 1) / num_sms;
+            const long cost = waves * (npx + 64);
+            if (best_cost < 0 || cost < best_cost) {
+                best_cost = cost;
+                best = npx;
+            }
+        }
+        return best;
+    }
+
     // Whether the last trunk layer computes the head projection in its
     // epilogue (tensor-core path with one tile spanning all channels).
     bool fused_heads(int bucket) const {
-        return precision != MG_PREC_FP32 && choose_bn(bucket * g.is) == cpad;
+        if (precision == MG_PREC_FP32) return false;
+        return use_pix() || choose_bn(bucket * g.is) == cpad;
     }
 
     ConvLayer layer_desc(int li, int bucket) const {
@@ -426,6 +450,11 @@ struct mg_engine {
             return;
         }
         const bool fp16 = precision == MG_PREC_FP16;
+        if (use_pix()) {
+            ck(launch_conv_pix(L, choose_npx(L.m_total), fp16, num_sms, stream),
+               "conv3x3_pix launch");
+            return;
+        }
         const int bn = choose_bn(L.m_total);
         CUtensorMap ta, tb;
         const char* why = "";
@@ -558,12 +587,14 @@ mg_engine* mg_create(int device, int flags) {
     }
     e->num_sms = prop.multiProcessorCount;
     if ((ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking)) != cudaSuccess ||
-        (ce = configure_conv_tc()) != cudaSuccess) {
+        (ce = configure_conv_tc()) != cudaSuccess || (ce = configure_conv_pix()) != cudaSuccess) {
         g_create_error = std::string("CUDA setup failed: ") + cudaGetErrorString(ce);
         return nullptr;
     }
     if (const char* s = std::getenv("MG_CONV_BN")) e->conv_bn_override = std::atoi(s);
     if (const char* s = std::getenv("MG_NO_GRAPHS")) e->use_graphs = std::atoi(s) == 0;
+    if (const char* s = std::getenv("MG_PIX")) e->pix_mode = std::atoi(s);
+    if (const char* s = std::getenv("MG_PIX_NPX")) e->pix_npx = std::atoi(s);
     return e.release();
 }
 

@@ -82,6 +82,14 @@ int conv_tc_smem_bytes(int bn);
 // launching or capturing).
 cudaError_t configure_conv_tc();
 
+// Tensor-core path for 128 output channels with pixels on the MMA N side
+// (conv_pix.cu): npx pixels per tile (multiple of 16, 32..256), one halo
+// slab per 64-channel block shared by the 9 taps.
+bool conv_pix_supported(const ConvLayer& layer, int npx);
+cudaError_t launch_conv_pix(const ConvLayer& layer, int npx, bool fp16, int grid_limit,
+                            cudaStream_t stream);
+cudaError_t configure_conv_pix();
+
 // fp32 SIMT path used by the fp32 verification mode.
 cudaError_t launch_conv_simt(const ConvLayer& layer, cudaStream_t stream);
 
