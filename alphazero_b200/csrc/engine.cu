@@ -25,6 +25,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -797,3 +798,192 @@ int mg_launches_per_forward(mg_engine* e, int n) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Forward pass that allocates nothing.
+//
+// mg_forward_device allocates its activation buffers on an engine's first
+// forward (and again after mg_set_max_batch).  Some callers cannot let a
+// library call cudaMalloc once they are running: cudaMalloc and especially
+// cudaFree synchronise the whole device, stalling every other stream the
+// process has in flight, and a host program that reserves all of its GPU
+// memory up front (or runs under a fixed memory budget) must not see an
+// allocation fail in the middle of a search.  For them this variant takes
+// every intermediate buffer - staged input, fp32 residual stream, 16-bit
+// operands, head features, FC outputs and the status word - from one
+// file-scope __device__ arena of kNoAllocArenaBytes, which each GPU that
+// loads this library holds until the process exits.
+//
+// The arena's device address is looked up once per device with
+// cudaGetSymbolAddress on the first call made on that device (so make that
+// first call before any stream capture); in host code the array's name is
+// only a host-side stand-in and must never be handed to a kernel.  All calls
+// on a device share the one arena, which keeps whatever the previous call
+// left there: every buffer is fully rewritten by each call except the
+// status word, which is cleared first.  Calls whose work overlaps on the GPU
+// (two engines on the same device, or two streams) race on the arena and
+// must be serialised by the caller.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocArenaBytes = size_t(32) << 20;  // 32 MiB per device
+__device__ __align__(256) unsigned char g_noalloc_arena[kNoAllocArenaBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of the arena for `dev` (which must be current).
+cudaError_t noalloc_arena(int dev, void** out) {
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_arena);
+        if (e != cudaSuccess) return e;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return cudaSuccess;
+}
+
+// Carves the per-call buffers for n positions out of the arena; returns the
+// bytes needed (which may exceed the arena, in which case nothing is set).
+struct NoAllocBuffers {
+    void* stage;
+    float* x32;
+    void* x16;
+    void* t;
+    float* feat;
+    float* fc;
+    float* logits;
+    int* err;
+};
+
+size_t noalloc_layout(const mg_engine* e, int n, unsigned char* base, NoAllocBuffers* b) {
+    const size_t rows = (size_t)n * e->g.is;
+    const size_t elem = e->elem_bytes();
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off += (bytes + 255) / 256 * 256;
+        return at;
+    };
+    const size_t o_stage = take(rows * kStagedChannels * elem);
+    const size_t o_x32 = take(rows * e->cpad * 4);
+    const size_t o_x16 = take(rows * e->cpad * 2);
+    const size_t o_t = take(rows * e->cpad * elem);
+    const size_t o_feat = take((size_t)n * 3 * e->hw * 4);
+    const size_t o_fc = take((size_t)n * (e->actions + e->net.hidden) * 4);
+    const size_t o_log = take((size_t)n * e->actions * 4);
+    const size_t o_err = take(sizeof(int));
+    if (base != nullptr && off <= kNoAllocArenaBytes) {
+        b->stage = base + o_stage;
+        b->x32 = reinterpret_cast<float*>(base + o_x32);
+        b->x16 = base + o_x16;
+        b->t = base + o_t;
+        b->feat = reinterpret_cast<float*>(base + o_feat);
+        b->fc = reinterpret_cast<float*>(base + o_fc);
+        b->logits = reinterpret_cast<float*>(base + o_log);
+        b->err = reinterpret_cast<int*>(base + o_err);
+    }
+    return off;
+}
+
+}  // namespace
+
+extern "C" int mg_forward_device_noalloc(mg_engine* e, const float* d_states, int n,
+                                         float* d_policy, float* d_value, float* d_logits) {
+    if (e == nullptr) return MG_E_ARG;
+    if (n < 0) return fail(e, MG_E_ARG, "negative batch size");
+    if (n == 0) return MG_OK;
+    if (d_states == nullptr || d_policy == nullptr || d_value == nullptr)
+        return fail(e, MG_E_ARG, "null buffer");
+    int dev_err = 0;
+    int rc = guarded(e, [&] {
+        e->check_ready();
+        const bool f32 = e->precision == MG_PREC_FP32;
+        if (f32 ? e->d_w32.size() != (size_t)e->n_convs : e->w16_prec != e->precision)
+            throw std::logic_error("weights for the current precision are not on the device");
+        // Largest batch that fits the arena, for the error message.
+        int cap = 0;
+        while (noalloc_layout(e, cap + 1, nullptr, nullptr) <= kNoAllocArenaBytes) ++cap;
+        if (n > cap)
+            throw std::invalid_argument("batch of " + std::to_string(n) +
+                                        " positions exceeds the no-allocation scratch arena (" +
+                                        std::to_string(kNoAllocArenaBytes >> 20) +
+                                        " MiB): at most " + std::to_string(cap) +
+                                        " positions for this network");
+        void* arena = nullptr;
+        ck(noalloc_arena(e->device, &arena), "cudaGetSymbolAddress(no-allocation arena)");
+        NoAllocBuffers b{};
+        noalloc_layout(e, n, reinterpret_cast<unsigned char*>(arena), &b);
+        cudaStream_t st = e->stream;
+        ck(cudaMemsetAsync(b.err, 0, sizeof(int), st), "cudaMemsetAsync(status)");
+        ck(launch_stage_input(d_states, n, n, e->planes, e->g, kStagedChannels,
+                              (e->flags & MG_FLAG_EIGEN_COMPAT) != 0, e->act_type(), b.stage, st),
+           "stage launch");
+        const bool fused = e->fused_heads(n);
+        for (int li = 0; li < e->n_convs; ++li) {
+            // The same wiring as the engine's own forward, on arena buffers.
+            ConvLayer L{};
+            L.m_total = n * e->g.is;
+            L.cin = e->wcin[li];
+            L.cout = e->cpad;
+            L.g = e->g;
+            L.bias = e->d_bias[li];
+            L.err = b.err;
+            L.weight = f32 ? (const void*)e->d_w32[li] : (const void*)e->d_w16[li];
+            if (li == 0) {
+                L.in = b.stage;
+                L.out32 = b.x32;
+                L.out16 = f32 ? nullptr : b.x16;
+            } else if (li % 2 == 1) {
+                L.in = f32 ? (const void*)b.x32 : (const void*)b.x16;
+                if (f32) L.out32 = reinterpret_cast<float*>(b.t);
+                else L.out16 = b.t;
+            } else {
+                L.in = b.t;
+                L.res32 = b.x32;
+                L.out32 = b.x32;
+                L.out16 = f32 ? nullptr : b.x16;
+            }
+            if (li == e->n_convs - 1 && fused) {
+                L.out32 = nullptr;
+                L.out16 = nullptr;
+                L.head_w = e->d_head_w;
+                L.head_b = e->d_head_b;
+                L.feat = b.feat;
+            }
+            if (f32) {
+                ck(launch_conv_simt(L, st), "conv3x3_simt launch");
+            } else if (e->use_pix()) {
+                ck(launch_conv_pix(L, e->choose_npx(L.m_total), e->precision == MG_PREC_FP16,
+                                   e->num_sms, st),
+                   "conv3x3_pix launch");
+            } else {
+                const bool fp16 = e->precision == MG_PREC_FP16;
+                const int bn = e->choose_bn(L.m_total);
+                CUtensorMap ta, tb;
+                const char* why = "";
+                if (!make_conv_tensor_maps(L, bn, fp16, &ta, &tb, &why))
+                    throw std::runtime_error(why);
+                ck(launch_conv_tc(L, ta, tb, bn, fp16, e->num_sms, st), "conv3x3_tc launch");
+            }
+        }
+        if (!fused)
+            ck(launch_head_projection(b.x32, n, e->cpad, e->g, e->d_head_w, e->d_head_b, b.feat, st),
+               "head projection launch");
+        ck(launch_heads_fc(b.feat, e->fc, n, b.fc, d_policy, d_logits ? d_logits : b.logits, d_value,
+                           st),
+           "heads launch");
+        ck(cudaMemcpyAsync(&dev_err, b.err, sizeof(int), cudaMemcpyDeviceToHost, st),
+           "cudaMemcpyAsync(status)");
+        ck(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    });
+    if (rc == MG_OK && dev_err != 0)
+        return fail(e, MG_E_DEVICE, "a kernel gave up waiting (device status " +
+                                        std::to_string(dev_err) + ")");
+    return rc;
+}
+
+

@@ -51,13 +51,15 @@ def lib() -> ctypes.CDLL:
         L.mg_set_max_batch.argtypes = [vp, ci]
         L.mg_forward.argtypes = [vp, fp, ci, fp, fp, fp]
         L.mg_forward_device.argtypes = [vp, fp, ci, fp, fp, fp]
+        L.mg_forward_device_noalloc.argtypes = [vp, fp, ci, fp, fp, fp]
         L.mg_synchronize.argtypes = [vp]
         L.mg_stream.argtypes = [vp]
         L.mg_stream.restype = vp
         L.mg_launch_conv.argtypes = [vp, ci, ci, ci]
         L.mg_launches_per_forward.argtypes = [vp, ci]
         for f in ("mg_load_onnx", "mg_load_weights", "mg_get_info", "mg_set_precision",
-                  "mg_set_max_batch", "mg_forward", "mg_forward_device", "mg_synchronize",
+                  "mg_set_max_batch", "mg_forward", "mg_forward_device", "mg_forward_device_noalloc",
+                  "mg_synchronize",
                   "mg_launch_conv", "mg_launches_per_forward"):
             getattr(L, f).restype = ci
         _LIB = L
@@ -167,6 +169,14 @@ class CudaEngine:
     def forward_device(self, d_states: int, n: int, d_policy: int, d_value: int,
                        d_logits: int | None = None) -> None:
         self._check(self._L.mg_forward_device(self._h, d_states, n, d_policy, d_value, d_logits))
+
+    def forward_device_noalloc(self, d_states: int, n: int, d_policy: int, d_value: int,
+                               d_logits: int | None = None) -> None:
+        """As forward_device, with every intermediate buffer taken from the
+        library's fixed per-device scratch arena (no device allocation);
+        blocks until the outputs are written."""
+        self._check(self._L.mg_forward_device_noalloc(self._h, d_states, n, d_policy, d_value,
+                                                      d_logits))
 
     def synchronize(self) -> None:
         self._check(self._L.mg_synchronize(self._h))

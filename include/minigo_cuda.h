@@ -108,6 +108,20 @@ int mg_forward(mg_engine* e, const float* states, int n, float* policy_out,
 int mg_forward_device(mg_engine* e, const float* d_states, int n, float* d_policy,
                       float* d_value, float* d_logits);
 
+/* As mg_forward_device, but allocates nothing: every intermediate buffer
+ * comes from a fixed 32 MiB per-device scratch arena compiled into this
+ * library, so it suits callers that may not call cudaMalloc/cudaFree once
+ * running (both synchronise the device; cudaFree waits for all of it) or
+ * that work inside a fixed GPU memory budget.  No counterpart in the
+ * reference.  Limits: n is capped by the arena (19x19 bf16: 71 positions
+ * with 128 filters, 38 with 256; the error message states the cap); the first call on
+ * a device looks up the arena's address and should come before any stream
+ * capture; all calls on a device share the arena, so calls whose work
+ * overlaps on the GPU race and must be serialised.  Blocks until the results
+ * are in the output buffers; d_logits may be NULL. */
+int mg_forward_device_noalloc(mg_engine* e, const float* d_states, int n, float* d_policy,
+                              float* d_value, float* d_logits);
+
 /* Waits for all work on the engine's stream and reports device-side errors. */
 int mg_synchronize(mg_engine* e);
 
