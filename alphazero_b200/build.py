@@ -53,8 +53,20 @@ HOST_HEADERS = [
     os.path.join(INCLUDE, "minigo_host.h"),
 ]
 
+EVAL_SOURCES = [
+    os.path.join(HOST, "cuda_engine.cpp"),
+    os.path.join(HOST, "gpu_evaluator.cpp"),
+]
+EVAL_HEADERS = [
+    os.path.join(HOST, "cuda_engine.h"),
+    os.path.join(HOST, "gpu_evaluator.h"),
+    os.path.join(HOST, "minigo_api.h"),
+    os.path.join(INCLUDE, "minigo_cuda.h"),
+]
+
 CUDA_LIB = os.path.join(LIB, "libminigo_cuda.so")
 HOST_LIB = os.path.join(LIB, "libminigo_host.so")
+EVAL_LIB = os.path.join(LIB, "libminigo_evaluator.so")
 
 
 def _stale(target: str, deps: list[str]) -> bool:
@@ -94,8 +106,21 @@ def build_cuda(force: bool = False) -> str:
     return CUDA_LIB
 
 
+def build_evaluator(force: bool = False) -> str:
+    """C++ InferenceEngine / BatchEvaluator classes over the C ABI (host
+    code only; links libminigo_cuda.so)."""
+    cuda = build_cuda(force)
+    if force or _stale(EVAL_LIB, EVAL_SOURCES + EVAL_HEADERS + [cuda]):
+        tmp = EVAL_LIB + ".tmp"
+        _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-pthread",
+              "-o", tmp] + EVAL_SOURCES +
+             ["-L" + LIB, "-lminigo_cuda", "-Wl,-rpath,$ORIGIN"])
+        os.replace(tmp, EVAL_LIB)
+    return EVAL_LIB
+
+
 def build_all(force: bool = False) -> list[str]:
-    return [build_host(force), build_cuda(force)]
+    return [build_host(force), build_cuda(force), build_evaluator(force)]
 
 
 if __name__ == "__main__":

@@ -777,6 +777,19 @@ int mg_synchronize(mg_engine* e) {
 
 void* mg_stream(mg_engine* e) { return e ? (void*)e->stream : nullptr; }
 
+float* mg_host_input(mg_engine* e) {
+    if (e == nullptr) return nullptr;
+    float* out = nullptr;
+    guarded(e, [&] {
+        e->check_ready();
+        e->ensure_buffers();
+        out = e->h_states;
+    });
+    return out;
+}
+
+int mg_max_batch(const mg_engine* e) { return e ? e->max_batch : 0; }
+
 int mg_launch_conv(mg_engine* e, int n, int layer, int reps) {
     if (e == nullptr) return MG_E_ARG;
     return guarded(e, [&] {

@@ -1,0 +1,253 @@
+#include "gpu_evaluator.h"
+
+#include "cuda_engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <limits>
+#include <stdexcept>
+#include <unordered_map>
+#include <utility>
+
+namespace minigo {
+
+GpuEvaluator::GpuEvaluator(InferenceEngine* engine, int max_batch_size)
+    : engine_(engine), cuda_(dynamic_cast<CudaEngine*>(engine)), max_batch_(max_batch_size) {
+    if (engine_ == nullptr || max_batch_ < 1) throw std::invalid_argument("GpuEvaluator: bad arguments");
+    queue_.reserve(max_batch_);
+    server_ = std::thread(&GpuEvaluator::server_loop, this);
+}
+
+GpuEvaluator::~GpuEvaluator() {
+    {
+        std::lock_guard<std::mutex> lock(mu_);
+        stop_ = true;
+    }
+    cv_.notify_all();
+    server_.join();
+}
+
+BatchEvaluator::Result GpuEvaluator::take_result(NNResultBuf& buf) {
+    if (buf.policy.empty()) {
+        std::string why;
+        {
+            std::lock_guard<std::mutex> lock(mu_);
+            why = last_error_;
+        }
+        throw std::runtime_error("batched evaluation failed: " + why);
+    }
+    return {std::move(buf.policy), buf.value};
+}
+
+BatchEvaluator::Result GpuEvaluator::evaluate_with_buf(NNResultBuf& buf,
+                                                      const std::vector<float>& state) {
+    buf.done = false;
+    buf.state_data = state.data();
+    buf.state_size = (int)state.size();
+    {
+        std::lock_guard<std::mutex> lock(mu_);
+        queue_.push_back(&buf);
+    }
+    cv_.notify_all();
+    {
+        std::unique_lock<std::mutex> lock(buf.mu);
+        buf.cv.wait(lock, [&] { return buf.done; });
+    }
+    return take_result(buf);
+}
+
+BatchEvaluator::Result GpuEvaluator::evaluate_single(const std::vector<float>& state) {
+    NNResultBuf buf;
+    return evaluate_with_buf(buf, state);
+}
+
+std::vector<BatchEvaluator::Result> GpuEvaluator::evaluate(
+    const std::vector<std::vector<float>>& states) {
+    if (states.empty()) return {};
+    const size_t n = states.size();
+    std::vector<std::unique_ptr<NNResultBuf>> bufs(n);
+    {
+        std::lock_guard<std::mutex> lock(mu_);
+        for (size_t i = 0; i < n; ++i) {
+            bufs[i] = std::make_unique<NNResultBuf>();
+            bufs[i]->state_data = states[i].data();
+            bufs[i]->state_size = (int)states[i].size();
+            queue_.push_back(bufs[i].get());
+        }
+    }
+    cv_.notify_all();
+    std::vector<Result> out;
+    out.reserve(n);
+    bool failed = false;
+    for (size_t i = 0; i < n; ++i) {
+        std::unique_lock<std::mutex> lock(bufs[i]->mu);
+        bufs[i]->cv.wait(lock, [&] { return bufs[i]->done; });
+        failed |= bufs[i]->policy.empty();
+        out.emplace_back(std::move(bufs[i]->policy), bufs[i]->value);
+    }
+    if (failed) {
+        std::lock_guard<std::mutex> lock(mu_);
+        throw std::runtime_error("batched evaluation failed: " + last_error_);
+    }
+    return out;
+}
+
+void GpuEvaluator::run_batch(std::vector<NNResultBuf*>& batch) {
+    const int n = (int)batch.size();
+    if (cuda_ != nullptr) {
+        const int a = cuda_->action_size();
+        ptrs_.resize(n);
+        for (int i = 0; i < n; ++i) ptrs_[i] = batch[i]->state_data;
+        policy_.resize((size_t)n * a);
+        value_.resize(n);
+        cuda_->predict_raw(ptrs_.data(), n, batch[0]->state_size, policy_.data(), value_.data());
+        for (int i = 0; i < n; ++i) {
+            NNResultBuf* buf = batch[i];
+            std::lock_guard<std::mutex> lock(buf->mu);
+            buf->policy.assign(policy_.begin() + (size_t)i * a, policy_.begin() + (size_t)(i + 1) * a);
+            buf->value = value_[i];
+            buf->done = true;
+            // Notify under the lock: once the client sees `done` it may return
+            // and destroy its buffer (and condition variable).
+            buf->cv.notify_one();
+        }
+        return;
+    }
+    std::vector<std::vector<float>> states;
+    states.reserve(n);
+    for (auto* buf : batch) states.emplace_back(buf->state_data, buf->state_data + buf->state_size);
+    auto results = engine_->predict_batch(states);
+    if ((int)results.size() != n) throw std::runtime_error("engine returned a short batch");
+    for (int i = 0; i < n; ++i) {
+        NNResultBuf* buf = batch[i];
+        std::lock_guard<std::mutex> lock(buf->mu);
+        buf->policy = std::move(results[i].first);
+        buf->value = results[i].second;
+        buf->done = true;
+        buf->cv.notify_one();
+    }
+}
+
+void GpuEvaluator::server_loop() {
+    std::vector<NNResultBuf*> batch;
+    batch.reserve(max_batch_);
+    while (true) {
+        {
+            std::unique_lock<std::mutex> lock(mu_);
+            cv_.wait(lock, [this] { return !queue_.empty() || stop_; });
+            if (stop_ && queue_.empty()) break;
+            const int n = std::min((int)queue_.size(), max_batch_);
+            batch.assign(queue_.begin(), queue_.begin() + n);
+            queue_.erase(queue_.begin(), queue_.begin() + n);
+        }
+        try {
+            run_batch(batch);
+            batches_.fetch_add(1);
+            positions_.fetch_add(batch.size());
+            int seen = largest_.load();
+            while ((int)batch.size() > seen && !largest_.compare_exchange_weak(seen, (int)batch.size())) {
+            }
+        } catch (const std::exception& ex) {
+            failed_.fetch_add(1);
+            {
+                std::lock_guard<std::mutex> lock(mu_);
+                last_error_ = ex.what();
+            }
+            // Wake every client of the batch with an empty policy: each one
+            // turns that into an exception on its own thread.
+            for (auto* buf : batch) {
+                std::lock_guard<std::mutex> lock(buf->mu);
+                if (!buf->done) {
+                    buf->policy.clear();
+                    buf->value = std::numeric_limits<float>::quiet_NaN();
+                    buf->done = true;
+                    buf->cv.notify_one();
+                }
+            }
+        }
+        batch.clear();
+    }
+}
+
+// ---------------------------------------------------------------------------
+
+namespace {
+std::atomic<uint64_t> g_sharded_ids{1};
+}
+
+ShardedEvaluator::ShardedEvaluator(const std::vector<InferenceEngine*>& engines, int max_batch_size)
+    : id_(g_sharded_ids.fetch_add(1)) {
+    if (engines.empty()) throw std::invalid_argument("ShardedEvaluator: no engines");
+    for (auto* e : engines) shards_.push_back(std::make_unique<GpuEvaluator>(e, max_batch_size));
+}
+
+std::unique_ptr<ShardedEvaluator> ShardedEvaluator::create_cuda(const std::string& model_path,
+                                                                const std::vector<int>& devices,
+                                                                int max_batch_size) {
+    std::vector<std::unique_ptr<InferenceEngine>> owned;
+    std::vector<InferenceEngine*> raw;
+    for (int d : devices) {
+        auto e = std::make_unique<CudaEngine>(d, CudaEngine::kBf16, false, max_batch_size);
+        e->load_model(model_path);
+        raw.push_back(e.get());
+        owned.push_back(std::move(e));
+    }
+    auto s = std::make_unique<ShardedEvaluator>(raw, max_batch_size);
+    s->owned_engines_ = std::move(owned);
+    return s;
+}
+
+ShardedEvaluator::~ShardedEvaluator() {
+    shards_.clear();  // servers stop before the engines they drive
+    owned_engines_.clear();
+}
+
+int ShardedEvaluator::shard_of_this_thread() {
+    thread_local std::unordered_map<uint64_t, int> assigned;
+    auto it = assigned.find(id_);
+    if (it != assigned.end()) return it->second;
+    const int s = (int)(next_.fetch_add(1) % shards_.size());
+    assigned.emplace(id_, s);
+    return s;
+}
+
+BatchEvaluator::Result ShardedEvaluator::evaluate_with_buf(NNResultBuf& buf,
+                                                          const std::vector<float>& state) {
+    return shards_[shard_of_this_thread()]->evaluate_with_buf(buf, state);
+}
+
+BatchEvaluator::Result ShardedEvaluator::evaluate_single(const std::vector<float>& state) {
+    return shards_[shard_of_this_thread()]->evaluate_single(state);
+}
+
+std::vector<BatchEvaluator::Result> ShardedEvaluator::evaluate(
+    const std::vector<std::vector<float>>& states) {
+    const size_t n = states.size(), k = shards_.size();
+    if (n == 0) return {};
+    if (k == 1 || n == 1) return shards_[shard_of_this_thread()]->evaluate(states);
+    std::vector<std::vector<Result>> parts(k);
+    std::vector<std::string> errors(k);
+    std::vector<std::thread> workers;
+    for (size_t s = 0; s < k; ++s) {
+        const size_t lo = n * s / k, hi = n * (s + 1) / k;
+        if (lo == hi) continue;
+        workers.emplace_back([&, s, lo, hi] {
+            try {
+                std::vector<std::vector<float>> slice(states.begin() + lo, states.begin() + hi);
+                parts[s] = shards_[s]->evaluate(slice);
+            } catch (const std::exception& ex) {
+                errors[s] = ex.what();
+            }
+        });
+    }
+    for (auto& w : workers) w.join();
+    for (auto& e : errors)
+        if (!e.empty()) throw std::runtime_error(e);
+    std::vector<Result> out;
+    out.reserve(n);
+    for (auto& p : parts)
+        for (auto& r : p) out.push_back(std::move(r));
+    return out;
+}
+
+}  // namespace minigo

@@ -1,0 +1,114 @@
+// Batching servers for the network evaluation path.
+//
+// GpuEvaluator is the reference's NNEvaluator (src/nn_evaluator.cpp:6-140)
+// for one engine: search threads push an NNResultBuf, one server thread pops
+// up to max_batch of them with no timeout or minimum (the batch size follows
+// the number of concurrent search threads), runs one batched evaluation and
+// wakes each client.  Three differences:
+//   * a failed batch is reported to its clients: evaluate_with_buf /
+//     evaluate / evaluate_single throw std::runtime_error on the calling
+//     thread, where the reference returned an empty policy that the search
+//     then indexed out of bounds (src/nn_evaluator.cpp:117-125,
+//     src/mcts.cpp:59-64);
+//   * with a CudaEngine, states are gathered straight from the clients'
+//     buffers into the engine's pinned input buffer (one host copy instead of
+//     the reference's two, src/nn_evaluator.cpp:108-112 plus the engine's);
+//   * a client is woken while its buffer's mutex is held: the reference
+//     notifies after unlocking (src/nn_evaluator.cpp:127-137), so a client
+//     that sees `done` can return and destroy its stack NNResultBuf while
+//     notify_one still runs on its condition variable (found by
+//     ThreadSanitizer in this repository's tests).
+//
+// ShardedEvaluator runs one GpuEvaluator per GPU (weights replicated, no
+// collective) and assigns each search thread to one of them round-robin on
+// its first call, so the MCTS code (src/mcts.cpp) uses it unchanged through
+// the BatchEvaluator interface.
+#pragma once
+
+#include "minigo_api.h"
+
+#include <atomic>
+#include <condition_variable>
+#include <cstdint>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+namespace minigo {
+
+class CudaEngine;
+
+class GpuEvaluator : public BatchEvaluator {
+public:
+    GpuEvaluator(InferenceEngine* engine, int max_batch_size);
+    ~GpuEvaluator() override;
+    GpuEvaluator(const GpuEvaluator&) = delete;
+    GpuEvaluator& operator=(const GpuEvaluator&) = delete;
+
+    std::vector<Result> evaluate(const std::vector<std::vector<float>>& states) override;
+    Result evaluate_with_buf(NNResultBuf& buf, const std::vector<float>& state) override;
+    Result evaluate_single(const std::vector<float>& state) override;
+
+    // Counters (for batching statistics and tests).
+    uint64_t batches() const { return batches_.load(); }
+    uint64_t positions() const { return positions_.load(); }
+    int largest_batch() const { return largest_.load(); }
+    uint64_t failed_batches() const { return failed_.load(); }
+
+private:
+    void server_loop();
+    void run_batch(std::vector<NNResultBuf*>& batch);
+    Result take_result(NNResultBuf& buf);
+
+    InferenceEngine* engine_;
+    CudaEngine* cuda_;  // engine_ when it is a CudaEngine, else null
+    int max_batch_;
+
+    std::mutex mu_;
+    std::condition_variable cv_;
+    std::vector<NNResultBuf*> queue_;
+    bool stop_ = false;
+    std::string last_error_;  // guarded by mu_
+
+    std::vector<const float*> ptrs_;
+    std::vector<float> policy_, value_;
+
+    std::atomic<uint64_t> batches_{0}, positions_{0}, failed_{0};
+    std::atomic<int> largest_{0};
+    std::thread server_;
+};
+
+class ShardedEvaluator : public BatchEvaluator {
+public:
+    // One GpuEvaluator per engine (the engines stay owned by the caller).
+    ShardedEvaluator(const std::vector<InferenceEngine*>& engines, int max_batch_size);
+
+    // Owning convenience: one CudaEngine per device, all loading model_path.
+    static std::unique_ptr<ShardedEvaluator> create_cuda(const std::string& model_path,
+                                                         const std::vector<int>& devices,
+                                                         int max_batch_size);
+
+    ~ShardedEvaluator() override;
+
+    // Splits the batch into contiguous slices, one per shard, evaluated
+    // concurrently; results keep the input order.
+    std::vector<Result> evaluate(const std::vector<std::vector<float>>& states) override;
+    // Routed to the calling thread's shard.
+    Result evaluate_with_buf(NNResultBuf& buf, const std::vector<float>& state) override;
+    Result evaluate_single(const std::vector<float>& state) override;
+
+    size_t shards() const { return shards_.size(); }
+    GpuEvaluator& shard(size_t i) { return *shards_[i]; }
+    // Shard the calling thread is assigned to (assigning it on first use).
+    int shard_of_this_thread();
+
+private:
+    std::vector<std::unique_ptr<InferenceEngine>> owned_engines_;
+    std::vector<std::unique_ptr<GpuEvaluator>> shards_;
+    std::atomic<uint32_t> next_{0};
+    uint64_t id_;
+};
+
+}  // namespace minigo

@@ -102,6 +102,16 @@ int mg_set_max_batch(mg_engine* e, int max_batch);
 int mg_forward(mg_engine* e, const float* states, int n, float* policy_out,
                float* value_out, float* logits_out);
 
+/* The engine's pinned (page-locked) host input buffer, room for
+ * mg_max_batch() positions.  Filling it and passing it to mg_forward avoids
+ * any intermediate host copy.  Valid until mg_set_max_batch,
+ * mg_set_precision, a new load or mg_destroy; NULL (see mg_last_error) if no
+ * model is loaded or allocation fails. */
+float* mg_host_input(mg_engine* e);
+
+/* Current max batch (mg_set_max_batch). */
+int mg_max_batch(const mg_engine* e);
+
 /* As mg_forward, with every pointer in this engine's device memory.
  * Enqueues on the engine's stream and returns without waiting; pair with
  * mg_synchronize.  n must not exceed the max batch. */
