@@ -73,12 +73,12 @@ def load_peaks():
 
 def profiled_traffic(workload):
     """DRAM bytes per conv launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", f"conv3x3_tc_{workload}.md")
-    try:
+    import glob
+    for p in sorted(glob.glob(os.path.join(ROOT, "profiles", f"conv3x3_*_{workload}.md"))):
         m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
-        return float(m.group(1)) if m else None
-    except OSError:
-        return None
+        if m:
+            return float(m.group(1))
+    return None
 
 
 class ClockSampler:
@@ -337,7 +337,7 @@ def run_b200(args, wl):
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                     "traffic": traffic, "kernel": "conv3x3_tc_kernel (residual-block conv)",
+                     "traffic": traffic, "kernel": "3x3 conv of residual block 0 (conv1)",
                      "flops_per_launch": conv_flops, "launch_ms": conv_ms,
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
         "tflops_whole_forward": value * flops_per_position(board, filters, blocks) / 1e12,
