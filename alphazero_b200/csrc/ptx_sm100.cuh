@@ -1,5 +1,6 @@
 // Inline-PTX wrappers for the sm_100a features the kernels use: mbarriers,
-// TMA tiled loads (never with cluster multicast), tcgen05 MMA / TMEM, and a
+// TMA tiled loads and stores (each CTA copies for itself only), tcgen05 MMA /
+// TMEM, and a
 // bounded wait that gives up with an error code instead of spinning forever.
 #pragma once
 

@@ -165,6 +165,52 @@ def dist_setup():
     return world, rank, local
 
 
+class Ranks:
+    """Barrier and max-over-ranks for the per-rank replicas (one process per
+    GPU launched by torchrun).  No collective touches the data path: NCCL
+    (or gloo on CPU) only carries these scalars."""
+
+    def __init__(self, backend="nccl", device=None, timeout_s=120):
+        self.world, self.rank, self.local = dist_setup()
+        self.pg = None
+        self.device = device
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+
+            kw = {"timeout": datetime.timedelta(seconds=timeout_s)}
+            if backend == "nccl" and device is not None:
+                kw["device_id"] = device
+            dist.init_process_group(backend, **kw)
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg is not None:
+            self.pg.barrier()
+
+    def max(self, v):
+        if self.pg is None:
+            return float(v)
+        import torch
+
+        t = torch.tensor([float(v)], dtype=torch.float64,
+                         device=self.device if self.device is not None else "cpu")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+            self.pg = None
+
+
+def aggregate_rate(world, per_rank_units, steps, max_seconds):
+    """Whole-job units per second: every rank processes per_rank_units per
+    step, the job takes the slowest rank's time."""
+    return world * per_rank_units * steps / max_seconds
+
+
 def run_reference(args, wl):
     world, rank, _ = dist_setup()
     if rank != 0:
@@ -225,14 +271,7 @@ def run_b200(args, wl):
 
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
-    pg = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-        pg = dist
+    ranks = Ranks("nccl", device=torch.device("cuda", local))
     board, filters, blocks, batch, max_moves = WORKLOADS[wl]
     hw = board * board
     actions = hw + 1
@@ -254,16 +293,10 @@ def run_b200(args, wl):
     torch.cuda.synchronize()
 
     def barrier():
-        if pg is not None:
-            pg.barrier()
+        ranks.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(v):
-        if pg is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        return float(t.item())
+    max_over_ranks = ranks.max
 
     # ---- value: device-resident inputs, L2 flushed before each step ----
     with torch.cuda.stream(stream):
@@ -285,7 +318,7 @@ def run_b200(args, wl):
     barrier()
     dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
     dev_ms = max_over_ranks(dev_ms)
-    value = world * batch * args.steps / (dev_ms / 1e3)
+    value = aggregate_rate(world, batch, args.steps, dev_ms / 1e3)
     launches = eng.launches_per_forward(batch) * args.steps
 
     # ---- e2e: host API, pinned inputs, H2D + forward + D2H per step ----
@@ -300,7 +333,7 @@ def run_b200(args, wl):
     e2e_s = time.perf_counter() - t0
     barrier()
     e2e_s = max_over_ranks(e2e_s)
-    e2e = world * batch * args.steps / e2e_s
+    e2e = aggregate_rate(world, batch, args.steps, e2e_s)
 
     # ---- roofline: the 3x3 conv kernel alone (conv1 of block 0) ----
     reps = 50
@@ -321,9 +354,7 @@ def run_b200(args, wl):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = cpu_baseline(sd, x)
 
-    if pg is not None:
-        pg.barrier()
-        pg.destroy_process_group()
+    ranks.close()
     if rank != 0:
         return
     line = {
