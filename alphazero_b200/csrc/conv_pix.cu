@@ -27,6 +27,12 @@
 // issuer, warps 2-9 epilogue in two groups of four (group g takes chunks
 // g, g+2, ...; warp w of a group reads TMEM lanes [32*(w%4), +32)).  All
 // waits are bounded.
+//
+// Work split: CTA b owns the contiguous pixel range [b*span, (b+1)*span),
+// cut into equal tiles of at most 256 pixels, so every SM gets the same
+// number of pixels (a fixed 256-pixel tiling left up to 10% of the last wave
+// idle).  Launches are programmatic dependent launches: a CTA's prologue
+// overlaps the previous kernel's tail.
 #include "kernels.cuh"
 #include "ptx_sm100.cuh"
 
@@ -49,8 +55,9 @@ constexpr uint32_t kStage16 = kChunk * kCo * 2;        // 4 KB 16-bit chunk
 
 struct PixArgs {
     int m_total;
-    int num_tiles;
-    int npx;        // pixels per tile (multiple of 16, <= 256)
+    int span;           // pixels per CTA (multiple of 16): CTA b owns [b*span, (b+1)*span)
+    int tiles_per_cta;  // tiles its range is cut into
+    int npx;            // pixels per tile (multiple of 16, <= 256; the last tile may be shorter)
     int cin;
     int rs, is, board;
     int slab_rows;  // rows per slab (multiple of 16)
@@ -73,6 +80,16 @@ template <>
 __device__ __forceinline__ uint16_t to16<true>(float v) {
     __half h = __float2half_rn(v);
     return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// Tile k of this CTA's contiguous pixel range: rows [m0, m0 + len);
+// len <= 0 when the range has no such tile.  Every CTA gets the same number
+// of pixels (to within one tile), so the last wave is not mostly idle.
+__device__ __forceinline__ void cta_tile(const PixArgs& a, int k, int& m0, int& len) {
+    const int start = blockIdx.x * a.span;
+    const int end = min(start + a.span, a.m_total);
+    m0 = start + k * a.npx;
+    len = min(a.npx, end - m0);
 }
 
 template <bool FP16>
@@ -133,6 +150,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything above touches only this CTA's resources and the layer's
+    // constant parameters.  Activations written by the previous kernel are
+    // read, and activations it may still read are overwritten, only after
+    // it has completed.
+    griddep_launch_dependents();
+    griddep_wait();
 
     const int cblocks = a.cin / kBK;
     const int halo = a.rs + 1;
@@ -145,8 +168,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_tensormap(&tmX);
             int iw = 0, is = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
-                const int m0 = tile * a.npx;
+            for (int k = 0; k < a.tiles_per_cta && ok; ++k) {
+                int m0, len;
+                cta_tile(a, k, m0, len);
+                if (len <= 0) break;
                 for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
                     const int sb = is & 1;
                     if (!mbar_wait(smem_u32(&sempty[sb]), ((is >> 1) & 1) ^ 1, a.err,
@@ -184,10 +209,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint32_t idesc = idesc_f16(kCo, a.npx, !FP16);
             int iw = 0, is = 0, t = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++t) {
+            for (int k = 0; k < a.tiles_per_cta && ok; ++k, ++t) {
+                int m0, len;
+                cta_tile(a, k, m0, len);
+                if (len <= 0) break;
+                // MMA N = the tile's pixels rounded up to 16
+                const uint32_t idesc = idesc_f16(kCo, (len + 15) & ~15, !FP16);
                 const int acc = t & 1;
                 if (!mbar_wait(smem_u32(&tempty[acc]), ((t >> 1) & 1) ^ 1, a.err, kErrWaitMma)) {
                     ok = false;
@@ -213,10 +242,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int r0 = halo + (tap / 3 - 1) * a.rs + (tap % 3 - 1);
                         const uint64_t ad = smem_desc_sw128(smem_u32(wring + s * kWBytes));
 #pragma unroll
-                        for (int k = 0; k < kBK / 16; ++k) {
+                        for (int kk = 0; kk < kBK / 16; ++kk) {
                             // row-shifted start, base offset 0 (see file comment)
-                            const uint64_t bd = smem_desc_sw128(slab + (uint32_t)r0 * 128u + 32u * k);
-                            mma_f16(d, ad + (uint64_t)(2 * k), bd, idesc, (cb | tap | k) != 0);
+                            const uint64_t bd = smem_desc_sw128(slab + (uint32_t)r0 * 128u + 32u * kk);
+                            mma_f16(d, ad + (uint64_t)(2 * kk), bd, idesc, (cb | tap | kk) != 0);
                         }
                         mma_commit(smem_u32(&wempty[s]));
                     }
@@ -238,25 +267,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int co = quarter * 32 + lane;
         const float bias = sbias[co];
         const int hw = a.board * a.board;
-        const int nchunks = a.npx / kChunk;
+        auto chunks_of = [&](int len) { return (len + kChunk - 1) / kChunk; };
         float* s32 = st32 + grp * (kChunk * kCo);
         uint16_t* s16 = st16 + grp * (kChunk * kCo);
         float* sres = stres + grp * (kChunk * kCo);
         const uint32_t rbar = smem_u32(&rfull[grp]);
         const bool store_out = (a.has_out32 | a.has_out16) != 0;
         int rissued = 0;  // residual loads issued (leader)
-        if (a.has_res && leader && blockIdx.x < a.num_tiles && grp < nchunks) {
-            // residual of this group's first chunk of its first tile
-            mbar_arrive_expect_tx(rbar, kStage32);
-            tma_load_2d(smem_u32(sres), &tmR, rbar, 0, blockIdx.x * a.npx + grp * kChunk);
-            ++rissued;
+        {
+            int m0, len;
+            cta_tile(a, 0, m0, len);
+            if (a.has_res && leader && len > 0 && grp < chunks_of(len)) {
+                // residual of this group's first chunk of its first tile
+                mbar_arrive_expect_tx(rbar, kStage32);
+                tma_load_2d(smem_u32(sres), &tmR, rbar, 0, m0 + grp * kChunk);
+                ++rissued;
+            }
         }
         int rseq = 0;  // residual loads consumed
         int t = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++t) {
+        for (int k = 0; k < a.tiles_per_cta && ok; ++k, ++t) {
+            int m0, len;
+            cta_tile(a, k, m0, len);
+            if (len <= 0) break;
+            const int nchunks = chunks_of(len);
             const int acc = t & 1;
-            const int m0 = tile * a.npx;
             ok = mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, a.err, kErrWaitEpilogue);
             if (bar_any(bar_a, 128, !ok)) {
                 ok = false;
@@ -273,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // lanes 0..15 classify pixels px0 + lane
                 const int mj = px0 + (lane & 15);
                 bool onb = false;
-                if (mj < a.m_total) {
+                if (c * kChunk + (lane & 15) < len) {
                     const int q = mj % a.is;
                     const int y = q / a.rs;
                     onb = (y < a.board) && (q - y * a.rs < a.board);
@@ -306,14 +342,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 named_barrier_sync(bar_a, 128);
                 if (a.has_res && leader) {
                     // Residual of this group's next chunk (this tile or the next).
-                    int nt = tile, nc = c + 2;
+                    int nm0 = m0, nlen = len, nc = c + 2;
                     if (nc >= nchunks) {
-                        nt = tile + gridDim.x;
+                        cta_tile(a, k + 1, nm0, nlen);
                         nc = grp;
+                        if (k + 1 >= a.tiles_per_cta) nlen = 0;
                     }
-                    if (nt < a.num_tiles) {
+                    if (nlen > 0 && nc < chunks_of(nlen)) {
                         mbar_arrive_expect_tx(rbar, kStage32);
-                        tma_load_2d(smem_u32(sres), &tmR, rbar, 0, nt * a.npx + nc * kChunk);
+                        tma_load_2d(smem_u32(sres), &tmR, rbar, 0, nm0 + nc * kChunk);
                         ++rissued;
                     }
                 }
@@ -437,17 +474,27 @@ cudaError_t configure_conv_pix() {
 }
 
 bool conv_pix_supported(const ConvLayer& L, int npx) {
-    return L.cout == kCo && L.cin % kBK == 0 && npx % kChunk == 0 && npx >= 32 &&
+    return L.cout == kCo && L.cin % kBK == 0 && npx % kChunk == 0 && npx >= 16 &&
            npx <= kMaxPx && pix_smem_bytes(npx, L.g.rs) <= 227 * 1024;
 }
 
-cudaError_t launch_conv_pix(const ConvLayer& L, int npx, bool fp16, int grid_limit,
+cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid_limit,
                             cudaStream_t stream) {
+    // Balanced ranges: each CTA takes span pixels (a multiple of 16) cut into
+    // equal tiles of at most max_npx.
+    const int units = (L.m_total + 15) / 16;
+    int grid = units < grid_limit ? units : grid_limit;
+    if (grid < 1) grid = 1;
+    const int span = (((L.m_total + grid - 1) / grid) + 15) / 16 * 16;
+    grid = (L.m_total + span - 1) / span;
+    const int tiles = (span + max_npx - 1) / max_npx;
+    const int npx = ((span + tiles - 1) / tiles + 15) / 16 * 16;
     if (!conv_pix_supported(L, npx)) return cudaErrorInvalidValue;
     PixArgs a;
     a.m_total = L.m_total;
+    a.span = span;
+    a.tiles_per_cta = tiles;
     a.npx = npx;
-    a.num_tiles = (L.m_total + npx - 1) / npx;
     a.cin = L.cin;
     a.rs = L.g.rs;
     a.is = L.g.is;
@@ -481,14 +528,22 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int npx, bool fp16, int grid_lim
         !encode(&tmO16, t16, 2, o16, kCo, L.out16 ? rows : kChunk, kCo, kChunk,
                 CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
-    int grid = a.num_tiles < grid_limit ? a.num_tiles : grid_limit;
-    if (grid < 1) grid = 1;
-    const size_t smem = pix_smem_bytes(npx, L.g.rs);
+    // Programmatic dependent launch: this kernel's CTAs may start (and run
+    // their prologue) while the previous kernel in the stream drains; they
+    // wait for its completion before touching activations (griddep_wait).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pix_smem_bytes(npx, L.g.rs);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (fp16)
-        conv3x3_pix_kernel<true><<<grid, kThreads, smem, stream>>>(tmW, tmX, tmR, tmO32, tmO16, a);
-    else
-        conv3x3_pix_kernel<false><<<grid, kThreads, smem, stream>>>(tmW, tmX, tmR, tmO32, tmO16, a);
-    return cudaGetLastError();
+        return cudaLaunchKernelEx(&cfg, conv3x3_pix_kernel<true>, tmW, tmX, tmR, tmO32, tmO16, a);
+    return cudaLaunchKernelEx(&cfg, conv3x3_pix_kernel<false>, tmW, tmX, tmR, tmO32, tmO16, a);
 }
 
 }  // namespace mgb

@@ -147,6 +147,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Activations of the previous kernel are read (and ones it may still
+    // read are overwritten) only after it has completed.
+    griddep_launch_dependents();
+    griddep_wait();
 
     const int cblocks = a.cin / kBK;
     const int kblocks = 9 * cblocks;
@@ -379,8 +383,18 @@ cudaError_t launch_bn(const ConvLayer& L, const CUtensorMap& tmA, const CUtensor
     a.err = L.err;
     int grid = a.num_tiles < grid_limit ? a.num_tiles : grid_limit;
     if (grid < 1) grid = 1;
-    conv3x3_tc_kernel<BN, FP16><<<grid, kThreads, Cfg::kSmem, stream>>>(tmA, tmB, a);
-    return cudaGetLastError();
+    // Programmatic dependent launch (see griddep_wait in the kernel).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, conv3x3_tc_kernel<BN, FP16>, tmA, tmB, a);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {

@@ -122,6 +122,8 @@ struct mg_engine {
     int* d_err = nullptr;
     float* h_states = nullptr;  // pinned staging for pageable inputs
     int* h_err = nullptr;       // pinned status word
+    uint32_t* d_bits = nullptr;  // bit-packed inputs [max_batch][words]
+    uint32_t* h_bits = nullptr;  // pinned staging for pageable packed inputs
 
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (bucket, precision)
     int last_bucket = 0;
@@ -140,6 +142,10 @@ struct mg_engine {
             if (p) cudaFree(p);
         if (h_states) cudaFreeHost(h_states);
         if (h_err) cudaFreeHost(h_err);
+        if (d_bits) cudaFree(d_bits);
+        if (h_bits) cudaFreeHost(h_bits);
+        d_bits = nullptr;
+        h_bits = nullptr;
         d_stage = d_x16 = d_t = nullptr;
         d_x = d_feat = d_fc = nullptr;
         d_states = d_probs = d_logits = d_value = nullptr;
@@ -172,6 +178,7 @@ struct mg_engine {
     }
 
     int elem_bytes() const { return precision == MG_PREC_FP32 ? 4 : 2; }
+    int words_per_pos() const { return (planes * hw + 31) / 32; }
     ActType act_type() const {
         return precision == MG_PREC_FP32 ? ActType::FP32
                                          : (precision == MG_PREC_FP16 ? ActType::FP16 : ActType::BF16);
@@ -356,6 +363,10 @@ struct mg_engine {
                           (size_t)max_batch * planes * hw * sizeof(float)),
            "cudaMallocHost(states)");
         ck(cudaMallocHost(reinterpret_cast<void**>(&h_err), sizeof(int)), "cudaMallocHost(err)");
+        d_bits = dalloc<uint32_t>((size_t)max_batch * words_per_pos(), "cudaMalloc(bits)");
+        ck(cudaMemset(d_bits, 0, (size_t)max_batch * words_per_pos() * 4), "cudaMemset(bits)");
+        ck(cudaMallocHost(reinterpret_cast<void**>(&h_bits), (size_t)max_batch * words_per_pos() * 4),
+           "cudaMallocHost(bits)");
         alloc_batch = max_batch;
         alloc_elem = elem;
     }
@@ -384,22 +395,11 @@ struct mg_engine {
     // 128-channel layers run the pixels-on-N kernel (conv_pix.cu).
     bool use_pix() const { return precision != MG_PREC_FP32 && cpad == 128 && pix_mode != 0; }
 
-    // Pixels per tile: the largest tile whose last wave is not much emptier
-    // than a smaller tile's (critical path ~ waves x (npx + weight reload)).
+    // Largest pixels per tile of the 128-channel kernel (its ranges are
+    // balanced across SMs by the launcher).
     int choose_npx(int m_total) const {
-        if (pix_npx > 0) return pix_npx;
-        int best = 256;
-        long best_cost = -1;
-        for (int npx = 256; npx >= 128; npx -= 16) {
-            const long tiles = (m_total + npx - 1) / npx;
-            const long waves = (tiles + num_sms - 1) / num_sms;
-            const long cost = waves * (npx + 64);
-            if (best_cost < 0 || cost < best_cost) {
-                best_cost = cost;
-                best = npx;
-            }
-        }
-        return best;
+        (void)m_total;
+        return pix_npx > 0 ? pix_npx : 256;
     }
 
     // Whether the last trunk layer computes the head projection in its
@@ -506,6 +506,17 @@ struct mg_engine {
         ck(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "cudaMemsetAsync(err)");
         ck(launch_stage_input(d_src, n, bucket, planes, g, kStagedChannels,
                               (flags & MG_FLAG_EIGEN_COMPAT) != 0, act_type(), d_stage, stream),
+           "stage launch");
+        run_graph(bucket);
+        last_bucket = bucket;
+    }
+
+    // As forward_core for bit-packed inputs (device pointer).
+    void forward_core_bits(const uint32_t* d_src, int n) {
+        const int bucket = bucket_for(n);
+        ck(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "cudaMemsetAsync(err)");
+        ck(launch_stage_bits(d_src, words_per_pos(), n, bucket, planes, g, kStagedChannels,
+                             (flags & MG_FLAG_EIGEN_COMPAT) != 0, act_type(), d_stage, stream),
            "stage launch");
         run_graph(bucket);
         last_bucket = bucket;
@@ -757,6 +768,87 @@ int mg_forward_device(mg_engine* e, const float* d_states, int n, float* d_polic
                                cudaMemcpyDeviceToDevice, e->stream),
                "cudaMemcpyAsync(logits)");
     });
+}
+
+int mg_words_per_position(const mg_engine* e) {
+    if (e == nullptr || !e->loaded) return 0;
+    return e->words_per_pos();
+}
+
+int mg_pack_states(const float* states, int n, int state_size, uint32_t* out) {
+    if (n < 0 || state_size <= 0 || (n > 0 && (states == nullptr || out == nullptr))) return MG_E_ARG;
+    const int words = (state_size + 31) / 32;
+    for (int i = 0; i < n; ++i) {
+        const float* s = states + (size_t)i * state_size;
+        uint32_t* w = out + (size_t)i * words;
+        for (int k = 0; k < words; ++k) {
+            uint32_t v = 0;
+            const int lo = k * 32, hi = std::min(state_size, lo + 32);
+            for (int j = lo; j < hi; ++j) {
+                const float x = s[j];
+                if (x == 1.0f) v |= 1u << (j - lo);
+                else if (x != 0.0f) return MG_E_ARG;  // not a binary plane
+            }
+            w[k] = v;
+        }
+    }
+    return MG_OK;
+}
+
+int mg_forward_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_out,
+                      float* value_out, float* logits_out) {
+    if (e == nullptr) return MG_E_ARG;
+    if (n < 0) return fail(e, MG_E_ARG, "negative batch size");
+    if (n == 0) return MG_OK;
+    if (bits == nullptr || policy_out == nullptr || value_out == nullptr)
+        return fail(e, MG_E_ARG, "null buffer");
+    int dev_err = 0;
+    int rc = guarded(e, [&] {
+        e->check_ready();
+        e->prepare_weights();
+        e->ensure_buffers();
+        const size_t words = (size_t)e->words_per_pos();
+        const int A = e->actions;
+        const bool pinned = is_pinned(bits);
+        for (int base = 0; base < n; base += e->max_batch) {
+            const int m = std::min(e->max_batch, n - base);
+            const uint32_t* src = bits + (size_t)base * words;
+            if (pinned) {
+                ck(cudaMemcpyAsync(e->d_bits, src, (size_t)m * words * 4, cudaMemcpyHostToDevice,
+                                   e->stream),
+                   "cudaMemcpyAsync(H2D bits)");
+            } else {
+                ck(cudaStreamSynchronize(e->stream), "cudaStreamSynchronize");
+                std::memcpy(e->h_bits, src, (size_t)m * words * 4);
+                ck(cudaMemcpyAsync(e->d_bits, e->h_bits, (size_t)m * words * 4,
+                                   cudaMemcpyHostToDevice, e->stream),
+                   "cudaMemcpyAsync(H2D bits)");
+            }
+            e->forward_core_bits(e->d_bits, m);
+            ck(cudaMemcpyAsync(policy_out + (size_t)base * A, e->d_probs, (size_t)m * A * sizeof(float),
+                               cudaMemcpyDeviceToHost, e->stream),
+               "cudaMemcpyAsync(D2H policy)");
+            ck(cudaMemcpyAsync(value_out + base, e->d_value, (size_t)m * sizeof(float),
+                               cudaMemcpyDeviceToHost, e->stream),
+               "cudaMemcpyAsync(D2H value)");
+            if (logits_out)
+                ck(cudaMemcpyAsync(logits_out + (size_t)base * A, e->d_logits,
+                                   (size_t)m * A * sizeof(float), cudaMemcpyDeviceToHost, e->stream),
+                   "cudaMemcpyAsync(D2H logits)");
+            ck(cudaMemcpyAsync(e->h_err, e->d_err, sizeof(int), cudaMemcpyDeviceToHost, e->stream),
+               "cudaMemcpyAsync(D2H status)");
+            if (base + m < n) {
+                ck(cudaStreamSynchronize(e->stream), "cudaStreamSynchronize");
+                dev_err |= *e->h_err;
+            }
+        }
+        ck(cudaStreamSynchronize(e->stream), "cudaStreamSynchronize");
+        dev_err |= *e->h_err;
+    });
+    if (rc == MG_OK && dev_err != 0)
+        return fail(e, MG_E_DEVICE, "a kernel gave up waiting (device status " +
+                                        std::to_string(dev_err) + ")");
+    return rc;
 }
 
 int mg_synchronize(mg_engine* e) {

@@ -83,10 +83,11 @@ int conv_tc_smem_bytes(int bn);
 cudaError_t configure_conv_tc();
 
 // Tensor-core path for 128 output channels with pixels on the MMA N side
-// (conv_pix.cu): npx pixels per tile (multiple of 16, 32..256), one halo
-// slab per 64-channel block shared by the 9 taps.
+// (conv_pix.cu): each of up to grid_limit CTAs takes an equal contiguous
+// pixel range cut into tiles of at most max_npx (<= 256) pixels; one halo
+// slab per 64-channel block is shared by the 9 taps.
 bool conv_pix_supported(const ConvLayer& layer, int npx);
-cudaError_t launch_conv_pix(const ConvLayer& layer, int npx, bool fp16, int grid_limit,
+cudaError_t launch_conv_pix(const ConvLayer& layer, int max_npx, bool fp16, int grid_limit,
                             cudaStream_t stream);
 cudaError_t configure_conv_pix();
 
@@ -102,6 +103,13 @@ enum class ActType { BF16 = 0, FP16 = 1, FP32 = 2 };
 cudaError_t launch_stage_input(const float* states, int n_valid, int n_pos, int planes,
                                const FrameGeom& g, int cpad, bool eigen_order, ActType t,
                                void* out, cudaStream_t stream);
+
+// As launch_stage_input for the bit-packed wire format: position n's
+// planes are words_per_pos 32-bit words, element j (plane-major) in bit
+// j & 31 of word j >> 5.
+cudaError_t launch_stage_bits(const uint32_t* bits, int words_per_pos, int n_valid, int n_pos,
+                              int planes, const FrameGeom& g, int cpad, bool eigen_order, ActType t,
+                              void* out, cudaStream_t stream);
 
 // Head projection as a separate pass (fp32 SIMT path, or when the
 // tensor-core tile does not span all channels): the 1x1 policy / value

@@ -75,6 +75,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     }
 }
 
+// Programmatic dependent launch: let the next kernel in the stream start
+// its prologue, and wait until the previous kernel's results are visible.
+// Both are no-ops for kernels launched without the programmatic attribute.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Named barrier `id` over `nthreads` threads (a multiple of 32).
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

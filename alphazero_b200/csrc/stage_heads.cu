@@ -58,6 +58,51 @@ __global__ void stage_input_kernel(const float* __restrict__ states, int n_valid
     }
 }
 
+// As stage_input_kernel for bit-packed binary planes: position n's element
+// j (plane-major, c*B*B + p) is bit (j & 31) of word j >> 5 of its
+// words_per_pos words.
+template <ActType T>
+__global__ void stage_bits_kernel(const uint32_t* __restrict__ bits, int words_per_pos, int n_valid,
+                                  int rows, int planes, FrameGeom g, int cpad, int eigen_order,
+                                  void* __restrict__ out) {
+    const int groups = cpad >> 3;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    const int m = idx / groups;
+    const int c8 = (idx - m * groups) * 8;
+    if (m >= rows) return;
+    const int n = m / g.is;
+    const int q = m - n * g.is;
+    const int y = q / g.rs;
+    const int x = q - y * g.rs;
+    const bool live = (n < n_valid) && (y < g.board) && (x < g.board);
+    const int hw = g.board * g.board;
+    const int p = y * g.board + x;
+    const uint32_t* w = bits + (size_t)n * words_per_pos;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int c = c8 + j;
+        float val = 0.0f;
+        if (live && c < planes) {
+            const int e = eigen_order ? c + p * planes : c * hw + p;
+            val = (float)((w[e >> 5] >> (e & 31)) & 1u);
+        }
+        v[j] = val;
+    }
+    if (T == ActType::FP32) {
+        float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)m * cpad + c8);
+        o[0] = make_float4(v[0], v[1], v[2], v[3]);
+        o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint4 wv;
+        wv.x = pack2(v[0], v[1], T);
+        wv.y = pack2(v[2], v[3], T);
+        wv.z = pack2(v[4], v[5], T);
+        wv.w = pack2(v[6], v[7], T);
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + (size_t)m * cpad + c8) = wv;
+    }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -222,6 +267,33 @@ cudaError_t launch_stage_input(const float* states, int n_valid, int n_pos, int 
         case ActType::FP32:
             stage_input_kernel<ActType::FP32><<<(unsigned)blocks, threads, 0, stream>>>(
                 states, n_valid, rows, planes, g, cpad, eo, out);
+            break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_stage_bits(const uint32_t* bits, int words_per_pos, int n_valid, int n_pos,
+                              int planes, const FrameGeom& g, int cpad, bool eigen_order, ActType t,
+                              void* out, cudaStream_t stream) {
+    if (cpad % 8 != 0) return cudaErrorInvalidValue;
+    const long threads_total = (long)n_pos * g.is * (cpad / 8);
+    const int threads = 256;
+    const long blocks = (threads_total + threads - 1) / threads;
+    if (blocks == 0) return cudaSuccess;
+    const int rows = n_pos * g.is;
+    const int eo = eigen_order ? 1 : 0;
+    switch (t) {
+        case ActType::BF16:
+            stage_bits_kernel<ActType::BF16><<<(unsigned)blocks, threads, 0, stream>>>(
+                bits, words_per_pos, n_valid, rows, planes, g, cpad, eo, out);
+            break;
+        case ActType::FP16:
+            stage_bits_kernel<ActType::FP16><<<(unsigned)blocks, threads, 0, stream>>>(
+                bits, words_per_pos, n_valid, rows, planes, g, cpad, eo, out);
+            break;
+        case ActType::FP32:
+            stage_bits_kernel<ActType::FP32><<<(unsigned)blocks, threads, 0, stream>>>(
+                bits, words_per_pos, n_valid, rows, planes, g, cpad, eo, out);
             break;
     }
     return cudaGetLastError();

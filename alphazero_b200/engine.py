@@ -52,6 +52,9 @@ def lib() -> ctypes.CDLL:
         L.mg_forward.argtypes = [vp, fp, ci, fp, fp, fp]
         L.mg_forward_device.argtypes = [vp, fp, ci, fp, fp, fp]
         L.mg_forward_device_noalloc.argtypes = [vp, fp, ci, fp, fp, fp]
+        L.mg_forward_packed.argtypes = [vp, fp, ci, fp, fp, fp]
+        L.mg_words_per_position.argtypes = [vp]
+        L.mg_pack_states.argtypes = [fp, ci, ci, fp]
         L.mg_synchronize.argtypes = [vp]
         L.mg_stream.argtypes = [vp]
         L.mg_stream.restype = vp
@@ -59,11 +62,22 @@ def lib() -> ctypes.CDLL:
         L.mg_launches_per_forward.argtypes = [vp, ci]
         for f in ("mg_load_onnx", "mg_load_weights", "mg_get_info", "mg_set_precision",
                   "mg_set_max_batch", "mg_forward", "mg_forward_device", "mg_forward_device_noalloc",
-                  "mg_synchronize",
+                  "mg_forward_packed", "mg_words_per_position", "mg_pack_states", "mg_synchronize",
                   "mg_launch_conv", "mg_launches_per_forward"):
             getattr(L, f).restype = ci
         _LIB = L
     return _LIB
+
+
+def pack_states(states) -> np.ndarray:
+    """[n, size] binary fp32 planes -> [n, ceil(size / 32)] uint32 words of
+    the packed wire format (bit j % 32 of word j / 32), via mg_pack_states."""
+    x = np.ascontiguousarray(states, dtype=np.float32)
+    n, size = x.shape
+    out = np.empty((n, (size + 31) // 32), np.uint32)
+    if lib().mg_pack_states(x.ctypes.data, n, size, out.ctypes.data) != 0:
+        raise ValueError("states are not binary planes (values other than 0 and 1)")
+    return out
 
 
 class CudaEngine:
@@ -151,6 +165,24 @@ class CudaEngine:
                                            vals.ctypes.data,
                                            logits.ctypes.data if want_logits else None))
         return probs, vals, logits
+
+    def forward_packed(self, bits, n: int, want_logits: bool = False, out=None):
+        """Bit-packed wire format (see pack_states): bits holds n x
+        words_per_position() uint32 words.  `out` may supply (probs, values)
+        arrays to fill (e.g. pinned); returns (probs, values, logits)."""
+        b = np.ascontiguousarray(bits, dtype=np.uint32)
+        A = self.action_size
+        probs, vals = out if out is not None else (np.empty((n, A), np.float32),
+                                                    np.empty((n,), np.float32))
+        logits = np.empty((n, A), np.float32) if want_logits else None
+        if n:
+            self._check(self._L.mg_forward_packed(self._h, b.ctypes.data, n, probs.ctypes.data,
+                                                  vals.ctypes.data,
+                                                  logits.ctypes.data if want_logits else None))
+        return probs, vals, logits
+
+    def words_per_position(self) -> int:
+        return self._L.mg_words_per_position(self._h)
 
     def predict(self, state):
         """(softmaxed policy, value in [-1, 1]) for one flat state."""

@@ -31,6 +31,25 @@ void CudaEngine::load_model(const std::string& model_path) {
           "mg_get_info");
 }
 
+namespace {
+// Packs one state's binary planes into words (bit j % 32 of word j / 32);
+// false if some value is neither 0 nor 1.
+bool pack_state(const float* s, int size, uint32_t* w) {
+    const int words = (size + 31) / 32;
+    for (int k = 0; k < words; ++k) {
+        uint32_t v = 0;
+        const int lo = k * 32, hi = std::min(size, lo + 32);
+        for (int j = lo; j < hi; ++j) {
+            const float x = s[j];
+            v |= (uint32_t)(x == 1.0f) << (j - lo);
+            if (x != 0.0f && x != 1.0f) return false;
+        }
+        w[k] = v;
+    }
+    return true;
+}
+}  // namespace
+
 void CudaEngine::predict_raw(const float* const* states, int n, int state_size, float* policy,
                              float* value) {
     if (n <= 0) return;
@@ -38,6 +57,16 @@ void CudaEngine::predict_raw(const float* const* states, int n, int state_size, 
     if (state_size != expect)
         throw std::invalid_argument("state has " + std::to_string(state_size) + " floats, expected " +
                                     std::to_string(expect));
+    // Encoded positions are binary planes: ship them bit-packed (32x fewer
+    // bytes over PCIe), unless some state is not binary.
+    const int words = (state_size + 31) / 32;
+    bits_.resize((size_t)n * words);
+    bool binary = true;
+    for (int i = 0; i < n && binary; ++i) binary = pack_state(states[i], state_size, bits_.data() + (size_t)i * words);
+    if (binary) {
+        check(mg_forward_packed(h_, bits_.data(), n, policy, value, nullptr), "mg_forward_packed");
+        return;
+    }
     float* pinned = mg_host_input(h_);
     if (pinned == nullptr) throw std::runtime_error(std::string("mg_host_input: ") + mg_last_error(h_));
     const int cap = mg_max_batch(h_);

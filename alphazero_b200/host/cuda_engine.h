@@ -7,6 +7,7 @@
 #include "minigo_api.h"
 
 #include <cstddef>
+#include <cstdint>
 #include <string>
 #include <utility>
 #include <vector>
@@ -41,9 +42,11 @@ public:
 
     std::string backend_name() const override { return "cuda"; }
 
-    // Zero-extra-copy batch evaluation for evaluators: n state pointers of
-    // state_size floats each are gathered straight into the engine's pinned
-    // input buffer; results land in policy (n x action_size) and value (n).
+    // Batch evaluation for evaluators: n state pointers of state_size floats
+    // each.  Binary states (the encoder's planes) are packed to bits while
+    // gathered and shipped in the packed wire format; otherwise the fp32
+    // planes are gathered straight into the engine's pinned input buffer.
+    // Results land in policy (n x action_size) and value (n).
     void predict_raw(const float* const* states, int n, int state_size, float* policy,
                      float* value);
 
@@ -57,6 +60,7 @@ private:
     int device_ = 0;
     int action_size_ = 0;
     std::vector<float> policy_scratch_, value_scratch_;
+    std::vector<uint32_t> bits_;
 };
 
 }  // namespace minigo

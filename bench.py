@@ -11,9 +11,10 @@ JSON line.  Numbers:
   value      positions/s over all ranks, inputs resident in HBM, L2 flushed
              (256 MB write) before every timed step, CUDA-event timed on the
              engine's stream, max over ranks;
-  e2e        the same through the host API (mg_forward with pinned host
-             inputs): H2D of the inputs, forward, D2H of policy and value,
-             wall-clock timed, max over ranks;
+  e2e        the same through the host API with pinned host buffers: H2D of
+             the inputs in the bit-packed wire format (mg_forward_packed),
+             forward, D2H of policy and value, wall-clock timed, max over
+             ranks (e2e_fp32_planes: the same with fp32 planes, mg_forward);
   roofline   the 3x3 convolution kernel (the dominant kernel) timed alone with
              CUDA events: algorithmic FLOPs per launch / average launch time,
              against the measured dense bf16 peak;
@@ -321,19 +322,28 @@ def run_b200(args, wl):
     value = aggregate_rate(world, batch, args.steps, dev_ms / 1e3)
     launches = eng.launches_per_forward(batch) * args.steps
 
-    # ---- e2e: host API, pinned inputs, H2D + forward + D2H per step ----
-    pinned = torch.from_numpy(x).pin_memory()
-    xin = pinned.numpy()
-    for _ in range(args.warmup):
-        eng.forward(xin, want_logits=False)
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        eng.forward(xin, want_logits=False)
-    e2e_s = time.perf_counter() - t0
-    barrier()
-    e2e_s = max_over_ranks(e2e_s)
-    e2e = aggregate_rate(world, batch, args.steps, e2e_s)
+    # ---- e2e: host API, pinned inputs and outputs, H2D + forward + D2H per
+    # step, in the bit-packed wire format (and, for comparison, fp32 planes)
+    from alphazero_b200.engine import pack_states
+
+    words = eng.words_per_position()
+    bits = torch.from_numpy(pack_states(x).view(np.int32)).pin_memory().numpy().view(np.uint32)
+    outs = (torch.empty((batch, actions)).pin_memory().numpy(), torch.empty((batch,)).pin_memory().numpy())
+
+    def e2e_loop(step):
+        for _ in range(args.warmup):
+            step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        dt = time.perf_counter() - t0
+        barrier()
+        return aggregate_rate(world, batch, args.steps, max_over_ranks(dt))
+
+    e2e = e2e_loop(lambda: eng.forward_packed(bits, batch, out=outs))
+    xin = torch.from_numpy(x).pin_memory().numpy()
+    e2e_planes = e2e_loop(lambda: eng.forward(xin, want_logits=False))
 
     # ---- roofline: the 3x3 conv kernel alone (conv1 of block 0) ----
     reps = 50
@@ -363,8 +373,13 @@ def run_b200(args, wl):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config(wl),
         "e2e": {"value": e2e, "unit": "positions/s",
-                "h2d_bytes_per_step": batch * 17 * hw * 4,
-                "d2h_bytes_per_step": batch * (actions + 1) * 4},
+                "h2d_bytes_per_step": batch * words * 4,
+                "d2h_bytes_per_step": batch * (actions + 1) * 4,
+                "api": "mg_forward_packed (bit-packed planes, pinned host buffers)"},
+        "e2e_fp32_planes": {"value": e2e_planes, "unit": "positions/s",
+                            "h2d_bytes_per_step": batch * 17 * hw * 4,
+                            "d2h_bytes_per_step": batch * (actions + 1) * 4,
+                            "api": "mg_forward (fp32 planes, pinned input)"},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],

@@ -102,6 +102,25 @@ int mg_set_max_batch(mg_engine* e, int max_batch);
 int mg_forward(mg_engine* e, const float* states, int n, float* policy_out,
                float* value_out, float* logits_out);
 
+/* Bit-packed wire format.  The 17 input planes are binary, so a position can
+ * travel as words_per_position = ceil(17 * board^2 / 32) little-endian
+ * 32-bit words: element j of the plane-major state (c * board^2 + p) is bit
+ * (j % 32) of word j / 32.  That is 768 bytes instead of 24.5 KB per 19x19
+ * position on the host-to-device link.  No counterpart in the reference,
+ * whose engines take fp32 planes (include/inference_engine.h:21-32). */
+int mg_words_per_position(const mg_engine* e);
+
+/* Packs n states of state_size fp32 values (each exactly 0 or 1) into
+ * n * ceil(state_size / 32) words.  Returns MG_E_ARG if a value is neither
+ * 0 nor 1 (such inputs need mg_forward).  Host-only; no engine needed. */
+int mg_pack_states(const float* states, int n, int state_size, uint32_t* out);
+
+/* As mg_forward for bit-packed inputs (n * mg_words_per_position words in
+ * host memory; pinned buffers are copied by DMA directly).  Results are
+ * identical to mg_forward on the unpacked planes. */
+int mg_forward_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_out,
+                      float* value_out, float* logits_out);
+
 /* The engine's pinned (page-locked) host input buffer, room for
  * mg_max_batch() positions.  Filling it and passing it to mg_forward avoids
  * any intermediate host copy.  Valid until mg_set_max_batch,

@@ -52,3 +52,22 @@ def test_create_without_gpu_fails_cleanly():
     from alphazero_b200.engine import CudaEngine
     with pytest.raises(RuntimeError, match="mg_create failed"):
         CudaEngine(0)
+
+
+def test_pack_states_matches_numpy_and_rejects_non_binary():
+    import numpy as np
+
+    from alphazero_b200 import host_lib
+    from alphazero_b200.engine import pack_states
+
+    for board, n in ((19, 7), (9, 33), (5, 3)):
+        x = host_lib.random_positions(board, n, 4, 250)
+        b = pack_states(x)
+        assert b.shape == (n, (17 * board * board + 31) // 32)
+        ref = np.packbits(x.astype(bool), axis=1, bitorder="little")
+        ref = np.pad(ref, ((0, 0), (0, b.shape[1] * 4 - ref.shape[1]))).view("<u4")
+        assert np.array_equal(b, ref)
+    bad = host_lib.random_positions(9, 2, 4, 60)
+    bad[1, 5] = 0.5
+    with pytest.raises(ValueError):
+        pack_states(bad)

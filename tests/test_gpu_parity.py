@@ -162,3 +162,17 @@ def test_precision_switch_round_trip(gpu_engine_factory):
     _, _, l_bf2 = e.forward(x)
     assert np.array_equal(l_bf, l_bf2)
     assert np.abs(l_32 - z["logits"]).max() < TOL["fp32"]
+
+
+@pytest.mark.parametrize("eigen_compat", [False, True])
+def test_packed_wire_format_matches_fp32_planes(gpu_engine_factory, eigen_compat):
+    from alphazero_b200.engine import pack_states
+
+    _, sd = load_golden("b19c128x10_pert")
+    e = gpu_engine_factory(sd, "bf16", eigen_compat=eigen_compat, max_batch=64)
+    x = host_lib.random_positions(19, 150, 31, 250)  # 150 > max batch: chunked
+    bits = pack_states(x)
+    assert bits.shape[1] == e.words_per_position()
+    p1, v1, l1 = e.forward(x)
+    p2, v2, l2 = e.forward_packed(bits, len(x), want_logits=True)
+    assert np.array_equal(l1, l2) and np.array_equal(v1, v2) and np.array_equal(p1, p2)
