@@ -12,16 +12,18 @@
 // nine times.  (The MMA derives the 128-byte swizzle phase from the absolute
 // shared-memory address, as TMA does when it writes the slab, so a start
 // address moved by whole 128-byte rows needs no descriptor base offset.)
-// Weight K blocks (128 x 64) stream through a 6-deep ring.
+// Weight K blocks (128 x 64) stream through a 5-deep ring.
 //
 // The accumulator is [co lanes][px columns] in TMEM, double-buffered across
 // tiles (2 x 256 columns).  The epilogue moves activations only through
-// TMA: per 16-pixel chunk the fp32 residual rows arrive by a TMA load into
-// shared memory (issued one chunk ahead), each thread (= one channel) adds
-// bias and residual and applies ReLU and the frame mask, and the results are
-// staged in shared memory and leave as TMA bulk stores (fp32 and/or 16-bit).
-// In the last trunk layer the staged chunk instead feeds the policy / value
-// 1x1 head projection.
+// TMA.  Each epilogue group owns a ring of three 16-pixel fp32 chunk buffers:
+// the residual rows of a chunk arrive there by a TMA load issued two chunks
+// ahead (and the producer prefetches each tile's residual rows into L2 a
+// tile ahead), each thread (= one channel) adds bias and residual, applies
+// ReLU and the frame mask, and writes the fp32 result back into the same
+// buffer, which a TMA bulk store then copies out; 16-bit results go through
+// a second, double-buffered staging area.  In the last trunk layer the
+// staged chunk instead feeds the policy / value 1x1 head projection.
 //
 // Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
 // issuer, warps 2-9 epilogue in two groups of four (group g takes chunks
@@ -46,12 +48,13 @@ namespace {
 constexpr int kCo = 128;        // output channels (MMA M)
 constexpr int kBK = 64;         // K per stage / slab channel block
 constexpr int kMaxPx = 256;     // MMA N limit
-constexpr int kStages = 6;      // weight ring depth
+constexpr int kStages = 5;      // weight ring depth
 constexpr int kThreads = 320;
 constexpr int kChunk = 16;      // pixels per epilogue chunk
+constexpr int kRing = 3;        // fp32 chunk slots per epilogue warp
 constexpr uint32_t kWBytes = kCo * kBK * 2;            // 16 KB weight stage
-constexpr uint32_t kStage32 = kChunk * kCo * 4;        // 8 KB fp32 chunk
-constexpr uint32_t kStage16 = kChunk * kCo * 2;        // 4 KB 16-bit chunk
+constexpr int kSlot = kChunk * 32;  // one warp's chunk: 16 pixels x 32 channels
+constexpr int kEpiWarps = 8;
 
 struct PixArgs {
     int m_total;
@@ -61,7 +64,8 @@ struct PixArgs {
     int cin;
     int rs, is, board;
     int slab_rows;  // rows per slab (multiple of 16)
-    int has_res, has_out32, has_out16;
+    int has_out32, has_out16;
+    const float* res;     // fp32 residual [m_total][128] or nullptr
     const float* bias;
     const float* head_w;  // [3][128] or nullptr (fused head projection)
     const float* head_b;
@@ -92,7 +96,22 @@ __device__ __forceinline__ void cta_tile(const PixArgs& a, int k, int& m0, int& 
     len = min(a.npx, end - m0);
 }
 
-template <bool FP16>
+// Advances (k, c) to epilogue group grp's next chunk (chunks grp, grp+2, ...
+// of each tile in turn); false when the CTA has none left.
+__device__ __forceinline__ bool group_next(const PixArgs& a, int grp, int& k, int& c) {
+    c += 2;
+    while (k < a.tiles_per_cta) {
+        int m0, len;
+        cta_tile(a, k, m0, len);
+        if (len <= 0) return false;
+        if (c * kChunk < len) return true;
+        ++k;
+        c = grp;
+    }
+    return false;
+}
+
+template <bool FP16, bool HEAD>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3x3_pix_kernel(const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmX,
@@ -105,18 +124,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t slab_bytes = (uint32_t)a.slab_rows * 128u;
     uint8_t* wring = smem;                                   // kStages x 16 KB
     uint8_t* slab0 = wring + kStages * kWBytes;              // 2 slabs
-    float* st32 = reinterpret_cast<float*>(slab0 + 2 * slab_bytes);        // [2 groups][16][128]
-    uint16_t* st16 = reinterpret_cast<uint16_t*>(st32 + 2 * kChunk * kCo);  // [2][16][128]
-    float* stres = reinterpret_cast<float*>(st16 + 2 * kChunk * kCo);      // [2][16][128]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stres + 2 * kChunk * kCo);
+    // per epilogue warp: kRing fp32 slots and 2 16-bit slots of [16 px][32 ch]
+    float* ring32 = reinterpret_cast<float*>(slab0 + 2 * slab_bytes);
+    uint16_t* st16 = reinterpret_cast<uint16_t*>(ring32 + kEpiWarps * kRing * kSlot);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(st16 + kEpiWarps * 2 * kSlot);
     uint64_t* wfull = bars;
     uint64_t* wempty = bars + kStages;
     uint64_t* sfull = bars + 2 * kStages;
     uint64_t* sempty = sfull + 2;
     uint64_t* tfull = sempty + 2;
     uint64_t* tempty = tfull + 2;
-    uint64_t* rfull = tempty + 2;
-    uint64_t* done = rfull + 2;
+    uint64_t* rfull = tempty + 2;  // [kEpiWarps][kRing]
+    uint64_t* done = rfull + kEpiWarps * kRing;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     float* sbias = reinterpret_cast<float*>(tmem_slot + 4);  // [128]
     float* shead = sbias + kCo;                              // [3][128]
@@ -134,8 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&sempty[i]), 1);
             mbar_init(smem_u32(&tfull[i]), 1);
             mbar_init(smem_u32(&tempty[i]), 8);
-            mbar_init(smem_u32(&rfull[i]), 1);
         }
+        for (int i = 0; i < kEpiWarps * kRing; ++i) mbar_init(smem_u32(&rfull[i]), 1);
         mbar_init(smem_u32(done), 1);
         fence_barrier_init();
     }
@@ -172,6 +191,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int m0, len;
                 cta_tile(a, k, m0, len);
                 if (len <= 0) break;
+                if (a.res != nullptr && k > 0)
+                    // residual rows of this tile (read by its epilogue about a
+                    // tile later) into L2, one 8 KB chunk per prefetch
+                    for (int r = 0; r < len; r += kChunk)
+                        prefetch_l2(a.res + (size_t)(m0 + r) * kCo,
+                                    (uint32_t)min(kChunk, len - r) * kCo * 4u);
                 for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
                     const int sb = is & 1;
                     if (!mbar_wait(smem_u32(&sempty[sb]), ((is >> 1) & 1) ^ 1, a.err,
@@ -258,43 +283,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue (warps 2..9, two groups) ----------------
-        const int quarter = warp & 3;                   // channels [32*quarter, +32)
-        const int grp = (warp - 2) >> 2;                // chunks grp, grp+2, ...
-        const int gtid = ((warp - 2) & 3) * 32 + lane;  // 0..127 within the group
-        const bool leader = gtid == 0;
-        const int bar_a = 2 + 2 * grp, bar_b = 3 + 2 * grp;
+        // ---------------- epilogue (warps 2..9) ----------------
+        // Each warp finishes its 32 channels (its TMEM lanes) of every other
+        // chunk on its own: no barrier couples it to the other warps except
+        // in the head-projection layer, which sums over all 128 channels.
+        const int quarter = warp & 3;     // channels [32*quarter, +32)
+        const int ew = warp - 2;          // 0..7
+        const int par = ew >> 2;          // chunks par, par+2, ...
         const int co = quarter * 32 + lane;
         const float bias = sbias[co];
         const int hw = a.board * a.board;
-        auto chunks_of = [&](int len) { return (len + kChunk - 1) / kChunk; };
-        float* s32 = st32 + grp * (kChunk * kCo);
-        uint16_t* s16 = st16 + grp * (kChunk * kCo);
-        float* sres = stres + grp * (kChunk * kCo);
-        const uint32_t rbar = smem_u32(&rfull[grp]);
+        const bool has_res = a.res != nullptr;
         const bool store_out = (a.has_out32 | a.has_out16) != 0;
-        int rissued = 0;  // residual loads issued (leader)
-        {
+        float* ring = ring32 + ew * (kRing * kSlot);
+        uint16_t* s16w = st16 + ew * (2 * kSlot);
+        const uint32_t rbar0 = smem_u32(&rfull[ew * kRing]);
+        const int bar_a = 2 + 2 * par, bar_b = 3 + 2 * par;  // head layer only
+        // Residual loads run two chunks ahead of the chunk being finished.
+        // Load j goes to ring slot j % kRing; it is issued once the bulk store
+        // (or, in the head layer, the head sums) that last read that slot are
+        // done with it.
+        int lk = 0, lc = par - 2;  // position of the next residual load
+        bool lvalid = group_next(a, par, lk, lc);
+        int nissued = 0;
+        auto issue_load = [&]() {
+            if (!lvalid) return;
             int m0, len;
-            cta_tile(a, 0, m0, len);
-            if (a.has_res && leader && len > 0 && grp < chunks_of(len)) {
-                // residual of this group's first chunk of its first tile
-                mbar_arrive_expect_tx(rbar, kStage32);
-                tma_load_2d(smem_u32(sres), &tmR, rbar, 0, m0 + grp * kChunk);
-                ++rissued;
-            }
+            cta_tile(a, lk, m0, len);
+            const int b = nissued % kRing;
+            mbar_arrive_expect_tx(rbar0 + 8u * b, kSlot * 4);
+            tma_load_2d(smem_u32(ring + b * kSlot), &tmR, rbar0 + 8u * b, quarter * 32,
+                        m0 + lc * kChunk);
+            ++nissued;
+            lvalid = group_next(a, par, lk, lc);
+        };
+        if (has_res && lane == 0) {
+            issue_load();
+            issue_load();
         }
-        int rseq = 0;  // residual loads consumed
+        int i = 0;  // chunks finished by this warp
         int t = 0;
         bool ok = true;
         for (int k = 0; k < a.tiles_per_cta && ok; ++k, ++t) {
             int m0, len;
             cta_tile(a, k, m0, len);
             if (len <= 0) break;
-            const int nchunks = chunks_of(len);
+            const int nchunks = (len + kChunk - 1) / kChunk;
             const int acc = t & 1;
             ok = mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, a.err, kErrWaitEpilogue);
-            if (bar_any(bar_a, 128, !ok)) {
+            if (HEAD ? bar_any(bar_a, 128, !ok) : __any_sync(0xffffffffu, !ok)) {
                 ok = false;
                 break;
             }
@@ -302,8 +339,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tcol =
                 tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kMaxPx);
 #pragma unroll 1
-            for (int c = grp; c < nchunks; c += 2) {
+            for (int c = par; c < nchunks; c += 2, ++i) {
                 const int px0 = m0 + c * kChunk;
+                const int b = i % kRing;
+                float* buf = ring + b * kSlot;
+                uint16_t* s16 = s16w + (i & 1) * kSlot;
                 uint32_t v[16];
                 tmem_ld_16cols(tcol + (uint32_t)(c * kChunk), v);
                 // lanes 0..15 classify pixels px0 + lane
@@ -315,17 +355,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     onb = (y < a.board) && (q - y * a.rs < a.board);
                 }
                 const uint32_t board_mask = __ballot_sync(0xffffffffu, onb) & 0xffffu;
+                bool rok = true;
+                if (has_res) rok = mbar_wait(rbar0 + 8u * b, (i / kRing) & 1, a.err, kErrWaitEpilogue);
+                // In the head layer this barrier also keeps the slot's new
+                // values from being written before every warp of the group
+                // has finished the previous chunk's head sums.
+                if (HEAD ? bar_any(bar_b, 128, !rok) : __any_sync(0xffffffffu, !rok)) {
+                    ok = false;
+                    break;
+                }
                 float f[16];
                 tmem_ld_wait();
-                if (a.has_res) {
-                    const bool rok = mbar_wait(rbar, rseq & 1, a.err, kErrWaitEpilogue);
-                    ++rseq;
-                    if (bar_any(bar_b, 128, !rok)) {
-                        ok = false;
-                        break;
-                    }
+                if (has_res) {
 #pragma unroll
-                    for (int j = 0; j < kChunk; ++j) f[j] = sres[j * kCo + co];
+                    for (int j = 0; j < kChunk; ++j) f[j] = buf[j * 32 + lane];
                 } else {
 #pragma unroll
                     for (int j = 0; j < kChunk; ++j) f[j] = 0.f;
@@ -335,56 +378,49 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float x = __uint_as_float(v[j]) + bias + f[j];
                     f[j] = ((board_mask >> j) & 1) ? fmaxf(x, 0.f) : 0.f;
                 }
-                // The staging buffers and the residual buffer are free once the
-                // previous bulk store has read them and every thread of the
-                // group has read its residual.
-                if (leader && store_out) bulk_wait_read();
-                named_barrier_sync(bar_a, 128);
-                if (a.has_res && leader) {
-                    // Residual of this group's next chunk (this tile or the next).
-                    int nm0 = m0, nlen = len, nc = c + 2;
-                    if (nc >= nchunks) {
-                        cta_tile(a, k + 1, nm0, nlen);
-                        nc = grp;
-                        if (k + 1 >= a.tiles_per_cta) nlen = 0;
-                    }
-                    if (nlen > 0 && nc < chunks_of(nlen)) {
-                        mbar_arrive_expect_tx(rbar, kStage32);
-                        tma_load_2d(smem_u32(sres), &tmR, rbar, 0, nm0 + nc * kChunk);
-                        ++rissued;
-                    }
-                }
-                if (a.has_out32 || a.head_w != nullptr) {
+                if (HEAD || a.has_out32) {
 #pragma unroll
-                    for (int j = 0; j < kChunk; ++j) s32[j * kCo + co] = f[j];
+                    for (int j = 0; j < kChunk; ++j) buf[j * 32 + lane] = f[j];
                 }
                 if (a.has_out16) {
 #pragma unroll
-                    for (int j = 0; j < kChunk; ++j) s16[j * kCo + co] = to16<FP16>(f[j]);
+                    for (int j = 0; j < kChunk; ++j) s16[j * 32 + lane] = to16<FP16>(f[j]);
                 }
                 if (store_out) fence_proxy_async_smem();
-                named_barrier_sync(bar_b, 128);
-                if (store_out) {
-                    if (leader && px0 < a.m_total) {  // rows past the end are clipped
-                        if (a.has_out32) tma_store_2d(&tmO32, smem_u32(s32), 0, px0);
-                        if (a.has_out16) tma_store_2d(&tmO16, smem_u32(s16), 0, px0);
+                if (HEAD)
+                    named_barrier_sync(bar_a, 128);
+                else
+                    __syncwarp();
+                if (lane == 0) {
+                    if (store_out) {
+                        if (a.has_out32) tma_store_2d(&tmO32, smem_u32(buf), quarter * 32, px0);
+                        if (a.has_out16) tma_store_2d(&tmO16, smem_u32(s16), quarter * 32, px0);
                         bulk_commit();
+                        // the previous chunk's stores have read their slots
+                        bulk_wait_read_n<1>();
                     }
-                } else if (a.head_w != nullptr) {
-                    // Policy / value 1x1 convs of the 16 staged pixels: thread
-                    // (pixel gtid/8, channel segment gtid%8) sums 16 channels,
-                    // then the 8 segments of a pixel combine by shuffles.
-                    const int p = gtid >> 3, seg = gtid & 7;
-                    const float* row = s32 + p * kCo + seg * 16;
+                    if (has_res) issue_load();  // into the previous chunk's slot
+                }
+                __syncwarp();
+                if (HEAD) {
+                    // Policy / value 1x1 convs of the chunk's 16 pixels:
+                    // thread (pixel g/8, channel segment g%8) of the group
+                    // sums 16 channels, which sit in the slot of the warp
+                    // owning that channel quarter; the 8 segments of a pixel
+                    // combine by shuffles.
+                    const int g = ((warp - 2) & 3) * 32 + lane;
+                    const int p = g >> 3, seg = g & 7, sq = seg >> 1;
+                    const float* row = ring32 + (par * 4 + ((sq + 2) & 3)) * (kRing * kSlot) +
+                                       b * kSlot + p * 32 + (seg & 1) * 16;
                     const float* hw0 = shead + seg * 16;
                     float d0 = 0.f, d1 = 0.f, d2 = 0.f;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int k = (i + 2 * seg) & 15;  // rotate to spread banks
-                        const float xv = row[k];
-                        d0 = fmaf(xv, hw0[k], d0);
-                        d1 = fmaf(xv, hw0[kCo + k], d1);
-                        d2 = fmaf(xv, hw0[2 * kCo + k], d2);
+                    for (int q = 0; q < 16; ++q) {
+                        const int kq = (q + 4 * sq + (p & 3)) & 15;  // spread banks
+                        const float xv = row[kq];
+                        d0 = fmaf(xv, hw0[kq], d0);
+                        d1 = fmaf(xv, hw0[kCo + kq], d1);
+                        d2 = fmaf(xv, hw0[2 * kCo + kq], d2);
                     }
 #pragma unroll
                     for (int o = 1; o < 8; o <<= 1) {
@@ -393,10 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         d2 += __shfl_xor_sync(0xffffffffu, d2, o);
                     }
                     if (seg == 0 && ((board_mask >> p) & 1)) {
-                        const int m = px0 + p;
-                        const int pos = m / a.is;
-                        const int q = m - pos * a.is;
-                        const int y = q / a.rs, x = q - y * a.rs;
+                        const int mp = px0 + p;
+                        const int pos = mp / a.is;
+                        const int qq = mp - pos * a.is;
+                        const int y = qq / a.rs, x = qq - y * a.rs;
                         float* fr = a.feat + (size_t)pos * 3 * hw + y * a.board + x;
                         fr[0] = fmaxf(d0 + a.head_b[0], 0.f);
                         fr[hw] = fmaxf(d1 + a.head_b[1], 0.f);
@@ -408,11 +444,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
         }
-        if (leader) {
+        if (lane == 0) {
             // Every bulk store complete and every issued residual load landed
             // before the CTA's shared memory is released.
             if (store_out) bulk_wait_all();
-            for (int j = rseq; j < rissued; ++j) mbar_wait(rbar, j & 1, a.err, kErrWaitDrain);
+            for (int j = i; j < nissued; ++j)
+                mbar_wait(rbar0 + 8u * (j % kRing), (j / kRing) & 1, a.err, kErrWaitDrain);
         }
     }
 
@@ -431,8 +468,8 @@ int slab_rows_for(int npx, int rs) {
 
 size_t pix_smem_bytes(int npx, int rs) {
     const size_t slab = (size_t)slab_rows_for(npx, rs) * 128;
-    return (size_t)kStages * kWBytes + 2 * slab + 2 * (kStage32 + kStage16 + kStage32) +
-           (2 * kStages + 11) * 8 + 16 + (kCo + 3 * kCo) * 4 + 1024;
+    return (size_t)kStages * kWBytes + 2 * slab + kEpiWarps * (kRing * kSlot * 4 + 2 * kSlot * 2) +
+           (2 * kStages + 8 + kEpiWarps * kRing + 1) * 8 + 16 + (kCo + 3 * kCo) * 4 + 1024;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -466,11 +503,15 @@ bool encode(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* bas
 
 cudaError_t configure_conv_pix() {
     const int smem = 227 * 1024;
-    cudaError_t e = cudaFuncSetAttribute(conv3x3_pix_kernel<false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(conv3x3_pix_kernel<true>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    const void* fns[4] = {(const void*)conv3x3_pix_kernel<false, false>,
+                          (const void*)conv3x3_pix_kernel<false, true>,
+                          (const void*)conv3x3_pix_kernel<true, false>,
+                          (const void*)conv3x3_pix_kernel<true, true>};
+    for (const void* f : fns) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 bool conv_pix_supported(const ConvLayer& L, int npx) {
@@ -500,9 +541,9 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
     a.is = L.g.is;
     a.board = L.g.board;
     a.slab_rows = slab_rows_for(npx, L.g.rs);
-    a.has_res = L.res32 != nullptr;
     a.has_out32 = L.out32 != nullptr;
     a.has_out16 = L.out16 != nullptr;
+    a.res = L.res32;
     a.bias = L.bias;
     a.head_w = L.head_w;
     a.head_b = L.head_b;
@@ -521,11 +562,12 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode(&tmX, t16, 2, L.in, (uint64_t)L.cin, rows, kBK, (uint32_t)(a.slab_rows / 2),
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode(&tmR, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, r, kCo, L.res32 ? rows : kChunk, kCo,
+        // epilogue boxes: one warp's 32 channels x 16 pixels
+        !encode(&tmR, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, r, kCo, L.res32 ? rows : kChunk, 32,
                 kChunk, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&tmO32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, o32, kCo, L.out32 ? rows : kChunk, kCo,
+        !encode(&tmO32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, o32, kCo, L.out32 ? rows : kChunk, 32,
                 kChunk, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&tmO16, t16, 2, o16, kCo, L.out16 ? rows : kChunk, kCo, kChunk,
+        !encode(&tmO16, t16, 2, o16, kCo, L.out16 ? rows : kChunk, 32, kChunk,
                 CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     // Programmatic dependent launch: this kernel's CTAs may start (and run
@@ -541,9 +583,10 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (fp16)
-        return cudaLaunchKernelEx(&cfg, conv3x3_pix_kernel<true>, tmW, tmX, tmR, tmO32, tmO16, a);
-    return cudaLaunchKernelEx(&cfg, conv3x3_pix_kernel<false>, tmW, tmX, tmR, tmO32, tmO16, a);
+    const bool head = L.head_w != nullptr;
+    auto fn = fp16 ? (head ? conv3x3_pix_kernel<true, true> : conv3x3_pix_kernel<true, false>)
+                   : (head ? conv3x3_pix_kernel<false, true> : conv3x3_pix_kernel<false, false>);
+    return cudaLaunchKernelEx(&cfg, fn, tmW, tmX, tmR, tmO32, tmO16, a);
 }
 
 }  // namespace mgb

@@ -140,6 +140,12 @@ __device__ __forceinline__ void bulk_commit() {
 __device__ __forceinline__ void bulk_wait_read() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// Waits until at most N of the most recently committed bulk groups still
+// read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read_n() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 
 // Waits until every committed bulk store has completed.
 __device__ __forceinline__ void bulk_wait_all() {
