@@ -16,19 +16,20 @@
 //
 // The accumulator is [co lanes][px columns] in TMEM, double-buffered across
 // tiles (2 x 256 columns).  The epilogue moves activations only through
-// TMA.  Each epilogue group owns a ring of three 16-pixel fp32 chunk buffers:
-// the residual rows of a chunk arrive there by a TMA load issued two chunks
-// ahead (and the producer prefetches each tile's residual rows into L2 a
-// tile ahead), each thread (= one channel) adds bias and residual, applies
-// ReLU and the frame mask, and writes the fp32 result back into the same
-// buffer, which a TMA bulk store then copies out; 16-bit results go through
-// a second, double-buffered staging area.  In the last trunk layer the
-// staged chunk instead feeds the policy / value 1x1 head projection.
+// TMA, and each epilogue warp works on its own: it owns 32 channels (its TMEM
+// lanes) of every other 16-pixel chunk and a ring of four 2 KB chunk slots.
+// The residual stream is a pair of 16-bit planes, x = hi + lo with hi = x
+// rounded to the operand type (the next layer's input) and lo = x - hi
+// rounded to fp16.  A chunk's residual hi / lo rows arrive in its slot by TMA
+// loads issued three chunks ahead (the producer also prefetches each tile's
+// residual rows into L2 a tile ahead); each thread (= one channel) adds bias
+// and residual, applies ReLU and the frame mask, re-splits the sum into hi
+// and lo in place, and TMA bulk stores copy the slot out.  In the last trunk
+// layer the fp32 sums feed the policy / value 1x1 head projection instead.
 //
 // Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
-// issuer, warps 2-9 epilogue in two groups of four (group g takes chunks
-// g, g+2, ...; warp w of a group reads TMEM lanes [32*(w%4), +32)).  All
-// waits are bounded.
+// issuer, warps 2-9 epilogue (warp w reads TMEM lanes [32*(w%4), +32) of
+// chunks (w-2)/4, (w-2)/4 + 2, ...).  All waits are bounded.
 //
 // Work split: CTA b owns the contiguous pixel range [b*span, (b+1)*span),
 // cut into equal tiles of at most 256 pixels, so every SM gets the same
@@ -51,10 +52,13 @@ constexpr int kMaxPx = 256;     // MMA N limit
 constexpr int kStages = 5;      // weight ring depth
 constexpr int kThreads = 320;
 constexpr int kChunk = 16;      // pixels per epilogue chunk
-constexpr int kRing = 3;        // fp32 chunk slots per epilogue warp
+constexpr int kRing = 4;        // chunk slots per epilogue warp
 constexpr uint32_t kWBytes = kCo * kBK * 2;            // 16 KB weight stage
 constexpr int kSlot = kChunk * 32;  // one warp's chunk: 16 pixels x 32 channels
+constexpr int kHalf = kSlot * 2;    // bytes of one 16-bit plane of a chunk
+constexpr int kSlotBytes = kSlot * 4;  // a slot: hi + lo planes, or fp32 sums
 constexpr int kEpiWarps = 8;
+constexpr int kMagicShift = 40;     // n / d == (n * ceil(2^40 / d)) >> 40 here
 
 struct PixArgs {
     int m_total;
@@ -64,8 +68,10 @@ struct PixArgs {
     int cin;
     int rs, is, board;
     int slab_rows;  // rows per slab (multiple of 16)
-    int has_out32, has_out16;
-    const float* res;     // fp32 residual [m_total][128] or nullptr
+    uint64_t is_magic, rs_magic;  // ceil(2^40 / is), ceil(2^40 / rs)
+    int has_out16, has_out_lo;
+    const uint16_t* res_hi;  // residual stream [m_total][128] hi plane or nullptr
+    const uint16_t* res_lo;  // and its fp16 remainder plane
     const float* bias;
     const float* head_w;  // [3][128] or nullptr (fused head projection)
     const float* head_b;
@@ -84,6 +90,24 @@ template <>
 __device__ __forceinline__ uint16_t to16<true>(float v) {
     __half h = __float2half_rn(v);
     return *reinterpret_cast<uint16_t*>(&h);
+}
+
+template <bool FP16>
+__device__ __forceinline__ float from16(uint16_t h);
+template <>
+__device__ __forceinline__ float from16<false>(uint16_t h) {
+    return __uint_as_float((uint32_t)h << 16);
+}
+template <>
+__device__ __forceinline__ float from16<true>(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+__device__ __forceinline__ float lo_value(uint16_t l) { return __half2float(__ushort_as_half(l)); }
+__device__ __forceinline__ uint16_t lo_bits(float r) { return __half_as_ushort(__float2half_rn(r)); }
+
+// n / d for 0 <= n < 2^23 and d <= 1200 (the launcher checks both).
+__device__ __forceinline__ int div_magic(int n, uint64_t magic) {
+    return (int)(((uint64_t)(uint32_t)n * magic) >> kMagicShift);
 }
 
 // Tile k of this CTA's contiguous pixel range: rows [m0, m0 + len);
@@ -115,19 +139,18 @@ template <bool FP16, bool HEAD>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3x3_pix_kernel(const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmX,
-                       const __grid_constant__ CUtensorMap tmR,
-                       const __grid_constant__ CUtensorMap tmO32,
-                       const __grid_constant__ CUtensorMap tmO16, const PixArgs a) {
+                       const __grid_constant__ CUtensorMap tmRh,
+                       const __grid_constant__ CUtensorMap tmRl,
+                       const __grid_constant__ CUtensorMap tmOh,
+                       const __grid_constant__ CUtensorMap tmOl, const PixArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t slab_bytes = (uint32_t)a.slab_rows * 128u;
     uint8_t* wring = smem;                                   // kStages x 16 KB
     uint8_t* slab0 = wring + kStages * kWBytes;              // 2 slabs
-    // per epilogue warp: kRing fp32 slots and 2 16-bit slots of [16 px][32 ch]
-    float* ring32 = reinterpret_cast<float*>(slab0 + 2 * slab_bytes);
-    uint16_t* st16 = reinterpret_cast<uint16_t*>(ring32 + kEpiWarps * kRing * kSlot);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(st16 + kEpiWarps * 2 * kSlot);
+    uint8_t* ring0 = slab0 + 2 * slab_bytes;                 // [kEpiWarps][kRing] slots
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring0 + kEpiWarps * kRing * kSlotBytes);
     uint64_t* wfull = bars;
     uint64_t* wempty = bars + kStages;
     uint64_t* sfull = bars + 2 * kStages;
@@ -191,12 +214,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int m0, len;
                 cta_tile(a, k, m0, len);
                 if (len <= 0) break;
-                if (a.res != nullptr && k > 0)
+                if (a.res_hi != nullptr && k > 0)
                     // residual rows of this tile (read by its epilogue about a
-                    // tile later) into L2, one 8 KB chunk per prefetch
-                    for (int r = 0; r < len; r += kChunk)
-                        prefetch_l2(a.res + (size_t)(m0 + r) * kCo,
-                                    (uint32_t)min(kChunk, len - r) * kCo * 4u);
+                    // tile later) into L2, one 4 KB chunk per prefetch
+                    for (int r = 0; r < len; r += kChunk) {
+                        const uint32_t bytes = (uint32_t)min(kChunk, len - r) * kCo * 2u;
+                        prefetch_l2(a.res_hi + (size_t)(m0 + r) * kCo, bytes);
+                        prefetch_l2(a.res_lo + (size_t)(m0 + r) * kCo, bytes);
+                    }
                 for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
                     const int sb = is & 1;
                     if (!mbar_wait(smem_u32(&sempty[sb]), ((is >> 1) & 1) ^ 1, a.err,
@@ -287,22 +312,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Each warp finishes its 32 channels (its TMEM lanes) of every other
         // chunk on its own: no barrier couples it to the other warps except
         // in the head-projection layer, which sums over all 128 channels.
-        const int quarter = warp & 3;     // channels [32*quarter, +32)
-        const int ew = warp - 2;          // 0..7
-        const int par = ew >> 2;          // chunks par, par+2, ...
+        const int quarter = warp & 3;  // channels [32*quarter, +32)
+        const int ew = warp - 2;       // 0..7
+        const int par = ew >> 2;       // chunks par, par+2, ...
         const int co = quarter * 32 + lane;
         const float bias = sbias[co];
         const int hw = a.board * a.board;
-        const bool has_res = a.res != nullptr;
-        const bool store_out = (a.has_out32 | a.has_out16) != 0;
-        float* ring = ring32 + ew * (kRing * kSlot);
-        uint16_t* s16w = st16 + ew * (2 * kSlot);
+        const bool has_res = a.res_hi != nullptr;
+        const bool store_out = a.has_out16 != 0;
+        uint8_t* ring = ring0 + ew * (kRing * kSlotBytes);
         const uint32_t rbar0 = smem_u32(&rfull[ew * kRing]);
         const int bar_a = 2 + 2 * par, bar_b = 3 + 2 * par;  // head layer only
-        // Residual loads run two chunks ahead of the chunk being finished.
-        // Load j goes to ring slot j % kRing; it is issued once the bulk store
-        // (or, in the head layer, the head sums) that last read that slot are
-        // done with it.
+        // Residual loads run kRing - 1 chunks ahead of the chunk being
+        // finished.  Load j goes to slot j % kRing; it is issued once the bulk
+        // stores (or, in the head layer, the head sums) that last read that
+        // slot are done with it.
         int lk = 0, lc = par - 2;  // position of the next residual load
         bool lvalid = group_next(a, par, lk, lc);
         int nissued = 0;
@@ -311,16 +335,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             int m0, len;
             cta_tile(a, lk, m0, len);
             const int b = nissued % kRing;
-            mbar_arrive_expect_tx(rbar0 + 8u * b, kSlot * 4);
-            tma_load_2d(smem_u32(ring + b * kSlot), &tmR, rbar0 + 8u * b, quarter * 32,
-                        m0 + lc * kChunk);
+            const uint32_t bar = rbar0 + 8u * b;
+            const uint32_t dst = smem_u32(ring + b * kSlotBytes);
+            mbar_arrive_expect_tx(bar, 2 * kHalf);
+            tma_load_2d(dst, &tmRh, bar, quarter * 32, m0 + lc * kChunk);
+            tma_load_2d(dst + kHalf, &tmRl, bar, quarter * 32, m0 + lc * kChunk);
             ++nissued;
             lvalid = group_next(a, par, lk, lc);
         };
-        if (has_res && lane == 0) {
-            issue_load();
-            issue_load();
-        }
+        if (has_res && lane == 0)
+            for (int j = 0; j < kRing - 1; ++j) issue_load();
         int i = 0;  // chunks finished by this warp
         int t = 0;
         bool ok = true;
@@ -342,49 +366,57 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = par; c < nchunks; c += 2, ++i) {
                 const int px0 = m0 + c * kChunk;
                 const int b = i % kRing;
-                float* buf = ring + b * kSlot;
-                uint16_t* s16 = s16w + (i & 1) * kSlot;
+                uint8_t* slot = ring + b * kSlotBytes;
+                uint16_t* shi = reinterpret_cast<uint16_t*>(slot);
+                uint16_t* slo = reinterpret_cast<uint16_t*>(slot + kHalf);
                 uint32_t v[16];
                 tmem_ld_16cols(tcol + (uint32_t)(c * kChunk), v);
                 // lanes 0..15 classify pixels px0 + lane
-                const int mj = px0 + (lane & 15);
                 bool onb = false;
                 if (c * kChunk + (lane & 15) < len) {
-                    const int q = mj % a.is;
-                    const int y = q / a.rs;
+                    const int mj = px0 + (lane & 15);
+                    const int q = mj - div_magic(mj, a.is_magic) * a.is;
+                    const int y = div_magic(q, a.rs_magic);
                     onb = (y < a.board) && (q - y * a.rs < a.board);
                 }
                 const uint32_t board_mask = __ballot_sync(0xffffffffu, onb) & 0xffffu;
                 bool rok = true;
                 if (has_res) rok = mbar_wait(rbar0 + 8u * b, (i / kRing) & 1, a.err, kErrWaitEpilogue);
-                // In the head layer this barrier also keeps the slot's new
-                // values from being written before every warp of the group
-                // has finished the previous chunk's head sums.
+                // In the head layer this barrier also keeps the slot from being
+                // rewritten before every warp of the group has finished the
+                // previous chunk's head sums.
                 if (HEAD ? bar_any(bar_b, 128, !rok) : __any_sync(0xffffffffu, !rok)) {
                     ok = false;
                     break;
                 }
                 float f[16];
-                tmem_ld_wait();
                 if (has_res) {
 #pragma unroll
-                    for (int j = 0; j < kChunk; ++j) f[j] = buf[j * 32 + lane];
+                    for (int j = 0; j < kChunk; ++j)
+                        f[j] = from16<FP16>(shi[j * 32 + lane]) + lo_value(slo[j * 32 + lane]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < kChunk; ++j) f[j] = 0.f;
                 }
+                tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < kChunk; ++j) {
                     const float x = __uint_as_float(v[j]) + bias + f[j];
                     f[j] = ((board_mask >> j) & 1) ? fmaxf(x, 0.f) : 0.f;
                 }
-                if (HEAD || a.has_out32) {
+                if (HEAD) {
+                    // fp32 sums for the head projection, over the whole slot
+                    __syncwarp();
+                    float* s32 = reinterpret_cast<float*>(slot);
 #pragma unroll
-                    for (int j = 0; j < kChunk; ++j) buf[j * 32 + lane] = f[j];
-                }
-                if (a.has_out16) {
+                    for (int j = 0; j < kChunk; ++j) s32[j * 32 + lane] = f[j];
+                } else {
 #pragma unroll
-                    for (int j = 0; j < kChunk; ++j) s16[j * 32 + lane] = to16<FP16>(f[j]);
+                    for (int j = 0; j < kChunk; ++j) {
+                        const uint16_t h = to16<FP16>(f[j]);
+                        shi[j * 32 + lane] = h;
+                        if (a.has_out_lo) slo[j * 32 + lane] = lo_bits(f[j] - from16<FP16>(h));
+                    }
                 }
                 if (store_out) fence_proxy_async_smem();
                 if (HEAD)
@@ -393,10 +425,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                 if (lane == 0) {
                     if (store_out) {
-                        if (a.has_out32) tma_store_2d(&tmO32, smem_u32(buf), quarter * 32, px0);
-                        if (a.has_out16) tma_store_2d(&tmO16, smem_u32(s16), quarter * 32, px0);
+                        tma_store_2d(&tmOh, smem_u32(shi), quarter * 32, px0);
+                        if (a.has_out_lo) tma_store_2d(&tmOl, smem_u32(slo), quarter * 32, px0);
                         bulk_commit();
-                        // the previous chunk's stores have read their slots
+                        // the previous chunk's stores have read their slot
                         bulk_wait_read_n<1>();
                     }
                     if (has_res) issue_load();  // into the previous chunk's slot
@@ -410,8 +442,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // combine by shuffles.
                     const int g = ((warp - 2) & 3) * 32 + lane;
                     const int p = g >> 3, seg = g & 7, sq = seg >> 1;
-                    const float* row = ring32 + (par * 4 + ((sq + 2) & 3)) * (kRing * kSlot) +
-                                       b * kSlot + p * 32 + (seg & 1) * 16;
+                    const float* row =
+                        reinterpret_cast<const float*>(
+                            ring0 + (par * 4 + ((sq + 2) & 3)) * (kRing * kSlotBytes) +
+                            b * kSlotBytes) +
+                        p * 32 + (seg & 1) * 16;
                     const float* hw0 = shead + seg * 16;
                     float d0 = 0.f, d1 = 0.f, d2 = 0.f;
 #pragma unroll
@@ -430,9 +465,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (seg == 0 && ((board_mask >> p) & 1)) {
                         const int mp = px0 + p;
-                        const int pos = mp / a.is;
+                        const int pos = div_magic(mp, a.is_magic);
                         const int qq = mp - pos * a.is;
-                        const int y = qq / a.rs, x = qq - y * a.rs;
+                        const int y = div_magic(qq, a.rs_magic), x = qq - y * a.rs;
                         float* fr = a.feat + (size_t)pos * 3 * hw + y * a.board + x;
                         fr[0] = fmaxf(d0 + a.head_b[0], 0.f);
                         fr[hw] = fmaxf(d1 + a.head_b[1], 0.f);
@@ -468,7 +503,7 @@ int slab_rows_for(int npx, int rs) {
 
 size_t pix_smem_bytes(int npx, int rs) {
     const size_t slab = (size_t)slab_rows_for(npx, rs) * 128;
-    return (size_t)kStages * kWBytes + 2 * slab + kEpiWarps * (kRing * kSlot * 4 + 2 * kSlot * 2) +
+    return (size_t)kStages * kWBytes + 2 * slab + (size_t)kEpiWarps * kRing * kSlotBytes +
            (2 * kStages + 8 + kEpiWarps * kRing + 1) * 8 + 16 + (kCo + 3 * kCo) * 4 + 1024;
 }
 
@@ -515,8 +550,12 @@ cudaError_t configure_conv_pix() {
 }
 
 bool conv_pix_supported(const ConvLayer& L, int npx) {
+    // The residual stream is the hi / lo pair; fp32 residuals are not read.
     return L.cout == kCo && L.cin % kBK == 0 && npx % kChunk == 0 && npx >= 16 &&
-           npx <= kMaxPx && pix_smem_bytes(npx, L.g.rs) <= 227 * 1024;
+           npx <= kMaxPx && pix_smem_bytes(npx, L.g.rs) <= 227 * 1024 && L.res32 == nullptr &&
+           L.out32 == nullptr && (L.res_hi == nullptr) == (L.res_lo == nullptr) &&
+           (L.out_lo == nullptr || L.out16 != nullptr) && L.g.is <= 1200 &&
+           L.m_total < (1 << 23) - 2 * kMaxPx;
 }
 
 cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid_limit,
@@ -541,9 +580,12 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
     a.is = L.g.is;
     a.board = L.g.board;
     a.slab_rows = slab_rows_for(npx, L.g.rs);
-    a.has_out32 = L.out32 != nullptr;
+    a.is_magic = ((1ull << kMagicShift) + (uint64_t)L.g.is - 1) / (uint64_t)L.g.is;
+    a.rs_magic = ((1ull << kMagicShift) + (uint64_t)L.g.rs - 1) / (uint64_t)L.g.rs;
     a.has_out16 = L.out16 != nullptr;
-    a.res = L.res32;
+    a.has_out_lo = L.out_lo != nullptr;
+    a.res_hi = static_cast<const uint16_t*>(L.res_hi);
+    a.res_lo = L.res_lo;
     a.bias = L.bias;
     a.head_w = L.head_w;
     a.head_b = L.head_b;
@@ -551,23 +593,26 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
     a.err = L.err;
     const CUtensorMapDataType t16 =
         fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    CUtensorMap tmW, tmX, tmR, tmO32, tmO16;
+    const CUtensorMapDataType tlo = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap tmW, tmX, tmRh, tmRl, tmOh, tmOl;
     // Epilogue maps of absent buffers describe a valid dummy (the first 16
     // rows' worth of the weight buffer, at least 147 KB) and are never used.
-    const void* r = L.res32 ? (const void*)L.res32 : L.weight;
-    const void* o32 = L.out32 ? (const void*)L.out32 : L.weight;
-    const void* o16 = L.out16 ? (const void*)L.out16 : L.weight;
+    auto or_dummy = [&](const void* p) { return p ? p : L.weight; };
     const uint64_t rows = (uint64_t)L.m_total;
+    const uint64_t rrows = L.res_hi ? rows : kChunk, orows = L.out16 ? rows : kChunk,
+                   lrows = L.out_lo ? rows : kChunk;
     if (!encode(&tmW, t16, 2, L.weight, (uint64_t)9 * L.cin, (uint64_t)kCo, kBK, kCo,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode(&tmX, t16, 2, L.in, (uint64_t)L.cin, rows, kBK, (uint32_t)(a.slab_rows / 2),
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
         // epilogue boxes: one warp's 32 channels x 16 pixels
-        !encode(&tmR, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, r, kCo, L.res32 ? rows : kChunk, 32,
-                kChunk, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&tmO32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, o32, kCo, L.out32 ? rows : kChunk, 32,
-                kChunk, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&tmO16, t16, 2, o16, kCo, L.out16 ? rows : kChunk, 32, kChunk,
+        !encode(&tmRh, t16, 2, or_dummy(L.res_hi), kCo, rrows, 32, kChunk,
+                CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(&tmRl, tlo, 2, or_dummy(L.res_lo), kCo, rrows, 32, kChunk,
+                CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(&tmOh, t16, 2, or_dummy(L.out16), kCo, orows, 32, kChunk,
+                CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(&tmOl, tlo, 2, or_dummy(L.out_lo), kCo, lrows, 32, kChunk,
                 CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     // Programmatic dependent launch: this kernel's CTAs may start (and run
@@ -586,7 +631,7 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
     const bool head = L.head_w != nullptr;
     auto fn = fp16 ? (head ? conv3x3_pix_kernel<true, true> : conv3x3_pix_kernel<true, false>)
                    : (head ? conv3x3_pix_kernel<false, true> : conv3x3_pix_kernel<false, false>);
-    return cudaLaunchKernelEx(&cfg, fn, tmW, tmX, tmR, tmO32, tmO16, a);
+    return cudaLaunchKernelEx(&cfg, fn, tmW, tmX, tmRh, tmRl, tmOh, tmOl, a);
 }
 
 }  // namespace mgb

@@ -112,6 +112,8 @@ struct mg_engine {
     void* d_stage = nullptr;  // staged input rows, operand type
     float* d_x = nullptr;     // fp32 residual stream
     void* d_x16 = nullptr;    // 16-bit copy of d_x (tensor-core operand)
+    // The 128-channel 16-bit path keeps the residual stream as d_x16 (hi) plus
+    // an fp16 remainder plane (lo), which lives in d_x's storage there.
     void* d_t = nullptr;      // block-internal activation, operand type
     float* d_feat = nullptr;  // head features [positions][3*hw]
     float* d_fc = nullptr;    // FC outputs [positions][actions + hidden]
@@ -409,6 +411,27 @@ struct mg_engine {
         return use_pix() || choose_bn(bucket * g.is) == cpad;
     }
 
+    // Buffers of layer li on the 128-channel 16-bit path, whose residual
+    // stream is the pair (hi, lo): input conv stage -> (hi, lo); conv1 of a
+    // block hi -> t; conv2 t + (hi, lo) -> (hi, lo) in place.
+    void wire_pix_layer(ConvLayer& L, int li, const void* stage, void* hi, uint16_t* lo,
+                        void* t) const {
+        if (li == 0) {
+            L.in = stage;
+            L.out16 = hi;
+            L.out_lo = lo;
+        } else if (li % 2 == 1) {
+            L.in = hi;
+            L.out16 = t;
+        } else {
+            L.in = t;
+            L.res_hi = hi;
+            L.res_lo = lo;
+            L.out16 = hi;
+            L.out_lo = lo;
+        }
+    }
+
     ConvLayer layer_desc(int li, int bucket) const {
         ConvLayer L{};
         L.m_total = bucket * g.is;
@@ -419,7 +442,9 @@ struct mg_engine {
         L.err = d_err;
         const bool f32 = precision == MG_PREC_FP32;
         L.weight = f32 ? (const void*)d_w32[li] : (const void*)d_w16[li];
-        if (li == 0) {  // input conv: staged planes -> x
+        if (use_pix()) {
+            wire_pix_layer(L, li, d_stage, d_x16, reinterpret_cast<uint16_t*>(d_x), d_t);
+        } else if (li == 0) {  // input conv: staged planes -> x
             L.in = d_stage;
             L.out32 = d_x;
             L.out16 = f32 ? nullptr : d_x16;
@@ -437,6 +462,7 @@ struct mg_engine {
             // The trunk output is consumed only by the heads.
             L.out32 = nullptr;
             L.out16 = nullptr;
+            L.out_lo = nullptr;
             L.head_w = d_head_w;
             L.head_b = d_head_b;
             L.feat = d_feat;
@@ -955,7 +981,7 @@ cudaError_t noalloc_arena(int dev, void** out) {
 // bytes needed (which may exceed the arena, in which case nothing is set).
 struct NoAllocBuffers {
     void* stage;
-    float* x32;
+    float* x32;  // fp32 residual stream (its fp16 remainder plane on the 128-channel path)
     void* x16;
     void* t;
     float* feat;
@@ -1038,7 +1064,9 @@ extern "C" int mg_forward_device_noalloc(mg_engine* e, const float* d_states, in
             L.bias = e->d_bias[li];
             L.err = b.err;
             L.weight = f32 ? (const void*)e->d_w32[li] : (const void*)e->d_w16[li];
-            if (li == 0) {
+            if (e->use_pix()) {
+                e->wire_pix_layer(L, li, b.stage, b.x16, reinterpret_cast<uint16_t*>(b.x32), b.t);
+            } else if (li == 0) {
                 L.in = b.stage;
                 L.out32 = b.x32;
                 L.out16 = f32 ? nullptr : b.x16;
@@ -1055,6 +1083,7 @@ extern "C" int mg_forward_device_noalloc(mg_engine* e, const float* d_states, in
             if (li == e->n_convs - 1 && fused) {
                 L.out32 = nullptr;
                 L.out16 = nullptr;
+                L.out_lo = nullptr;
                 L.head_w = e->d_head_w;
                 L.head_b = e->d_head_b;
                 L.feat = b.feat;

@@ -38,7 +38,10 @@ inline FrameGeom make_frame(int board) {
 //   y[r, co] = 0                                     on frame pixels,
 // written as fp32 to out32 and/or as the 16-bit operand type to out16.
 // The residual stream is kept in fp32 (res32 / out32) so 16-bit rounding
-// enters only through the tensor-core operands, not the running sum.
+// enters only through the tensor-core operands, not the running sum.  The
+// 128-channel kernel keeps it instead as a 16-bit pair (res_hi + res_lo ->
+// out16 + out_lo, below): about 20 significant bits in 4 bytes, of which the
+// hi half is at once the next layer's operand.
 //
 // Optional fused head projection (tensor-core path, when one tile spans all
 // output channels): for each board pixel p of position n,
@@ -58,6 +61,12 @@ struct ConvLayer {
     const float* res32;     // [m_total][cout] fp32 or nullptr (may equal out32)
     float* out32;           // [m_total][cout] fp32 or nullptr
     void* out16;            // [m_total][cout] 16-bit or nullptr (tensor-core path)
+    // Residual stream as a 16-bit pair (128-channel kernel only): x = hi + lo,
+    // hi = x rounded to the operand type (the next layer reads it as its
+    // input), lo = the remainder x - hi rounded to fp16.
+    const void* res_hi;     // [m_total][cout] operand type or nullptr (may equal out16)
+    const uint16_t* res_lo; // [m_total][cout] fp16 (may equal out_lo)
+    uint16_t* out_lo;       // [m_total][cout] fp16 remainder of out16, or nullptr
     const float* head_w;    // [3][cout] or nullptr: fused head projection
     const float* head_b;    // [3]
     float* feat;            // [positions][3*B*B]
