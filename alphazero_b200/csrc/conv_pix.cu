@@ -15,21 +15,22 @@
 // Weight K blocks (128 x 64) stream through a 5-deep ring.
 //
 // The accumulator is [co lanes][px columns] in TMEM, double-buffered across
-// tiles (2 x 256 columns).  The epilogue moves activations only through
-// TMA, and each epilogue warp works on its own: it owns 32 channels (its TMEM
-// lanes) of every other 16-pixel chunk and a ring of four 2 KB chunk slots.
-// The residual stream is a pair of 16-bit planes, x = hi + lo with hi = x
+// tiles (2 x 256 columns).  Each epilogue warp works on its own: it owns 32
+// channels (its TMEM lanes) of every other 16-pixel chunk and moves them
+// straight between registers and global memory (lane = channel, so each
+// 16-bit access of a warp covers 64 contiguous bytes of a pixel row).  The
+// residual stream is a pair of 16-bit planes, x = hi + lo with hi = x
 // rounded to the operand type (the next layer's input) and lo = x - hi
-// rounded to fp16.  A chunk's residual hi / lo rows arrive in its slot by TMA
-// loads issued three chunks ahead (the producer also prefetches each tile's
-// residual rows into L2 a tile ahead); each thread (= one channel) adds bias
-// and residual, applies ReLU and the frame mask, re-splits the sum into hi
-// and lo in place, and TMA bulk stores copy the slot out.  In the last trunk
-// layer the fp32 sums feed the policy / value 1x1 head projection instead.
+// rounded to fp16.  A chunk's residual hi / lo values are loaded one chunk
+// ahead into registers; each thread adds bias and residual, applies
+// ReLU and the frame mask, and stores the sum re-split into hi and lo.  In
+// the last trunk layer the fp32 sums go through shared memory to the
+// policy / value 1x1 head projection instead.
 //
-// Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
-// issuer, warps 2-9 epilogue (warp w reads TMEM lanes [32*(w%4), +32) of
-// chunks (w-2)/4, (w-2)/4 + 2, ...).  All waits are bounded.
+// Warp roles (352 threads): warp 0 weight TMA producer, warp 1 TMEM
+// allocator + MMA issuer, warps 2-9 epilogue (warp w reads TMEM lanes
+// [32*(w%4), +32) of chunks (w-2)/4, (w-2)/4 + 2, ...), warp 10 activation
+// slab TMA producer (two slab buffers).  All waits are bounded.
 //
 // Work split: CTA b owns the contiguous pixel range [b*span, (b+1)*span),
 // cut into equal tiles of at most 256 pixels, so every SM gets the same
@@ -50,13 +51,11 @@ constexpr int kCo = 128;        // output channels (MMA M)
 constexpr int kBK = 64;         // K per stage / slab channel block
 constexpr int kMaxPx = 256;     // MMA N limit
 constexpr int kStages = 5;      // weight ring depth
-constexpr int kThreads = 320;
+constexpr int kSlabs = 2;       // activation slab ring depth
+constexpr int kThreads = 352;
 constexpr int kChunk = 16;      // pixels per epilogue chunk
-constexpr int kRing = 4;        // chunk slots per epilogue warp
 constexpr uint32_t kWBytes = kCo * kBK * 2;            // 16 KB weight stage
 constexpr int kSlot = kChunk * 32;  // one warp's chunk: 16 pixels x 32 channels
-constexpr int kHalf = kSlot * 2;    // bytes of one 16-bit plane of a chunk
-constexpr int kSlotBytes = kSlot * 4;  // a slot: hi + lo planes, or fp32 sums
 constexpr int kEpiWarps = 8;
 constexpr int kMagicShift = 40;     // n / d == (n * ceil(2^40 / d)) >> 40 here
 
@@ -69,9 +68,10 @@ struct PixArgs {
     int rs, is, board;
     int slab_rows;  // rows per slab (multiple of 16)
     uint64_t is_magic, rs_magic;  // ceil(2^40 / is), ceil(2^40 / rs)
-    int has_out16, has_out_lo;
     const uint16_t* res_hi;  // residual stream [m_total][128] hi plane or nullptr
     const uint16_t* res_lo;  // and its fp16 remainder plane
+    uint16_t* out16;         // output [m_total][128] (hi plane) or nullptr
+    uint16_t* out_lo;        // its fp16 remainder plane or nullptr
     const float* bias;
     const float* head_w;  // [3][128] or nullptr (fused head projection)
     const float* head_b;
@@ -138,27 +138,22 @@ __device__ __forceinline__ bool group_next(const PixArgs& a, int grp, int& k, in
 template <bool FP16, bool HEAD>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3x3_pix_kernel(const __grid_constant__ CUtensorMap tmW,
-                       const __grid_constant__ CUtensorMap tmX,
-                       const __grid_constant__ CUtensorMap tmRh,
-                       const __grid_constant__ CUtensorMap tmRl,
-                       const __grid_constant__ CUtensorMap tmOh,
-                       const __grid_constant__ CUtensorMap tmOl, const PixArgs a) {
+                       const __grid_constant__ CUtensorMap tmX, const PixArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t slab_bytes = (uint32_t)a.slab_rows * 128u;
     uint8_t* wring = smem;                                   // kStages x 16 KB
-    uint8_t* slab0 = wring + kStages * kWBytes;              // 2 slabs
-    uint8_t* ring0 = slab0 + 2 * slab_bytes;                 // [kEpiWarps][kRing] slots
-    uint64_t* bars = reinterpret_cast<uint64_t*>(ring0 + kEpiWarps * kRing * kSlotBytes);
+    uint8_t* slab0 = wring + kStages * kWBytes;              // kSlabs slabs
+    float* hslot = reinterpret_cast<float*>(slab0 + kSlabs * slab_bytes);  // [kEpiWarps][16][32]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(hslot + kEpiWarps * kSlot);
     uint64_t* wfull = bars;
     uint64_t* wempty = bars + kStages;
     uint64_t* sfull = bars + 2 * kStages;
-    uint64_t* sempty = sfull + 2;
-    uint64_t* tfull = sempty + 2;
+    uint64_t* sempty = sfull + kSlabs;
+    uint64_t* tfull = sempty + kSlabs;
     uint64_t* tempty = tfull + 2;
-    uint64_t* rfull = tempty + 2;  // [kEpiWarps][kRing]
-    uint64_t* done = rfull + kEpiWarps * kRing;
+    uint64_t* done = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     float* sbias = reinterpret_cast<float*>(tmem_slot + 4);  // [128]
     float* shead = sbias + kCo;                              // [3][128]
@@ -171,13 +166,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&wfull[s]), 1);
             mbar_init(smem_u32(&wempty[s]), 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kSlabs; ++i) {
             mbar_init(smem_u32(&sfull[i]), 1);
             mbar_init(smem_u32(&sempty[i]), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&tfull[i]), 1);
             mbar_init(smem_u32(&tempty[i]), 8);
         }
-        for (int i = 0; i < kEpiWarps * kRing; ++i) mbar_init(smem_u32(&rfull[i]), 1);
         mbar_init(smem_u32(done), 1);
         fence_barrier_init();
     }
@@ -204,37 +200,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half_rows = a.slab_rows / 2;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- weight producer ----------------
         if (lane == 0) {
             prefetch_tensormap(&tmW);
-            prefetch_tensormap(&tmX);
-            int iw = 0, is = 0;
+            int iw = 0;
             bool ok = true;
             for (int k = 0; k < a.tiles_per_cta && ok; ++k) {
                 int m0, len;
                 cta_tile(a, k, m0, len);
                 if (len <= 0) break;
-                if (a.res_hi != nullptr && k > 0)
-                    // residual rows of this tile (read by its epilogue about a
-                    // tile later) into L2, one 4 KB chunk per prefetch
-                    for (int r = 0; r < len; r += kChunk) {
-                        const uint32_t bytes = (uint32_t)min(kChunk, len - r) * kCo * 2u;
-                        prefetch_l2(a.res_hi + (size_t)(m0 + r) * kCo, bytes);
-                        prefetch_l2(a.res_lo + (size_t)(m0 + r) * kCo, bytes);
-                    }
-                for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
-                    const int sb = is & 1;
-                    if (!mbar_wait(smem_u32(&sempty[sb]), ((is >> 1) & 1) ^ 1, a.err,
-                                   kErrWaitProducer)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t sfb = smem_u32(&sfull[sb]);
-                    uint8_t* slab = slab0 + sb * slab_bytes;
-                    mbar_arrive_expect_tx(sfb, slab_bytes);
-                    tma_load_2d(smem_u32(slab), &tmX, sfb, cb * kBK, m0 - halo);
-                    tma_load_2d(smem_u32(slab + half_rows * 128), &tmX, sfb, cb * kBK,
-                                m0 - halo + half_rows);
+                for (int cb = 0; cb < cblocks && ok; ++cb) {
                     for (int tap = 0; tap < 9; ++tap, ++iw) {
                         const int s = iw % kStages;
                         if (!mbar_wait(smem_u32(&wempty[s]), ((iw / kStages) & 1) ^ 1, a.err,
@@ -252,8 +227,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Drain every copy still in flight before the CTA exits.
             for (int j = (iw > kStages ? iw - kStages : 0); j < iw; ++j)
                 mbar_wait(smem_u32(&wfull[j % kStages]), (j / kStages) & 1, a.err, kErrWaitDrain);
-            for (int j = (is > 2 ? is - 2 : 0); j < is; ++j)
-                mbar_wait(smem_u32(&sfull[j & 1]), (j >> 1) & 1, a.err, kErrWaitDrain);
+        }
+        __syncwarp();
+    } else if (warp == 2 + kEpiWarps) {
+        // ---------------- activation slab producer ----------------
+        // Separate from the weight producer so a slab load is issued as soon
+        // as a slab buffer frees up, not behind the weight ring's waits.
+        if (lane == 0) {
+            prefetch_tensormap(&tmX);
+            int is = 0;
+            bool ok = true;
+            for (int k = 0; k < a.tiles_per_cta && ok; ++k) {
+                int m0, len;
+                cta_tile(a, k, m0, len);
+                if (len <= 0) break;
+                for (int cb = 0; cb < cblocks; ++cb, ++is) {
+                    const int sb = is % kSlabs;
+                    if (!mbar_wait(smem_u32(&sempty[sb]), ((is / kSlabs) & 1) ^ 1, a.err,
+                                   kErrWaitProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sfb = smem_u32(&sfull[sb]);
+                    uint8_t* slab = slab0 + sb * slab_bytes;
+                    mbar_arrive_expect_tx(sfb, slab_bytes);
+                    tma_load_2d(smem_u32(slab), &tmX, sfb, cb * kBK, m0 - halo);
+                    tma_load_2d(smem_u32(slab + half_rows * 128), &tmX, sfb, cb * kBK,
+                                m0 - halo + half_rows);
+                }
+            }
+            for (int j = (is > kSlabs ? is - kSlabs : 0); j < is; ++j)
+                mbar_wait(smem_u32(&sfull[j % kSlabs]), (j / kSlabs) & 1, a.err, kErrWaitDrain);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -275,8 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * kMaxPx);
                 for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
-                    const int sb = is & 1;
-                    if (!mbar_wait(smem_u32(&sfull[sb]), (is >> 1) & 1, a.err, kErrWaitMma)) {
+                    const int sb = is % kSlabs;
+                    if (!mbar_wait(smem_u32(&sfull[sb]), (is / kSlabs) & 1, a.err, kErrWaitMma)) {
                         ok = false;
                         break;
                     }
@@ -310,8 +314,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ---------------- epilogue (warps 2..9) ----------------
         // Each warp finishes its 32 channels (its TMEM lanes) of every other
-        // chunk on its own: no barrier couples it to the other warps except
-        // in the head-projection layer, which sums over all 128 channels.
+        // chunk on its own, straight between registers and global memory:
+        // lane = channel, so each 16-bit access of the warp covers 64
+        // contiguous bytes of a pixel row.  Only the head-projection layer,
+        // which sums over all 128 channels, couples the warps (through
+        // shared memory).
         const int quarter = warp & 3;  // channels [32*quarter, +32)
         const int ew = warp - 2;       // 0..7
         const int par = ew >> 2;       // chunks par, par+2, ...
@@ -319,33 +326,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float bias = sbias[co];
         const int hw = a.board * a.board;
         const bool has_res = a.res_hi != nullptr;
-        const bool store_out = a.has_out16 != 0;
-        uint8_t* ring = ring0 + ew * (kRing * kSlotBytes);
-        const uint32_t rbar0 = smem_u32(&rfull[ew * kRing]);
+        const bool has_lo = a.out_lo != nullptr;
+        float* slot = hslot + ew * kSlot;  // head layer: this warp's fp32 sums [16][32]
         const int bar_a = 2 + 2 * par, bar_b = 3 + 2 * par;  // head layer only
-        // Residual loads run kRing - 1 chunks ahead of the chunk being
-        // finished.  Load j goes to slot j % kRing; it is issued once the bulk
-        // stores (or, in the head layer, the head sums) that last read that
-        // slot are done with it.
+        // Residual of the next chunk, loaded one chunk ahead into registers.
+        uint16_t nh[kChunk], nl[kChunk];
+        auto load_res = [&](int px) {
+            const uint16_t* ph = a.res_hi + (size_t)px * kCo + co;
+            const uint16_t* pl = a.res_lo + (size_t)px * kCo + co;
+            if (px + kChunk <= a.m_total) {
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    nh[j] = __ldcg(ph + j * kCo);
+                    nl[j] = __ldcg(pl + j * kCo);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    const bool in = px + j < a.m_total;
+                    nh[j] = in ? __ldcg(ph + j * kCo) : (uint16_t)0;
+                    nl[j] = in ? __ldcg(pl + j * kCo) : (uint16_t)0;
+                }
+            }
+        };
         int lk = 0, lc = par - 2;  // position of the next residual load
         bool lvalid = group_next(a, par, lk, lc);
-        int nissued = 0;
-        auto issue_load = [&]() {
-            if (!lvalid) return;
+        if (has_res && lvalid) {
             int m0, len;
             cta_tile(a, lk, m0, len);
-            const int b = nissued % kRing;
-            const uint32_t bar = rbar0 + 8u * b;
-            const uint32_t dst = smem_u32(ring + b * kSlotBytes);
-            mbar_arrive_expect_tx(bar, 2 * kHalf);
-            tma_load_2d(dst, &tmRh, bar, quarter * 32, m0 + lc * kChunk);
-            tma_load_2d(dst + kHalf, &tmRl, bar, quarter * 32, m0 + lc * kChunk);
-            ++nissued;
+            load_res(m0 + lc * kChunk);
             lvalid = group_next(a, par, lk, lc);
-        };
-        if (has_res && lane == 0)
-            for (int j = 0; j < kRing - 1; ++j) issue_load();
-        int i = 0;  // chunks finished by this warp
+        }
         int t = 0;
         bool ok = true;
         for (int k = 0; k < a.tiles_per_cta && ok; ++k, ++t) {
@@ -363,14 +374,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tcol =
                 tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kMaxPx);
 #pragma unroll 1
-            for (int c = par; c < nchunks; c += 2, ++i) {
+            for (int c = par; c < nchunks; c += 2) {
                 const int px0 = m0 + c * kChunk;
-                const int b = i % kRing;
-                uint8_t* slot = ring + b * kSlotBytes;
-                uint16_t* shi = reinterpret_cast<uint16_t*>(slot);
-                uint16_t* slo = reinterpret_cast<uint16_t*>(slot + kHalf);
                 uint32_t v[16];
                 tmem_ld_16cols(tcol + (uint32_t)(c * kChunk), v);
+                float f[16];
+                if (has_res) {
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j) f[j] = from16<FP16>(nh[j]) + lo_value(nl[j]);
+                    if (lvalid) {  // next chunk's residual, in flight during this one
+                        int m1, len1;
+                        cta_tile(a, lk, m1, len1);
+                        load_res(m1 + lc * kChunk);
+                        lvalid = group_next(a, par, lk, lc);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j) f[j] = 0.f;
+                }
                 // lanes 0..15 classify pixels px0 + lane
                 bool onb = false;
                 if (c * kChunk + (lane & 15) < len) {
@@ -380,73 +401,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                     onb = (y < a.board) && (q - y * a.rs < a.board);
                 }
                 const uint32_t board_mask = __ballot_sync(0xffffffffu, onb) & 0xffffu;
-                bool rok = true;
-                if (has_res) rok = mbar_wait(rbar0 + 8u * b, (i / kRing) & 1, a.err, kErrWaitEpilogue);
-                // In the head layer this barrier also keeps the slot from being
-                // rewritten before every warp of the group has finished the
-                // previous chunk's head sums.
-                if (HEAD ? bar_any(bar_b, 128, !rok) : __any_sync(0xffffffffu, !rok)) {
-                    ok = false;
-                    break;
-                }
-                float f[16];
-                if (has_res) {
-#pragma unroll
-                    for (int j = 0; j < kChunk; ++j)
-                        f[j] = from16<FP16>(shi[j * 32 + lane]) + lo_value(slo[j * 32 + lane]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < kChunk; ++j) f[j] = 0.f;
-                }
                 tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < kChunk; ++j) {
                     const float x = __uint_as_float(v[j]) + bias + f[j];
                     f[j] = ((board_mask >> j) & 1) ? fmaxf(x, 0.f) : 0.f;
                 }
-                if (HEAD) {
-                    // fp32 sums for the head projection, over the whole slot
-                    __syncwarp();
-                    float* s32 = reinterpret_cast<float*>(slot);
-#pragma unroll
-                    for (int j = 0; j < kChunk; ++j) s32[j * 32 + lane] = f[j];
-                } else {
+                if (!HEAD) {
+                    uint16_t* oh = a.out16 + (size_t)px0 * kCo + co;
+                    uint16_t* ol = a.out_lo + (size_t)px0 * kCo + co;
+                    const int nrow = min(kChunk, a.m_total - px0);
 #pragma unroll
                     for (int j = 0; j < kChunk; ++j) {
-                        const uint16_t h = to16<FP16>(f[j]);
-                        shi[j * 32 + lane] = h;
-                        if (a.has_out_lo) slo[j * 32 + lane] = lo_bits(f[j] - from16<FP16>(h));
+                        if (j < nrow) {
+                            const uint16_t h = to16<FP16>(f[j]);
+                            oh[j * kCo] = h;
+                            if (has_lo) ol[j * kCo] = lo_bits(f[j] - from16<FP16>(h));
+                        }
                     }
-                }
-                if (store_out) fence_proxy_async_smem();
-                if (HEAD)
-                    named_barrier_sync(bar_a, 128);
-                else
-                    __syncwarp();
-                if (lane == 0) {
-                    if (store_out) {
-                        tma_store_2d(&tmOh, smem_u32(shi), quarter * 32, px0);
-                        if (a.has_out_lo) tma_store_2d(&tmOl, smem_u32(slo), quarter * 32, px0);
-                        bulk_commit();
-                        // the previous chunk's stores have read their slot
-                        bulk_wait_read_n<1>();
-                    }
-                    if (has_res) issue_load();  // into the previous chunk's slot
-                }
-                __syncwarp();
-                if (HEAD) {
+                } else {
                     // Policy / value 1x1 convs of the chunk's 16 pixels:
                     // thread (pixel g/8, channel segment g%8) of the group
                     // sums 16 channels, which sit in the slot of the warp
                     // owning that channel quarter; the 8 segments of a pixel
-                    // combine by shuffles.
+                    // combine by shuffles.  The first barrier keeps the slots
+                    // from being rewritten while the previous chunk's sums
+                    // still read them.
+                    named_barrier_sync(bar_b, 128);
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j) slot[j * 32 + lane] = f[j];
+                    named_barrier_sync(bar_a, 128);
                     const int g = ((warp - 2) & 3) * 32 + lane;
                     const int p = g >> 3, seg = g & 7, sq = seg >> 1;
                     const float* row =
-                        reinterpret_cast<const float*>(
-                            ring0 + (par * 4 + ((sq + 2) & 3)) * (kRing * kSlotBytes) +
-                            b * kSlotBytes) +
-                        p * 32 + (seg & 1) * 16;
+                        hslot + (par * 4 + ((sq + 2) & 3)) * kSlot + p * 32 + (seg & 1) * 16;
                     const float* hw0 = shead + seg * 16;
                     float d0 = 0.f, d1 = 0.f, d2 = 0.f;
 #pragma unroll
@@ -479,13 +467,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
         }
-        if (lane == 0) {
-            // Every bulk store complete and every issued residual load landed
-            // before the CTA's shared memory is released.
-            if (store_out) bulk_wait_all();
-            for (int j = i; j < nissued; ++j)
-                mbar_wait(rbar0 + 8u * (j % kRing), (j / kRing) & 1, a.err, kErrWaitDrain);
-        }
     }
 
     tc_fence_before();
@@ -503,8 +484,8 @@ int slab_rows_for(int npx, int rs) {
 
 size_t pix_smem_bytes(int npx, int rs) {
     const size_t slab = (size_t)slab_rows_for(npx, rs) * 128;
-    return (size_t)kStages * kWBytes + 2 * slab + (size_t)kEpiWarps * kRing * kSlotBytes +
-           (2 * kStages + 8 + kEpiWarps * kRing + 1) * 8 + 16 + (kCo + 3 * kCo) * 4 + 1024;
+    return (size_t)kStages * kWBytes + kSlabs * slab + (size_t)kEpiWarps * kSlot * 4 +
+           (2 * kStages + 2 * kSlabs + 4 + 1) * 8 + 16 + (kCo + 3 * kCo) * 4 + 1024;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -582,10 +563,10 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
     a.slab_rows = slab_rows_for(npx, L.g.rs);
     a.is_magic = ((1ull << kMagicShift) + (uint64_t)L.g.is - 1) / (uint64_t)L.g.is;
     a.rs_magic = ((1ull << kMagicShift) + (uint64_t)L.g.rs - 1) / (uint64_t)L.g.rs;
-    a.has_out16 = L.out16 != nullptr;
-    a.has_out_lo = L.out_lo != nullptr;
     a.res_hi = static_cast<const uint16_t*>(L.res_hi);
     a.res_lo = L.res_lo;
+    a.out16 = static_cast<uint16_t*>(L.out16);
+    a.out_lo = L.out_lo;
     a.bias = L.bias;
     a.head_w = L.head_w;
     a.head_b = L.head_b;
@@ -593,27 +574,12 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
     a.err = L.err;
     const CUtensorMapDataType t16 =
         fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    const CUtensorMapDataType tlo = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUtensorMap tmW, tmX, tmRh, tmRl, tmOh, tmOl;
-    // Epilogue maps of absent buffers describe a valid dummy (the first 16
-    // rows' worth of the weight buffer, at least 147 KB) and are never used.
-    auto or_dummy = [&](const void* p) { return p ? p : L.weight; };
+    CUtensorMap tmW, tmX;
     const uint64_t rows = (uint64_t)L.m_total;
-    const uint64_t rrows = L.res_hi ? rows : kChunk, orows = L.out16 ? rows : kChunk,
-                   lrows = L.out_lo ? rows : kChunk;
     if (!encode(&tmW, t16, 2, L.weight, (uint64_t)9 * L.cin, (uint64_t)kCo, kBK, kCo,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode(&tmX, t16, 2, L.in, (uint64_t)L.cin, rows, kBK, (uint32_t)(a.slab_rows / 2),
-                CU_TENSOR_MAP_SWIZZLE_128B) ||
-        // epilogue boxes: one warp's 32 channels x 16 pixels
-        !encode(&tmRh, t16, 2, or_dummy(L.res_hi), kCo, rrows, 32, kChunk,
-                CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&tmRl, tlo, 2, or_dummy(L.res_lo), kCo, rrows, 32, kChunk,
-                CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&tmOh, t16, 2, or_dummy(L.out16), kCo, orows, 32, kChunk,
-                CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode(&tmOl, tlo, 2, or_dummy(L.out_lo), kCo, lrows, 32, kChunk,
-                CU_TENSOR_MAP_SWIZZLE_NONE))
+                CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     // Programmatic dependent launch: this kernel's CTAs may start (and run
     // their prologue) while the previous kernel in the stream drains; they
@@ -631,7 +597,7 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
     const bool head = L.head_w != nullptr;
     auto fn = fp16 ? (head ? conv3x3_pix_kernel<true, true> : conv3x3_pix_kernel<true, false>)
                    : (head ? conv3x3_pix_kernel<false, true> : conv3x3_pix_kernel<false, false>);
-    return cudaLaunchKernelEx(&cfg, fn, tmW, tmX, tmRh, tmRl, tmOh, tmOl, a);
+    return cudaLaunchKernelEx(&cfg, fn, tmW, tmX, a);
 }
 
 }  // namespace mgb
