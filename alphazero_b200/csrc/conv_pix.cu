@@ -1,5 +1,6 @@
-// 3x3 convolution with 128 output channels as an implicit GEMM on the
-// sm_100a tensor cores, pixels on the MMA's N side.
+// 3x3 convolutions with 128 output channels as implicit GEMMs on the sm_100a
+// tensor cores, pixels on the MMA's N side; one launch runs one layer or a
+// whole run of trunk layers.
 //
 //   D[co][px] = sum_{cb, tap, k} W[co][tap][cb*64 + k] * X[px + off(tap)][cb*64 + k]
 //
@@ -22,21 +23,35 @@
 // residual stream is a pair of 16-bit planes, x = hi + lo with hi = x
 // rounded to the operand type (the next layer's input) and lo = x - hi
 // rounded to fp16.  A chunk's residual hi / lo values are loaded one chunk
-// ahead into registers; each thread adds bias and residual, applies
-// ReLU and the frame mask, and stores the sum re-split into hi and lo.  In
-// the last trunk layer the fp32 sums go through shared memory to the
-// policy / value 1x1 head projection instead.
+// ahead into registers; each thread adds bias and residual, applies ReLU and
+// the frame mask, and stores the sum re-split into hi and lo.  In the last
+// trunk layer the fp32 sums go through shared memory to the policy / value
+// 1x1 head projection instead.
 //
 // Warp roles (352 threads): warp 0 weight TMA producer, warp 1 TMEM
 // allocator + MMA issuer, warps 2-9 epilogue (warp w reads TMEM lanes
 // [32*(w%4), +32) of chunks (w-2)/4, (w-2)/4 + 2, ...), warp 10 activation
 // slab TMA producer (two slab buffers).  All waits are bounded.
 //
-// Work split: CTA b owns the contiguous pixel range [b*span, (b+1)*span),
-// cut into equal tiles of at most 256 pixels, so every SM gets the same
-// number of pixels (a fixed 256-pixel tiling left up to 10% of the last wave
-// idle).  Launches are programmatic dependent launches: a CTA's prologue
-// overlaps the previous kernel's tail.
+// Work split: CTA b owns the contiguous pixel range [b*span, (b+1)*span) in
+// every layer, cut into equal tiles of at most 256 pixels, so every SM gets
+// the same number of pixels.  Even CTAs take their tiles left to right, odd
+// CTAs right to left.
+//
+// Several layers in one launch (a cooperative launch, so every CTA is
+// resident): a tile of layer l reads layer l-1's rows [m0 - RS - 1, m0 + len
+// + RS + 1), i.e. the CTA's own neighbouring tiles and, at the ends of its
+// range, the nearest tiles of the neighbouring CTAs.  After all 8 epilogue
+// warps have stored a tile, the CTA publishes its count of finished tiles
+// (release, GPU scope); the slab producer waits (acquire) until the tiles
+// it needs are counted before loading a slab.  The same wait covers the
+// reverse hazard: a tile's outputs overwrite rows that only those tiles of
+// the layer before read.  Because neighbouring CTAs run in opposite
+// directions, the first tile of layer l needs only tiles that were among the
+// first finished in layer l-1, so the MMA moves on to layer l while the
+// epilogue finishes layer l-1.  Single-layer launches are ordinary
+// programmatic dependent launches: a CTA's prologue overlaps the previous
+// kernel's tail.
 #include "kernels.cuh"
 #include "ptx_sm100.cuh"
 
@@ -58,26 +73,61 @@ constexpr uint32_t kWBytes = kCo * kBK * 2;            // 16 KB weight stage
 constexpr int kSlot = kChunk * 32;  // one warp's chunk: 16 pixels x 32 channels
 constexpr int kEpiWarps = 8;
 constexpr int kMagicShift = 40;     // n / d == (n * ceil(2^40 / d)) >> 40 here
+constexpr int kMaxLayers = 44;      // layers per launch (kernel parameter space)
+
+// One layer of a launch.
+struct PixLayer {
+    const float* bias;       // [128]
+    const uint16_t* res_hi;  // residual stream [m_total][128] hi plane, or nullptr
+    const uint16_t* res_lo;  // and its fp16 remainder plane
+    uint16_t* out16;         // output [m_total][128] (hi plane), or nullptr
+    uint16_t* out_lo;        // its fp16 remainder plane, or nullptr
+    int cin;                 // 64 or 128
+    int xmap;                // activation tensor map of the input slabs (0..2)
+    int wmap;                // weight tensor map (0 or 1)
+    int wrow;                // first row of this layer's weights in that map
+    int head;                // fused head projection (last trunk layer)
+    int pad[1];
+};
+static_assert(sizeof(PixLayer) == 64, "PixLayer layout");
 
 struct PixArgs {
     int m_total;
     int span;           // pixels per CTA (multiple of 16): CTA b owns [b*span, (b+1)*span)
-    int tiles_per_cta;  // tiles its range is cut into
+    int tiles_per_cta;  // tiles a full range is cut into
     int npx;            // pixels per tile (multiple of 16, <= 256; the last tile may be shorter)
-    int cin;
     int rs, is, board;
-    int slab_rows;  // rows per slab (multiple of 16)
+    int slab_rows;                // rows per slab (multiple of 16)
     uint64_t is_magic, rs_magic;  // ceil(2^40 / is), ceil(2^40 / rs)
-    const uint16_t* res_hi;  // residual stream [m_total][128] hi plane or nullptr
-    const uint16_t* res_lo;  // and its fp16 remainder plane
-    uint16_t* out16;         // output [m_total][128] (hi plane) or nullptr
-    uint16_t* out_lo;        // its fp16 remainder plane or nullptr
-    const float* bias;
+    int n_layers;
+    int* err;
+    unsigned* progress;  // [grid] tiles finished per CTA (several layers), else nullptr
     const float* head_w;  // [3][128] or nullptr (fused head projection)
     const float* head_b;
     float* feat;
-    int* err;
+    PixLayer layer[kMaxLayers];
 };
+
+// The launch geometry, copied out of the parameters once: kept in registers,
+// it is not re-read after every store the way fields reached through a
+// reference to the parameter block can be.
+struct Geo {
+    int m_total, span, npx, rs, is, board;
+    uint64_t is_magic, rs_magic;
+};
+
+__device__ __forceinline__ Geo geo_of(const PixArgs& a) {
+    Geo g;
+    g.m_total = a.m_total;
+    g.span = a.span;
+    g.npx = a.npx;
+    g.rs = a.rs;
+    g.is = a.is;
+    g.board = a.board;
+    g.is_magic = a.is_magic;
+    g.rs_magic = a.rs_magic;
+    return g;
+}
 
 template <bool FP16>
 __device__ __forceinline__ uint16_t to16(float v);
@@ -110,35 +160,256 @@ __device__ __forceinline__ int div_magic(int n, uint64_t magic) {
     return (int)(((uint64_t)(uint32_t)n * magic) >> kMagicShift);
 }
 
-// Tile k of this CTA's contiguous pixel range: rows [m0, m0 + len);
-// len <= 0 when the range has no such tile.  Every CTA gets the same number
-// of pixels (to within one tile), so the last wave is not mostly idle.
-__device__ __forceinline__ void cta_tile(const PixArgs& a, int k, int& m0, int& len) {
-    const int start = blockIdx.x * a.span;
-    const int end = min(start + a.span, a.m_total);
-    m0 = start + k * a.npx;
-    len = min(a.npx, end - m0);
+// Number of tiles of CTA c (those of the last CTA may be fewer).
+__device__ __forceinline__ int cta_tiles(const Geo& g, int c) {
+    const int start = c * g.span;
+    const int end = min(start + g.span, g.m_total);
+    return end > start ? (end - start + g.npx - 1) / g.npx : 0;
 }
 
-// Advances (k, c) to epilogue group grp's next chunk (chunks grp, grp+2, ...
-// of each tile in turn); false when the CTA has none left.
-__device__ __forceinline__ bool group_next(const PixArgs& a, int grp, int& k, int& c) {
-    c += 2;
-    while (k < a.tiles_per_cta) {
-        int m0, len;
-        cta_tile(a, k, m0, len);
-        if (len <= 0) return false;
-        if (c * kChunk < len) return true;
-        ++k;
-        c = grp;
+// Rows [m0, m0 + len) of CTA c's tile j.
+__device__ __forceinline__ void tile_rows(const Geo& g, int c, int j, int& m0, int& len) {
+    const int start = c * g.span;
+    const int end = min(start + g.span, g.m_total);
+    m0 = start + j * g.npx;
+    len = min(g.npx, end - m0);
+}
+
+// The tile CTA c takes q-th in each layer, and the position of tile j in
+// that order: even CTAs left to right, odd CTAs right to left.
+__device__ __forceinline__ int tile_at(int c, int q, int nt) { return (c & 1) ? nt - 1 - q : q; }
+__device__ __forceinline__ int order_of(int c, int j, int nt) { return (c & 1) ? nt - 1 - j : j; }
+
+// Before a tile of layer l (>= 1) reads rows [m0 - halo, m0 + len + halo)
+// of layer l-1's output: waits until every CTA owning some of those rows has
+// published the tiles that hold them.
+__device__ __forceinline__ bool wait_inputs(const Geo& g, const unsigned* progress, int* err, int l,
+                                            int m0, int len, int halo) {
+    const int lo = max(m0 - halo, 0);
+    const int hi = min(m0 + len + halo, g.m_total) - 1;
+    for (int c = lo / g.span; c <= hi / g.span; ++c) {
+        const int start = c * g.span;
+        const int nt = cta_tiles(g, c);
+        const int j0 = (max(lo, start) - start) / g.npx;
+        const int j1 = (min(hi, start + g.span - 1) - start) / g.npx;
+        const int last = (c & 1) ? order_of(c, j0, nt) : order_of(c, j1, nt);
+        if (!wait_counter(&progress[c], (unsigned)((l - 1) * nt + last + 1), err, kErrWaitDep))
+            return false;
     }
-    return false;
+    return true;
 }
 
+// One layer of the epilogue for one warp (see the kernel's epilogue): t
+// counts the CTA's tiles so far.  Returns false when a wait gave up.
 template <bool FP16, bool HEAD>
+__device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, int l, int nt, int& t,
+                                               uint64_t* tfull, uint64_t* tempty, uint32_t* tcount,
+                                               uint32_t tmem_base, float* hslot, const float* shead,
+                                               int warp, int lane) {
+    const int quarter = warp & 3;  // channels [32*quarter, +32)
+    const int ew = warp - 2;       // 0..7
+    const int par = ew >> 2;       // chunks par, par+2, ...
+    const int co = quarter * 32 + lane;
+    const int hw = G.board * G.board;
+    int* const err = a.err;
+    unsigned* const progress = a.progress;
+    float* const feat = a.feat;
+    const float* const head_b = a.head_b;
+    float* slot = hslot + ew * kSlot;  // head layer: this warp's fp32 sums [16][32]
+    const int bar_a = 2 + 2 * par, bar_b = 3 + 2 * par;  // head layer only
+    bool ok = true;
+    // The layer's parameters in registers (read once, not after every
+    // store or wait).
+    const uint16_t* const res_hi = a.layer[l].res_hi;
+    const uint16_t* const res_lo = a.layer[l].res_lo;
+    uint16_t* const out16 = a.layer[l].out16;
+    uint16_t* const out_lo = a.layer[l].out_lo;
+    const float bias = a.layer[l].bias[co];
+    const bool has_res = res_hi != nullptr;
+    const bool has_lo = out_lo != nullptr;
+    // Residual of the next chunk (tile order position lq, chunk lc),
+    // loaded one chunk ahead into registers.
+    uint16_t nh[kChunk], nl[kChunk];
+    auto load_res = [&](int px) {
+        const uint16_t* ph = res_hi + (size_t)px * kCo + co;
+        const uint16_t* pl = res_lo + (size_t)px * kCo + co;
+        if (px + kChunk <= G.m_total) {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                nh[j] = ld_cg_u16_early(ph + j * kCo);
+                nl[j] = ld_cg_u16_early(pl + j * kCo);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                const bool in = px + j < G.m_total;
+                nh[j] = in ? ld_cg_u16_early(ph + j * kCo) : (uint16_t)0;
+                nl[j] = in ? ld_cg_u16_early(pl + j * kCo) : (uint16_t)0;
+            }
+        }
+    };
+    // Advances (lq, lc) to this warp's next chunk of the layer.
+    auto next_chunk = [&](int& lq, int& lc) {
+        lc += 2;
+        while (lq < nt) {
+            int m, n;
+            tile_rows(G, blockIdx.x, tile_at(blockIdx.x, lq, nt), m, n);
+            if (lc * kChunk < n) return true;
+            ++lq;
+            lc = par;
+        }
+        return false;
+    };
+    int lq = 0, lc = par - 2;
+    bool lvalid = next_chunk(lq, lc);
+    if (has_res && lvalid) {
+        int m, n;
+        tile_rows(G, blockIdx.x, tile_at(blockIdx.x, lq, nt), m, n);
+        load_res(m + lc * kChunk);
+        lvalid = next_chunk(lq, lc);
+    }
+    for (int q = 0; q < nt && ok; ++q, ++t) {
+        int m0, len;
+        tile_rows(G, blockIdx.x, tile_at(blockIdx.x, q, nt), m0, len);
+        const int nchunks = (len + kChunk - 1) / kChunk;
+        const int acc = t & 1;
+        ok = mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, err, kErrWaitEpilogue);
+        if (HEAD ? bar_any(bar_a, 128, !ok) : __any_sync(0xffffffffu, !ok)) {
+            ok = false;
+            break;
+        }
+        tc_fence_after();
+        const uint32_t tcol =
+            tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kMaxPx);
+#pragma unroll 1
+        for (int c = par; c < nchunks; c += 2) {
+            const int px0 = m0 + c * kChunk;
+            uint32_t v[16];
+            tmem_ld_16cols(tcol + (uint32_t)(c * kChunk), v);
+            float f[16];
+            if (has_res) {
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j)
+                    f[j] = from16<FP16>(nh[j]) + lo_value(nl[j]);
+                if (lvalid) {  // next chunk's residual, in flight during this one
+                    int m1, len1;
+                    tile_rows(G, blockIdx.x, tile_at(blockIdx.x, lq, nt), m1, len1);
+                    load_res(m1 + lc * kChunk);
+                    lvalid = next_chunk(lq, lc);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) f[j] = 0.f;
+            }
+            // lanes 0..15 classify pixels px0 + lane
+            bool onb = false;
+            if (c * kChunk + (lane & 15) < len) {
+                const int mj = px0 + (lane & 15);
+                const int qq = mj - div_magic(mj, G.is_magic) * G.is;
+                const int y = div_magic(qq, G.rs_magic);
+                onb = (y < G.board) && (qq - y * G.rs < G.board);
+            }
+            const uint32_t board_mask = __ballot_sync(0xffffffffu, onb) & 0xffffu;
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                const float x = __uint_as_float(v[j]) + bias + f[j];
+                f[j] = ((board_mask >> j) & 1) ? fmaxf(x, 0.f) : 0.f;
+            }
+            if (!HEAD) {
+                uint16_t* oh = out16 + (size_t)px0 * kCo + co;
+                uint16_t* ol = out_lo + (size_t)px0 * kCo + co;
+                const int nrow = min(kChunk, G.m_total - px0);
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    if (j < nrow) {
+                        const uint16_t h = to16<FP16>(f[j]);
+                        oh[j * kCo] = h;
+                        if (has_lo) ol[j * kCo] = lo_bits(f[j] - from16<FP16>(h));
+                    }
+                }
+            } else {
+                // Policy / value 1x1 convs of the chunk's 16 pixels:
+                // thread (pixel g/8, channel segment g%8) of the group
+                // sums 16 channels, which sit in the slot of the warp
+                // owning that channel quarter; the 8 segments of a
+                // pixel combine by shuffles.  The first barrier keeps
+                // the slots from being rewritten while the previous
+                // chunk's sums still read them.
+                named_barrier_sync(bar_b, 128);
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) slot[j * 32 + lane] = f[j];
+                named_barrier_sync(bar_a, 128);
+                const int g = ((warp - 2) & 3) * 32 + lane;
+                const int p = g >> 3, seg = g & 7, sq = seg >> 1;
+                const float* row =
+                    hslot + (par * 4 + ((sq + 2) & 3)) * kSlot + p * 32 + (seg & 1) * 16;
+                const float* hw0 = shead + seg * 16;
+                float d0 = 0.f, d1 = 0.f, d2 = 0.f;
+#pragma unroll 4
+                for (int k = 0; k < 16; ++k) {
+                    const int kq = (k + 4 * sq + (p & 3)) & 15;  // spread banks
+                    const float xv = row[kq];
+                    d0 = fmaf(xv, hw0[kq], d0);
+                    d1 = fmaf(xv, hw0[kCo + kq], d1);
+                    d2 = fmaf(xv, hw0[2 * kCo + kq], d2);
+                }
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) {
+                    d0 += __shfl_xor_sync(0xffffffffu, d0, o);
+                    d1 += __shfl_xor_sync(0xffffffffu, d1, o);
+                    d2 += __shfl_xor_sync(0xffffffffu, d2, o);
+                }
+                if (seg == 0 && ((board_mask >> p) & 1)) {
+                    const int mp = px0 + p;
+                    const int pos = div_magic(mp, G.is_magic);
+                    const int qq = mp - pos * G.is;
+                    const int y = div_magic(qq, G.rs_magic), x = qq - y * G.rs;
+                    float* fr = feat + (size_t)pos * 3 * hw + y * G.board + x;
+                    fr[0] = fmaxf(d0 + head_b[0], 0.f);
+                    fr[hw] = fmaxf(d1 + head_b[1], 0.f);
+                    fr[2 * hw] = fmaxf(d2 + head_b[2], 0.f);
+                }
+            }
+        }
+        tc_fence_before();
+        if (progress != nullptr) {
+            // This warp's stores of the tile are done; the last of the
+            // 8 warps publishes the CTA's count of finished tiles.
+            fence_proxy_async_global();
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) {
+                const unsigned before = atom_add_acq_rel_cta(smem_u32(&tcount[acc]), 1u);
+                if (before == (unsigned)(kEpiWarps * (t >> 1) + kEpiWarps - 1))
+                    red_max_release_gpu(&progress[blockIdx.x], (unsigned)(l * nt + q + 1));
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+    }
+    return ok;
+}
+
+// The head-projection layer's epilogue kept out of line: inlined next to
+// the other layers' epilogue it made the compiler schedule that hot loop
+// worse (measured: the residual layers' epilogue 20% slower).
+template <bool FP16>
+__device__ __noinline__ bool epilogue_head_layer(const PixArgs& a, const Geo G, int l, int nt,
+                                                 int& t, uint64_t* tfull, uint64_t* tempty,
+                                                 uint32_t* tcount, uint32_t tmem_base, float* hslot,
+                                                 const float* shead, int warp, int lane) {
+    return epilogue_layer<FP16, true>(a, G, l, nt, t, tfull, tempty, tcount, tmem_base, hslot,
+                                      shead, warp, lane);
+}
+
+template <bool FP16>
 __global__ void __launch_bounds__(kThreads, 1)
-    conv3x3_pix_kernel(const __grid_constant__ CUtensorMap tmW,
-                       const __grid_constant__ CUtensorMap tmX, const PixArgs a) {
+    conv3x3_pix_kernel(const __grid_constant__ CUtensorMap tmW0,
+                       const __grid_constant__ CUtensorMap tmW1,
+                       const __grid_constant__ CUtensorMap tmX0,
+                       const __grid_constant__ CUtensorMap tmX1,
+                       const __grid_constant__ CUtensorMap tmX2, const __grid_constant__ PixArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -155,11 +426,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tempty = tfull + 2;
     uint64_t* done = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-    float* sbias = reinterpret_cast<float*>(tmem_slot + 4);  // [128]
-    float* shead = sbias + kCo;                              // [3][128]
+    uint32_t* tcount = tmem_slot + 1;                        // [2] epilogue warps done, per buffer
+    float* shead = reinterpret_cast<float*>(tmem_slot + 4);  // [3][128]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const Geo G = geo_of(a);
+    int* const err = a.err;
+    const int nt = cta_tiles(G, blockIdx.x);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -172,7 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&tfull[i]), 1);
-            mbar_init(smem_u32(&tempty[i]), 8);
+            mbar_init(smem_u32(&tempty[i]), kEpiWarps);
+            tcount[i] = 0;
         }
         mbar_init(smem_u32(done), 1);
         fence_barrier_init();
@@ -181,52 +456,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(smem_u32(tmem_slot), 512);
         tmem_relinquish();
     }
-    for (int i = threadIdx.x; i < kCo; i += kThreads) sbias[i] = a.bias[i];
     if (a.head_w != nullptr)
         for (int i = threadIdx.x; i < 3 * kCo; i += kThreads) shead[i] = a.head_w[i];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // Everything above touches only this CTA's resources and the layer's
+    // Everything above touches only this CTA's resources and the launch's
     // constant parameters.  Activations written by the previous kernel are
     // read, and activations it may still read are overwritten, only after
     // it has completed.
     griddep_launch_dependents();
     griddep_wait();
 
-    const int cblocks = a.cin / kBK;
-    const int halo = a.rs + 1;
+    const int halo = G.rs + 1;
     const int half_rows = a.slab_rows / 2;
 
     if (warp == 0) {
         // ---------------- weight producer ----------------
         if (lane == 0) {
-            prefetch_tensormap(&tmW);
+            prefetch_tensormap(&tmW0);
+            prefetch_tensormap(&tmW1);
             int iw = 0;
             bool ok = true;
-            for (int k = 0; k < a.tiles_per_cta && ok; ++k) {
-                int m0, len;
-                cta_tile(a, k, m0, len);
-                if (len <= 0) break;
-                for (int cb = 0; cb < cblocks && ok; ++cb) {
-                    for (int tap = 0; tap < 9; ++tap, ++iw) {
-                        const int s = iw % kStages;
-                        if (!mbar_wait(smem_u32(&wempty[s]), ((iw / kStages) & 1) ^ 1, a.err,
-                                       kErrWaitProducer)) {
-                            ok = false;
-                            break;
+            for (int l = 0; l < a.n_layers && ok; ++l) {
+                const int cin = a.layer[l].cin, wrow = a.layer[l].wrow;
+                const CUtensorMap* map = a.layer[l].wmap ? &tmW1 : &tmW0;
+                for (int q = 0; q < nt && ok; ++q) {
+                    for (int cb = 0; cb < cin / kBK && ok; ++cb) {
+                        for (int tap = 0; tap < 9; ++tap, ++iw) {
+                            const int s = iw % kStages;
+                            if (!mbar_wait(smem_u32(&wempty[s]), ((iw / kStages) & 1) ^ 1, err,
+                                           kErrWaitProducer)) {
+                                ok = false;
+                                break;
+                            }
+                            const uint32_t wfb = smem_u32(&wfull[s]);
+                            mbar_arrive_expect_tx(wfb, kWBytes);
+                            tma_load_2d(smem_u32(wring + s * kWBytes), map, wfb, tap * cin + cb * kBK,
+                                        wrow);
                         }
-                        const uint32_t wfb = smem_u32(&wfull[s]);
-                        mbar_arrive_expect_tx(wfb, kWBytes);
-                        tma_load_2d(smem_u32(wring + s * kWBytes), &tmW, wfb, tap * a.cin + cb * kBK,
-                                    0);
                     }
                 }
             }
             // Drain every copy still in flight before the CTA exits.
             for (int j = (iw > kStages ? iw - kStages : 0); j < iw; ++j)
-                mbar_wait(smem_u32(&wfull[j % kStages]), (j / kStages) & 1, a.err, kErrWaitDrain);
+                mbar_wait(smem_u32(&wfull[j % kStages]), (j / kStages) & 1, err, kErrWaitDrain);
         }
         __syncwarp();
     } else if (warp == 2 + kEpiWarps) {
@@ -234,30 +509,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Separate from the weight producer so a slab load is issued as soon
         // as a slab buffer frees up, not behind the weight ring's waits.
         if (lane == 0) {
-            prefetch_tensormap(&tmX);
+            prefetch_tensormap(&tmX0);
+            prefetch_tensormap(&tmX1);
+            prefetch_tensormap(&tmX2);
             int is = 0;
             bool ok = true;
-            for (int k = 0; k < a.tiles_per_cta && ok; ++k) {
-                int m0, len;
-                cta_tile(a, k, m0, len);
-                if (len <= 0) break;
-                for (int cb = 0; cb < cblocks; ++cb, ++is) {
-                    const int sb = is % kSlabs;
-                    if (!mbar_wait(smem_u32(&sempty[sb]), ((is / kSlabs) & 1) ^ 1, a.err,
-                                   kErrWaitProducer)) {
-                        ok = false;
-                        break;
+            for (int l = 0; l < a.n_layers && ok; ++l) {
+                const int cin = a.layer[l].cin, xmap = a.layer[l].xmap;
+                const CUtensorMap* map = xmap == 0 ? &tmX0 : (xmap == 1 ? &tmX1 : &tmX2);
+                for (int q = 0; q < nt && ok; ++q) {
+                    int m0, len;
+                    tile_rows(G, blockIdx.x, tile_at(blockIdx.x, q, nt), m0, len);
+                    if (l > 0 && a.progress != nullptr) {
+                        if (!wait_inputs(G, a.progress, err, l, m0, len, halo)) {
+                            ok = false;
+                            break;
+                        }
+                        // the rows were written through the generic proxy
+                        fence_proxy_async_global();
                     }
-                    const uint32_t sfb = smem_u32(&sfull[sb]);
-                    uint8_t* slab = slab0 + sb * slab_bytes;
-                    mbar_arrive_expect_tx(sfb, slab_bytes);
-                    tma_load_2d(smem_u32(slab), &tmX, sfb, cb * kBK, m0 - halo);
-                    tma_load_2d(smem_u32(slab + half_rows * 128), &tmX, sfb, cb * kBK,
-                                m0 - halo + half_rows);
+                    for (int cb = 0; cb < cin / kBK; ++cb, ++is) {
+                        const int sb = is % kSlabs;
+                        if (!mbar_wait(smem_u32(&sempty[sb]), ((is / kSlabs) & 1) ^ 1, err,
+                                       kErrWaitProducer)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t sfb = smem_u32(&sfull[sb]);
+                        uint8_t* slab = slab0 + sb * slab_bytes;
+                        mbar_arrive_expect_tx(sfb, slab_bytes);
+                        tma_load_2d(smem_u32(slab), map, sfb, cb * kBK, m0 - halo);
+                        tma_load_2d(smem_u32(slab + half_rows * 128), map, sfb, cb * kBK,
+                                    m0 - halo + half_rows);
+                    }
                 }
             }
             for (int j = (is > kSlabs ? is - kSlabs : 0); j < is; ++j)
-                mbar_wait(smem_u32(&sfull[j % kSlabs]), (j / kSlabs) & 1, a.err, kErrWaitDrain);
+                mbar_wait(smem_u32(&sfull[j % kSlabs]), (j / kSlabs) & 1, err, kErrWaitDrain);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -265,208 +553,70 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int iw = 0, is = 0, t = 0;
             bool ok = true;
-            for (int k = 0; k < a.tiles_per_cta && ok; ++k, ++t) {
-                int m0, len;
-                cta_tile(a, k, m0, len);
-                if (len <= 0) break;
-                // MMA N = the tile's pixels rounded up to 16
-                const uint32_t idesc = idesc_f16(kCo, (len + 15) & ~15, !FP16);
-                const int acc = t & 1;
-                if (!mbar_wait(smem_u32(&tempty[acc]), ((t >> 1) & 1) ^ 1, a.err, kErrWaitMma)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(acc * kMaxPx);
-                for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
-                    const int sb = is % kSlabs;
-                    if (!mbar_wait(smem_u32(&sfull[sb]), (is / kSlabs) & 1, a.err, kErrWaitMma)) {
+            for (int l = 0; l < a.n_layers && ok; ++l) {
+                const int cblocks = a.layer[l].cin / kBK;
+                for (int q = 0; q < nt && ok; ++q, ++t) {
+                    int m0, len;
+                    tile_rows(G, blockIdx.x, tile_at(blockIdx.x, q, nt), m0, len);
+                    // MMA N = the tile's pixels rounded up to 16
+                    const uint32_t idesc = idesc_f16(kCo, (len + 15) & ~15, !FP16);
+                    const int acc = t & 1;
+                    if (!mbar_wait(smem_u32(&tempty[acc]), ((t >> 1) & 1) ^ 1, err, kErrWaitMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t slab = smem_u32(slab0 + sb * slab_bytes);
-                    for (int tap = 0; tap < 9; ++tap, ++iw) {
-                        const int s = iw % kStages;
-                        if (!mbar_wait(smem_u32(&wfull[s]), (iw / kStages) & 1, a.err, kErrWaitMma)) {
+                    const uint32_t d = tmem_base + (uint32_t)(acc * kMaxPx);
+                    for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
+                        const int sb = is % kSlabs;
+                        if (!mbar_wait(smem_u32(&sfull[sb]), (is / kSlabs) & 1, err, kErrWaitMma)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const int r0 = halo + (tap / 3 - 1) * a.rs + (tap % 3 - 1);
-                        const uint64_t ad = smem_desc_sw128(smem_u32(wring + s * kWBytes));
+                        const uint32_t slab = smem_u32(slab0 + sb * slab_bytes);
+                        for (int tap = 0; tap < 9; ++tap, ++iw) {
+                            const int s = iw % kStages;
+                            if (!mbar_wait(smem_u32(&wfull[s]), (iw / kStages) & 1, err,
+                                           kErrWaitMma)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const int r0 = halo + (tap / 3 - 1) * G.rs + (tap % 3 - 1);
+                            const uint64_t ad = smem_desc_sw128(smem_u32(wring + s * kWBytes));
 #pragma unroll
-                        for (int kk = 0; kk < kBK / 16; ++kk) {
-                            // row-shifted start, base offset 0 (see file comment)
-                            const uint64_t bd = smem_desc_sw128(slab + (uint32_t)r0 * 128u + 32u * kk);
-                            mma_f16(d, ad + (uint64_t)(2 * kk), bd, idesc, (cb | tap | kk) != 0);
+                            for (int kk = 0; kk < kBK / 16; ++kk) {
+                                // row-shifted start, base offset 0 (see file comment)
+                                const uint64_t bd =
+                                    smem_desc_sw128(slab + (uint32_t)r0 * 128u + 32u * kk);
+                                mma_f16(d, ad + (uint64_t)(2 * kk), bd, idesc, (cb | tap | kk) != 0);
+                            }
+                            mma_commit(smem_u32(&wempty[s]));
                         }
-                        mma_commit(smem_u32(&wempty[s]));
+                        if (ok) mma_commit(smem_u32(&sempty[sb]));
                     }
-                    if (ok) mma_commit(smem_u32(&sempty[sb]));
+                    if (ok) mma_commit(smem_u32(&tfull[acc]));
                 }
-                if (ok) mma_commit(smem_u32(&tfull[acc]));
             }
             mma_commit(smem_u32(done));
-            mbar_wait(smem_u32(done), 0, a.err, kErrWaitDrain);
+            mbar_wait(smem_u32(done), 0, err, kErrWaitDrain);
         }
         __syncwarp();
     } else {
         // ---------------- epilogue (warps 2..9) ----------------
         // Each warp finishes its 32 channels (its TMEM lanes) of every other
-        // chunk on its own, straight between registers and global memory:
-        // lane = channel, so each 16-bit access of the warp covers 64
-        // contiguous bytes of a pixel row.  Only the head-projection layer,
-        // which sums over all 128 channels, couples the warps (through
-        // shared memory).
-        const int quarter = warp & 3;  // channels [32*quarter, +32)
-        const int ew = warp - 2;       // 0..7
-        const int par = ew >> 2;       // chunks par, par+2, ...
-        const int co = quarter * 32 + lane;
-        const float bias = sbias[co];
-        const int hw = a.board * a.board;
-        const bool has_res = a.res_hi != nullptr;
-        const bool has_lo = a.out_lo != nullptr;
-        float* slot = hslot + ew * kSlot;  // head layer: this warp's fp32 sums [16][32]
-        const int bar_a = 2 + 2 * par, bar_b = 3 + 2 * par;  // head layer only
-        // Residual of the next chunk, loaded one chunk ahead into registers.
-        uint16_t nh[kChunk], nl[kChunk];
-        auto load_res = [&](int px) {
-            const uint16_t* ph = a.res_hi + (size_t)px * kCo + co;
-            const uint16_t* pl = a.res_lo + (size_t)px * kCo + co;
-            if (px + kChunk <= a.m_total) {
-#pragma unroll
-                for (int j = 0; j < kChunk; ++j) {
-                    nh[j] = __ldcg(ph + j * kCo);
-                    nl[j] = __ldcg(pl + j * kCo);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < kChunk; ++j) {
-                    const bool in = px + j < a.m_total;
-                    nh[j] = in ? __ldcg(ph + j * kCo) : (uint16_t)0;
-                    nl[j] = in ? __ldcg(pl + j * kCo) : (uint16_t)0;
-                }
-            }
-        };
-        int lk = 0, lc = par - 2;  // position of the next residual load
-        bool lvalid = group_next(a, par, lk, lc);
-        if (has_res && lvalid) {
-            int m0, len;
-            cta_tile(a, lk, m0, len);
-            load_res(m0 + lc * kChunk);
-            lvalid = group_next(a, par, lk, lc);
-        }
+        // chunk on its own, straight between registers and global memory.
+        // Only the head-projection layer, which sums over all 128 channels,
+        // couples the warps (through shared memory).
         int t = 0;
         bool ok = true;
-        for (int k = 0; k < a.tiles_per_cta && ok; ++k, ++t) {
-            int m0, len;
-            cta_tile(a, k, m0, len);
-            if (len <= 0) break;
-            const int nchunks = (len + kChunk - 1) / kChunk;
-            const int acc = t & 1;
-            ok = mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, a.err, kErrWaitEpilogue);
-            if (HEAD ? bar_any(bar_a, 128, !ok) : __any_sync(0xffffffffu, !ok)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t tcol =
-                tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kMaxPx);
-#pragma unroll 1
-            for (int c = par; c < nchunks; c += 2) {
-                const int px0 = m0 + c * kChunk;
-                uint32_t v[16];
-                tmem_ld_16cols(tcol + (uint32_t)(c * kChunk), v);
-                float f[16];
-                if (has_res) {
-#pragma unroll
-                    for (int j = 0; j < kChunk; ++j) f[j] = from16<FP16>(nh[j]) + lo_value(nl[j]);
-                    if (lvalid) {  // next chunk's residual, in flight during this one
-                        int m1, len1;
-                        cta_tile(a, lk, m1, len1);
-                        load_res(m1 + lc * kChunk);
-                        lvalid = group_next(a, par, lk, lc);
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < kChunk; ++j) f[j] = 0.f;
-                }
-                // lanes 0..15 classify pixels px0 + lane
-                bool onb = false;
-                if (c * kChunk + (lane & 15) < len) {
-                    const int mj = px0 + (lane & 15);
-                    const int q = mj - div_magic(mj, a.is_magic) * a.is;
-                    const int y = div_magic(q, a.rs_magic);
-                    onb = (y < a.board) && (q - y * a.rs < a.board);
-                }
-                const uint32_t board_mask = __ballot_sync(0xffffffffu, onb) & 0xffffu;
-                tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < kChunk; ++j) {
-                    const float x = __uint_as_float(v[j]) + bias + f[j];
-                    f[j] = ((board_mask >> j) & 1) ? fmaxf(x, 0.f) : 0.f;
-                }
-                if (!HEAD) {
-                    uint16_t* oh = a.out16 + (size_t)px0 * kCo + co;
-                    uint16_t* ol = a.out_lo + (size_t)px0 * kCo + co;
-                    const int nrow = min(kChunk, a.m_total - px0);
-#pragma unroll
-                    for (int j = 0; j < kChunk; ++j) {
-                        if (j < nrow) {
-                            const uint16_t h = to16<FP16>(f[j]);
-                            oh[j * kCo] = h;
-                            if (has_lo) ol[j * kCo] = lo_bits(f[j] - from16<FP16>(h));
-                        }
-                    }
-                } else {
-                    // Policy / value 1x1 convs of the chunk's 16 pixels:
-                    // thread (pixel g/8, channel segment g%8) of the group
-                    // sums 16 channels, which sit in the slot of the warp
-                    // owning that channel quarter; the 8 segments of a pixel
-                    // combine by shuffles.  The first barrier keeps the slots
-                    // from being rewritten while the previous chunk's sums
-                    // still read them.
-                    named_barrier_sync(bar_b, 128);
-#pragma unroll
-                    for (int j = 0; j < kChunk; ++j) slot[j * 32 + lane] = f[j];
-                    named_barrier_sync(bar_a, 128);
-                    const int g = ((warp - 2) & 3) * 32 + lane;
-                    const int p = g >> 3, seg = g & 7, sq = seg >> 1;
-                    const float* row =
-                        hslot + (par * 4 + ((sq + 2) & 3)) * kSlot + p * 32 + (seg & 1) * 16;
-                    const float* hw0 = shead + seg * 16;
-                    float d0 = 0.f, d1 = 0.f, d2 = 0.f;
-#pragma unroll
-                    for (int q = 0; q < 16; ++q) {
-                        const int kq = (q + 4 * sq + (p & 3)) & 15;  // spread banks
-                        const float xv = row[kq];
-                        d0 = fmaf(xv, hw0[kq], d0);
-                        d1 = fmaf(xv, hw0[kCo + kq], d1);
-                        d2 = fmaf(xv, hw0[2 * kCo + kq], d2);
-                    }
-#pragma unroll
-                    for (int o = 1; o < 8; o <<= 1) {
-                        d0 += __shfl_xor_sync(0xffffffffu, d0, o);
-                        d1 += __shfl_xor_sync(0xffffffffu, d1, o);
-                        d2 += __shfl_xor_sync(0xffffffffu, d2, o);
-                    }
-                    if (seg == 0 && ((board_mask >> p) & 1)) {
-                        const int mp = px0 + p;
-                        const int pos = div_magic(mp, a.is_magic);
-                        const int qq = mp - pos * a.is;
-                        const int y = div_magic(qq, a.rs_magic), x = qq - y * a.rs;
-                        float* fr = a.feat + (size_t)pos * 3 * hw + y * a.board + x;
-                        fr[0] = fmaxf(d0 + a.head_b[0], 0.f);
-                        fr[hw] = fmaxf(d1 + a.head_b[1], 0.f);
-                        fr[2 * hw] = fmaxf(d2 + a.head_b[2], 0.f);
-                    }
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
-        }
+        for (int l = 0; l < a.n_layers && ok; ++l)
+            ok = a.layer[l].head != 0
+                     ? epilogue_head_layer<FP16>(a, G, l, nt, t, tfull, tempty, tcount, tmem_base,
+                                                  hslot, shead, warp, lane)
+                     : epilogue_layer<FP16, false>(a, G, l, nt, t, tfull, tempty, tcount, tmem_base,
+                                                   hslot, shead, warp, lane);
     }
 
     tc_fence_before();
@@ -485,7 +635,7 @@ int slab_rows_for(int npx, int rs) {
 size_t pix_smem_bytes(int npx, int rs) {
     const size_t slab = (size_t)slab_rows_for(npx, rs) * 128;
     return (size_t)kStages * kWBytes + kSlabs * slab + (size_t)kEpiWarps * kSlot * 4 +
-           (2 * kStages + 2 * kSlabs + 4 + 1) * 8 + 16 + (kCo + 3 * kCo) * 4 + 1024;
+           (2 * kStages + 2 * kSlabs + 4 + 1) * 8 + 16 + 3 * kCo * 4 + 1024;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -515,14 +665,150 @@ bool encode(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* bas
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool layer_ok(const ConvLayer& L, const ConvLayer& first) {
+    // The residual stream is the hi / lo pair; fp32 residuals are not read.
+    return L.cout == kCo && (L.cin == 64 || L.cin == 128) && L.m_total == first.m_total &&
+           L.g.rs == first.g.rs && L.res32 == nullptr && L.out32 == nullptr &&
+           (L.res_hi == nullptr) == (L.res_lo == nullptr) &&
+           (L.out_lo == nullptr || L.out16 != nullptr) &&
+           (L.head_w != nullptr || L.out16 != nullptr) && L.g.is <= 1200 &&
+           L.m_total < (1 << 23) - 2 * kMaxPx;
+}
+
+// Launches layers[0..n) (n <= kMaxLayers) as one kernel.  Layer 0 may have
+// any supported cin; layers 1.. must have cin 128 and weights laid out back
+// to back from layers[1].weight.  With several layers, progress must point
+// at grid_limit counters.
+cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16, int grid_limit,
+                          unsigned* progress, cudaStream_t stream) {
+    if (n < 1 || n > kMaxLayers || (n > 1 && progress == nullptr)) return cudaErrorInvalidValue;
+    const ConvLayer& F = layers[0];
+    // Balanced ranges: each CTA takes span pixels (a multiple of 16) cut into
+    // equal tiles of at most max_npx.
+    const int units = (F.m_total + 15) / 16;
+    int grid = units < grid_limit ? units : grid_limit;
+    if (grid < 1) grid = 1;
+    const int span = (((F.m_total + grid - 1) / grid) + 15) / 16 * 16;
+    grid = (F.m_total + span - 1) / span;
+    const int tiles = (span + max_npx - 1) / max_npx;
+    const int npx = ((span + tiles - 1) / tiles + 15) / 16 * 16;
+    if (npx % kChunk != 0 || npx < 16 || npx > kMaxPx ||
+        pix_smem_bytes(npx, F.g.rs) > 227 * 1024)
+        return cudaErrorInvalidValue;
+    PixArgs a;
+    a.m_total = F.m_total;
+    a.span = span;
+    a.tiles_per_cta = tiles;
+    a.npx = npx;
+    a.rs = F.g.rs;
+    a.is = F.g.is;
+    a.board = F.g.board;
+    a.slab_rows = slab_rows_for(npx, F.g.rs);
+    a.is_magic = ((1ull << kMagicShift) + (uint64_t)F.g.is - 1) / (uint64_t)F.g.is;
+    a.rs_magic = ((1ull << kMagicShift) + (uint64_t)F.g.rs - 1) / (uint64_t)F.g.rs;
+    a.n_layers = n;
+    a.err = F.err;
+    a.progress = n > 1 ? progress : nullptr;
+    a.head_w = nullptr;
+    a.head_b = nullptr;
+    a.feat = nullptr;
+    // Up to three distinct input buffers, each with its own tensor map.
+    const void* xin[3] = {nullptr, nullptr, nullptr};
+    int xcin[3] = {0, 0, 0};
+    int nx = 0;
+    const size_t wstride = (size_t)kCo * 9 * 128;  // elements per cin-128 layer
+    for (int l = 0; l < n; ++l) {
+        const ConvLayer& L = layers[l];
+        if (!layer_ok(L, F)) return cudaErrorInvalidValue;
+        if (L.head_w != nullptr && l != n - 1) return cudaErrorInvalidValue;
+        PixLayer& P = a.layer[l];
+        P = PixLayer{};
+        P.bias = L.bias;
+        P.res_hi = static_cast<const uint16_t*>(L.res_hi);
+        P.res_lo = L.res_lo;
+        P.out16 = static_cast<uint16_t*>(L.out16);
+        P.out_lo = L.out_lo;
+        P.cin = L.cin;
+        int xm = 0;
+        while (xm < nx && xin[xm] != L.in) ++xm;
+        if (xm == nx) {
+            if (nx == 3) return cudaErrorInvalidValue;
+            xin[nx] = L.in;
+            xcin[nx] = L.cin;
+            ++nx;
+        } else if (xcin[xm] != L.cin) {
+            return cudaErrorInvalidValue;
+        }
+        P.xmap = xm;
+        if (l == 0) {
+            P.wmap = 0;
+            P.wrow = 0;
+        } else {
+            if (L.cin != 128 ||
+                L.weight != static_cast<const uint16_t*>(layers[1].weight) + (l - 1) * wstride)
+                return cudaErrorInvalidValue;
+            P.wmap = 1;
+            P.wrow = (l - 1) * kCo;
+        }
+        if (L.head_w != nullptr) {
+            P.head = 1;
+            a.head_w = L.head_w;
+            a.head_b = L.head_b;
+            a.feat = L.feat;
+        }
+    }
+    const CUtensorMapDataType t16 =
+        fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap tmW[2], tmX[3];
+    const uint64_t rows = (uint64_t)F.m_total;
+    if (!encode(&tmW[0], t16, 2, F.weight, (uint64_t)9 * F.cin, (uint64_t)kCo, kBK, kCo,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    // Maps that a launch does not use describe a valid dummy and are never read.
+    if (!encode(&tmW[1], t16, 2, n > 1 ? layers[1].weight : F.weight,
+                n > 1 ? (uint64_t)9 * 128 : (uint64_t)9 * F.cin,
+                n > 1 ? (uint64_t)(n - 1) * kCo : (uint64_t)kCo, kBK, kCo,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    for (int i = 0; i < 3; ++i) {
+        const int k = i < nx ? i : 0;
+        if (!encode(&tmX[i], t16, 2, xin[k], (uint64_t)xcin[k], rows, kBK,
+                    (uint32_t)(a.slab_rows / 2), CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+    }
+    if (n > 1) {
+        cudaError_t e = cudaMemsetAsync(progress, 0, (size_t)grid * sizeof(unsigned), stream);
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pix_smem_bytes(npx, F.g.rs);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (n > 1) {
+        // CTAs wait on one another's progress: all of them must be resident.
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+    } else {
+        // Programmatic dependent launch: this kernel's CTAs may start (and
+        // run their prologue) while the previous kernel in the stream
+        // drains; they wait for its completion before touching activations.
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    auto fn = fp16 ? conv3x3_pix_kernel<true> : conv3x3_pix_kernel<false>;
+    return cudaLaunchKernelEx(&cfg, fn, tmW[0], tmW[1], tmX[0], tmX[1], tmX[2], a);
+}
+
 }  // namespace
 
 cudaError_t configure_conv_pix() {
     const int smem = 227 * 1024;
-    const void* fns[4] = {(const void*)conv3x3_pix_kernel<false, false>,
-                          (const void*)conv3x3_pix_kernel<false, true>,
-                          (const void*)conv3x3_pix_kernel<true, false>,
-                          (const void*)conv3x3_pix_kernel<true, true>};
+    const void* fns[2] = {(const void*)conv3x3_pix_kernel<false>,
+                          (const void*)conv3x3_pix_kernel<true>};
     for (const void* f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
@@ -531,73 +817,47 @@ cudaError_t configure_conv_pix() {
 }
 
 bool conv_pix_supported(const ConvLayer& L, int npx) {
-    // The residual stream is the hi / lo pair; fp32 residuals are not read.
-    return L.cout == kCo && L.cin % kBK == 0 && npx % kChunk == 0 && npx >= 16 &&
-           npx <= kMaxPx && pix_smem_bytes(npx, L.g.rs) <= 227 * 1024 && L.res32 == nullptr &&
-           L.out32 == nullptr && (L.res_hi == nullptr) == (L.res_lo == nullptr) &&
-           (L.out_lo == nullptr || L.out16 != nullptr) && L.g.is <= 1200 &&
-           L.m_total < (1 << 23) - 2 * kMaxPx;
+    return layer_ok(L, L) && npx % kChunk == 0 && npx >= 16 && npx <= kMaxPx &&
+           pix_smem_bytes(npx, L.g.rs) <= 227 * 1024;
 }
 
 cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid_limit,
                             cudaStream_t stream) {
-    // Balanced ranges: each CTA takes span pixels (a multiple of 16) cut into
-    // equal tiles of at most max_npx.
-    const int units = (L.m_total + 15) / 16;
-    int grid = units < grid_limit ? units : grid_limit;
-    if (grid < 1) grid = 1;
-    const int span = (((L.m_total + grid - 1) / grid) + 15) / 16 * 16;
-    grid = (L.m_total + span - 1) / span;
-    const int tiles = (span + max_npx - 1) / max_npx;
-    const int npx = ((span + tiles - 1) / tiles + 15) / 16 * 16;
-    if (!conv_pix_supported(L, npx)) return cudaErrorInvalidValue;
-    PixArgs a;
-    a.m_total = L.m_total;
-    a.span = span;
-    a.tiles_per_cta = tiles;
-    a.npx = npx;
-    a.cin = L.cin;
-    a.rs = L.g.rs;
-    a.is = L.g.is;
-    a.board = L.g.board;
-    a.slab_rows = slab_rows_for(npx, L.g.rs);
-    a.is_magic = ((1ull << kMagicShift) + (uint64_t)L.g.is - 1) / (uint64_t)L.g.is;
-    a.rs_magic = ((1ull << kMagicShift) + (uint64_t)L.g.rs - 1) / (uint64_t)L.g.rs;
-    a.res_hi = static_cast<const uint16_t*>(L.res_hi);
-    a.res_lo = L.res_lo;
-    a.out16 = static_cast<uint16_t*>(L.out16);
-    a.out_lo = L.out_lo;
-    a.bias = L.bias;
-    a.head_w = L.head_w;
-    a.head_b = L.head_b;
-    a.feat = L.feat;
-    a.err = L.err;
-    const CUtensorMapDataType t16 =
-        fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    CUtensorMap tmW, tmX;
-    const uint64_t rows = (uint64_t)L.m_total;
-    if (!encode(&tmW, t16, 2, L.weight, (uint64_t)9 * L.cin, (uint64_t)kCo, kBK, kCo,
-                CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode(&tmX, t16, 2, L.in, (uint64_t)L.cin, rows, kBK, (uint32_t)(a.slab_rows / 2),
-                CU_TENSOR_MAP_SWIZZLE_128B))
-        return cudaErrorInvalidValue;
-    // Programmatic dependent launch: this kernel's CTAs may start (and run
-    // their prologue) while the previous kernel in the stream drains; they
-    // wait for its completion before touching activations (griddep_wait).
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = pix_smem_bytes(npx, L.g.rs);
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const bool head = L.head_w != nullptr;
-    auto fn = fp16 ? (head ? conv3x3_pix_kernel<true, true> : conv3x3_pix_kernel<true, false>)
-                   : (head ? conv3x3_pix_kernel<false, true> : conv3x3_pix_kernel<false, false>);
-    return cudaLaunchKernelEx(&cfg, fn, tmW, tmX, a);
+    return launch_layers(&L, 1, max_npx, fp16, grid_limit, nullptr, stream);
+}
+
+cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool fp16,
+                             int grid_limit, unsigned* progress, cudaStream_t stream) {
+    // With fewer than kTrunkMinTiles tiles per CTA a tile of the next layer
+    // depends on most of the CTA's range and its neighbours' of the layer
+    // before, so one launch per layer (programmatic dependent launches) is
+    // faster than the cross-CTA handoff (measured: 19x19 batch 64 and 9x9
+    // batch 256, one or two tiles per CTA).
+    constexpr int kTrunkMinTiles = 3;
+    if (n > 0) {
+        const int m_total = layers[0].m_total;
+        const int units = (m_total + 15) / 16;
+        const int grid = units < grid_limit ? (units < 1 ? 1 : units) : grid_limit;
+        const int span = (((m_total + grid - 1) / grid) + 15) / 16 * 16;
+        if ((span + max_npx - 1) / max_npx < kTrunkMinTiles) {
+            for (int l = 0; l < n; ++l) {
+                cudaError_t e =
+                    launch_layers(layers + l, 1, max_npx, fp16, grid_limit, nullptr, stream);
+                if (e != cudaSuccess) return e;
+            }
+            return cudaSuccess;
+        }
+    }
+    // Runs of at most kMaxLayers layers per launch; a run's first layer
+    // takes its weights through its own tensor map, so a run may start at
+    // any layer.
+    for (int l0 = 0; l0 < n; l0 += kMaxLayers) {
+        const int cnt = n - l0 < kMaxLayers ? n - l0 : kMaxLayers;
+        cudaError_t e = launch_layers(layers + l0, cnt, max_npx, fp16, grid_limit,
+                                      cnt > 1 ? progress : nullptr, stream);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace mgb

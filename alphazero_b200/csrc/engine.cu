@@ -81,6 +81,7 @@ struct mg_engine {
     int conv_bn_override = 0;
     int pix_mode = 1;      // 1: pixels-on-N kernel for 128-channel layers
     int pix_npx = 0;       // pixels per tile override (0 = heuristic)
+    int pix_trunk = 1;     // 1: all 128-channel trunk layers as one persistent launch
     bool use_graphs = true;
     cudaStream_t stream = nullptr;
     std::string err;
@@ -97,7 +98,8 @@ struct mg_engine {
     std::vector<std::vector<float>> bf;
 
     // Device weights.
-    std::vector<void*> d_w16;  // current 16-bit type (w16_prec)
+    std::vector<void*> d_w16;  // current 16-bit type (w16_prec), pointers into d_w16_all
+    void* d_w16_all = nullptr;  // all layers' 16-bit weights, back to back
     int w16_prec = -1;
     std::vector<float*> d_w32;
     std::vector<float*> d_bias;
@@ -122,6 +124,7 @@ struct mg_engine {
     float* d_logits = nullptr;
     float* d_value = nullptr;
     int* d_err = nullptr;
+    unsigned* d_progress = nullptr;  // [num_sms] per-CTA counters of the trunk kernel
     float* h_states = nullptr;  // pinned staging for pageable inputs
     int* h_err = nullptr;       // pinned status word
     uint32_t* d_bits = nullptr;  // bit-packed inputs [max_batch][words]
@@ -140,8 +143,10 @@ struct mg_engine {
     void free_buffers() {
         drop_graphs();
         for (void* p : {d_stage, (void*)d_x, d_x16, d_t, (void*)d_feat, (void*)d_fc}) if (p) cudaFree(p);
-        for (void* p : {(void*)d_states, (void*)d_probs, (void*)d_logits, (void*)d_value, (void*)d_err})
+        for (void* p : {(void*)d_states, (void*)d_probs, (void*)d_logits, (void*)d_value, (void*)d_err,
+                        (void*)d_progress})
             if (p) cudaFree(p);
+        d_progress = nullptr;
         if (h_states) cudaFreeHost(h_states);
         if (h_err) cudaFreeHost(h_err);
         if (d_bits) cudaFree(d_bits);
@@ -160,7 +165,8 @@ struct mg_engine {
 
     void free_weights() {
         drop_graphs();
-        for (void* p : d_w16) if (p) cudaFree(p);
+        if (d_w16_all) cudaFree(d_w16_all);
+        d_w16_all = nullptr;
         for (float* p : d_w32) if (p) cudaFree(p);
         for (float* p : d_bias) if (p) cudaFree(p);
         if (d_head) cudaFree(d_head);
@@ -317,8 +323,15 @@ struct mg_engine {
         }
         if (w16_prec == precision) return;
         drop_graphs();  // captured graphs hold the old weight pointers
-        for (void* p : d_w16) if (p) cudaFree(p);
+        if (d_w16_all) cudaFree(d_w16_all);
+        d_w16_all = nullptr;
         d_w16.assign(n_convs, nullptr);
+        // One allocation, layers back to back (each layer's size is a
+        // multiple of 16 bytes), as the persistent trunk kernel reads them.
+        size_t total = 0;
+        for (int li = 0; li < n_convs; ++li) total += wf[li].size();
+        d_w16_all = dalloc<uint16_t>(total, "cudaMalloc(w16)");
+        size_t off = 0;
         for (int li = 0; li < n_convs; ++li) {
             const size_t cnt = wf[li].size();
             std::vector<uint16_t> h(cnt);
@@ -333,7 +346,8 @@ struct mg_engine {
                     std::memcpy(&h[i], &v, 2);
                 }
             }
-            d_w16[li] = dalloc<uint16_t>(cnt, "cudaMalloc(w16)");
+            d_w16[li] = static_cast<uint16_t*>(d_w16_all) + off;
+            off += cnt;
             ck(cudaMemcpy(d_w16[li], h.data(), cnt * 2, cudaMemcpyHostToDevice), "cudaMemcpy(w16)");
         }
         w16_prec = precision;
@@ -360,6 +374,7 @@ struct mg_engine {
         d_logits = dalloc<float>((size_t)max_batch * actions, "cudaMalloc(logits)");
         d_value = dalloc<float>((size_t)max_batch, "cudaMalloc(value)");
         d_err = dalloc<int>(1, "cudaMalloc(err)");
+        d_progress = dalloc<unsigned>((size_t)num_sms, "cudaMalloc(progress)");
         ck(cudaMemset(d_err, 0, sizeof(int)), "cudaMemset(err)");
         ck(cudaMallocHost(reinterpret_cast<void**>(&h_states),
                           (size_t)max_batch * planes * hw * sizeof(float)),
@@ -490,7 +505,15 @@ struct mg_engine {
     }
 
     void enqueue_trunk_heads(int bucket) {
-        for (int li = 0; li < n_convs; ++li) launch_conv(li, bucket);
+        if (use_pix() && pix_trunk) {
+            std::vector<ConvLayer> layers(n_convs);
+            for (int li = 0; li < n_convs; ++li) layers[li] = layer_desc(li, bucket);
+            ck(launch_trunk_pix(layers.data(), n_convs, choose_npx(bucket * g.is),
+                                precision == MG_PREC_FP16, num_sms, d_progress, stream),
+               "conv3x3_pix trunk launch");
+        } else {
+            for (int li = 0; li < n_convs; ++li) launch_conv(li, bucket);
+        }
         if (!fused_heads(bucket))
             ck(launch_head_projection(d_x, bucket, cpad, g, d_head_w, d_head_b, d_feat, stream),
                "head projection launch");
@@ -633,6 +656,7 @@ mg_engine* mg_create(int device, int flags) {
     if (const char* s = std::getenv("MG_NO_GRAPHS")) e->use_graphs = std::atoi(s) == 0;
     if (const char* s = std::getenv("MG_PIX")) e->pix_mode = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_NPX")) e->pix_npx = std::atoi(s);
+    if (const char* s = std::getenv("MG_PIX_TRUNK")) e->pix_trunk = std::atoi(s);
     return e.release();
 }
 

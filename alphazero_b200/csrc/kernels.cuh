@@ -100,6 +100,16 @@ cudaError_t launch_conv_pix(const ConvLayer& layer, int max_npx, bool fp16, int 
                             cudaStream_t stream);
 cudaError_t configure_conv_pix();
 
+// The n trunk layers of a network (input conv first) as one persistent
+// cooperative launch of the same kernel (several launches past 44 layers):
+// each CTA keeps its pixel range through all layers and starts a tile of the
+// next layer as soon as the tiles of the previous layer that it reads are
+// stored.  Layers 1..n-1 must have cin 128 and their weights back to back
+// from layers[1].weight; progress points at grid_limit counters of scratch.
+// When CTAs get fewer than 3 tiles the layers go out as one launch each.
+cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool fp16,
+                             int grid_limit, unsigned* progress, cudaStream_t stream);
+
 // fp32 SIMT path used by the fp32 verification mode.
 cudaError_t launch_conv_simt(const ConvLayer& layer, cudaStream_t stream);
 

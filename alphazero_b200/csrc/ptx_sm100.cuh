@@ -16,6 +16,7 @@ enum DeviceError : int {
     kErrWaitMma = 2,        // MMA issuer gave up waiting for data / TMEM
     kErrWaitEpilogue = 3,   // epilogue gave up waiting for an accumulator
     kErrWaitDrain = 4,      // exit-time drain of in-flight copies timed out
+    kErrWaitDep = 5,        // gave up waiting for another CTA's tiles of the previous layer
 };
 
 // Every mbarrier wait gives up after this many nanoseconds of %globaltimer.
@@ -73,6 +74,58 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
             return false;
         }
     }
+}
+
+// ---- cross-CTA progress (one persistent kernel over several layers) ----
+
+// Release / acquire on a global counter at GPU scope.
+__device__ __forceinline__ void red_max_release_gpu(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.max.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Shared-memory add with acquire-release semantics at CTA scope; returns the
+// old value.
+__device__ __forceinline__ unsigned atom_add_acq_rel_cta(uint32_t addr, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;"
+                 : "=r"(old)
+                 : "r"(addr), "r"(v)
+                 : "memory");
+    return old;
+}
+// Orders this thread's generic-proxy global accesses with its async-proxy
+// (TMA) accesses to global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Waits until *p >= target (acquire).  Returns false (and records `code` in
+// *err) if that has not happened within kWaitLimitNs.
+__device__ __forceinline__ bool wait_counter(const unsigned* p, unsigned target, int* err,
+                                             int code) {
+    if (ld_acquire_gpu(p) >= target) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        for (int i = 0; i < 8; ++i)
+            if (ld_acquire_gpu(p) >= target) return true;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+}
+
+// 16-bit global load cached in L2 only, issued exactly where it is written
+// (volatile), so a load meant to run ahead of other work is not sunk next to
+// its use by the scheduler.
+__device__ __forceinline__ uint16_t ld_cg_u16_early(const uint16_t* p) {
+    uint16_t v;
+    asm volatile("ld.global.cg.b16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
 }
 
 // Programmatic dependent launch: let the next kernel in the stream start
