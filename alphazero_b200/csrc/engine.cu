@@ -504,7 +504,9 @@ struct mg_engine {
         ck(launch_conv_tc(L, ta, tb, bn, fp16, num_sms, stream), "conv3x3_tc launch");
     }
 
-    void enqueue_trunk_heads(int bucket) {
+    // All trunk convolutions of a forward pass (the persistent trunk kernel
+    // on the 128-channel 16-bit path, else one launch per layer).
+    void enqueue_trunk(int bucket) {
         if (use_pix() && pix_trunk) {
             std::vector<ConvLayer> layers(n_convs);
             for (int li = 0; li < n_convs; ++li) layers[li] = layer_desc(li, bucket);
@@ -514,6 +516,16 @@ struct mg_engine {
         } else {
             for (int li = 0; li < n_convs; ++li) launch_conv(li, bucket);
         }
+    }
+
+    int trunk_launches(int bucket) const {
+        if (use_pix() && pix_trunk)
+            return trunk_pix_launches(bucket * g.is, n_convs, choose_npx(bucket * g.is), num_sms);
+        return n_convs;
+    }
+
+    void enqueue_trunk_heads(int bucket) {
+        enqueue_trunk(bucket);
         if (!fused_heads(bucket))
             ck(launch_head_projection(d_x, bucket, cpad, g, d_head_w, d_head_b, d_feat, stream),
                "head projection launch");
@@ -945,11 +957,23 @@ int mg_launch_conv(mg_engine* e, int n, int layer, int reps) {
     });
 }
 
+int mg_launch_trunk(mg_engine* e, int n, int reps) {
+    if (e == nullptr) return MG_E_ARG;
+    return guarded(e, [&] {
+        e->check_ready();
+        if (e->last_bucket == 0 || e->alloc_batch == 0)
+            throw std::logic_error("run a forward pass before mg_launch_trunk");
+        if (reps < 0 || n < 1 || n > e->max_batch) throw std::invalid_argument("bad n or reps");
+        const int bucket = e->bucket_for(n);
+        for (int r = 0; r < reps; ++r) e->enqueue_trunk(bucket);
+    });
+}
+
 int mg_launches_per_forward(mg_engine* e, int n) {
     if (e == nullptr || !e->loaded) return 0;
-    (void)n;
     const int bucket = e->bucket_for(std::max(1, std::min(n, e->max_batch)));
-    return 1 /* stage */ + e->n_convs + (e->fused_heads(bucket) ? 0 : 1) + 2 /* FC, finish */;
+    return 1 /* stage */ + e->trunk_launches(bucket) + (e->fused_heads(bucket) ? 0 : 1) +
+           2 /* FC, finish */;
 }
 
 }  // extern "C"

@@ -109,6 +109,8 @@ cudaError_t configure_conv_pix();
 // When CTAs get fewer than 3 tiles the layers go out as one launch each.
 cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool fp16,
                              int grid_limit, unsigned* progress, cudaStream_t stream);
+// Number of kernel launches launch_trunk_pix makes for n layers of m_total rows.
+int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit);
 
 // fp32 SIMT path used by the fp32 verification mode.
 cudaError_t launch_conv_simt(const ConvLayer& layer, cudaStream_t stream);

@@ -59,11 +59,12 @@ def lib() -> ctypes.CDLL:
         L.mg_stream.argtypes = [vp]
         L.mg_stream.restype = vp
         L.mg_launch_conv.argtypes = [vp, ci, ci, ci]
+        L.mg_launch_trunk.argtypes = [vp, ci, ci]
         L.mg_launches_per_forward.argtypes = [vp, ci]
         for f in ("mg_load_onnx", "mg_load_weights", "mg_get_info", "mg_set_precision",
                   "mg_set_max_batch", "mg_forward", "mg_forward_device", "mg_forward_device_noalloc",
                   "mg_forward_packed", "mg_words_per_position", "mg_pack_states", "mg_synchronize",
-                  "mg_launch_conv", "mg_launches_per_forward"):
+                  "mg_launch_conv", "mg_launch_trunk", "mg_launches_per_forward"):
             getattr(L, f).restype = ci
         _LIB = L
     return _LIB
@@ -218,6 +219,9 @@ class CudaEngine:
 
     def launch_conv(self, n: int, layer: int, reps: int) -> None:
         self._check(self._L.mg_launch_conv(self._h, n, layer, reps))
+
+    def launch_trunk(self, n: int, reps: int) -> None:
+        self._check(self._L.mg_launch_trunk(self._h, n, reps))
 
     def launches_per_forward(self, n: int) -> int:
         return self._L.mg_launches_per_forward(self._h, n)

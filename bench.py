@@ -15,9 +15,10 @@ JSON line.  Numbers:
              the inputs in the bit-packed wire format (mg_forward_packed),
              forward, D2H of policy and value, wall-clock timed, max over
              ranks (e2e_fp32_planes: the same with fp32 planes, mg_forward);
-  roofline   the 3x3 convolution kernel (the dominant kernel) timed alone with
-             CUDA events: algorithmic FLOPs per launch / average launch time,
-             against the measured dense bf16 peak;
+  roofline   the trunk (all 3x3 convolution layers; the dominant kernel,
+             one persistent launch) timed alone with CUDA events:
+             algorithmic FLOPs per launch / average launch time, against the
+             measured dense bf16 peak;
   cpu_baseline  the oracle (C restatement of src/eigen_engine.cpp) on the
              host cores over a bounded sample (rank 0, N = 1 only).
 --impl reference times that CPU implementation alone as the reference arm.
@@ -51,14 +52,22 @@ DEFAULT_WORKLOAD = "b19c128x10_bs512"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
+def trunk_flops_per_position(board, filters, blocks, inputs=17):
+    """Algorithmic FLOPs of the trunk's 3x3 convolutions for one position:
+    board pixels only and the 17 real input planes (the frame rows and the
+    zero-padded input channels the kernels also multiply are not counted)."""
+    hw = board * board
+    c = filters
+    return 2 * hw * (9 * inputs * c + blocks * 2 * 9 * c * c)
+
+
 def flops_per_position(board, filters, blocks, inputs=17, hidden=64):
     """Algorithmic FLOPs of one forward pass (2 per multiply-add)."""
     hw = board * board
     a = hw + 1
     c = filters
-    trunk = 2 * hw * (9 * inputs * c + blocks * 2 * 9 * c * c)
     heads = 2 * hw * 3 * c + 2 * 2 * hw * a + 2 * hw * hidden + 2 * hidden
-    return trunk + heads
+    return trunk_flops_per_position(board, filters, blocks, inputs) + heads
 
 
 def load_peaks():
@@ -73,9 +82,9 @@ def load_peaks():
 
 
 def profiled_traffic(workload):
-    """DRAM bytes per conv launch from the committed ncu summary, if any."""
+    """DRAM bytes per trunk launch from the committed ncu summary, if any."""
     import glob
-    for p in sorted(glob.glob(os.path.join(ROOT, "profiles", f"conv3x3_*_{workload}.md"))):
+    for p in sorted(glob.glob(os.path.join(ROOT, "profiles", f"trunk_*_{workload}.md"))):
         m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
         if m:
             return float(m.group(1))
@@ -345,19 +354,20 @@ def run_b200(args, wl):
     xin = torch.from_numpy(x).pin_memory().numpy()
     e2e_planes = e2e_loop(lambda: eng.forward(xin, want_logits=False))
 
-    # ---- roofline: the 3x3 conv kernel alone (conv1 of block 0) ----
-    reps = 50
+    # ---- roofline: the dominant kernel, the trunk (every 3x3 conv layer;
+    # one persistent launch on the 128-channel path), timed alone ----
+    reps = 10
     eng.forward_device(d_x.data_ptr(), batch, d_p.data_ptr(), d_v.data_ptr(), None)
-    eng.launch_conv(batch, 0, 5)
+    eng.launch_trunk(batch, 2)
     c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     c0.record(stream)
-    eng.launch_conv(batch, 0, reps)
+    eng.launch_trunk(batch, reps)
     c1.record(stream)
     eng.synchronize()
-    conv_ms = c0.elapsed_time(c1) / reps
-    conv_flops = 2.0 * batch * hw * 9 * filters * filters
+    trunk_ms = c0.elapsed_time(c1) / reps
+    trunk_flops = float(batch) * trunk_flops_per_position(board, filters, blocks)
     peaks, peak_src = load_peaks()
-    achieved = conv_flops / (conv_ms / 1e3) / 1e12
+    achieved = trunk_flops / (trunk_ms / 1e3) / 1e12
     traffic = profiled_traffic(wl)
 
     base = None
@@ -383,8 +393,9 @@ def run_b200(args, wl):
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                     "traffic": traffic, "kernel": "3x3 conv of residual block 0 (conv1)",
-                     "flops_per_launch": conv_flops, "launch_ms": conv_ms,
+                     "traffic": traffic,
+                     "kernel": "trunk: all 3x3 conv layers (conv3x3_pix_kernel, persistent)",
+                     "flops_per_launch": trunk_flops, "launch_ms": trunk_ms,
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
         "tflops_whole_forward": value * flops_per_position(board, filters, blocks) / 1e12,
         "clocks": clocks.summary(),

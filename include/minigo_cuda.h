@@ -163,6 +163,12 @@ void* mg_stream(mg_engine* e);
  * time the trunk's convolution kernel alone with events on mg_stream(). */
 int mg_launch_conv(mg_engine* e, int n, int layer, int reps);
 
+/* Launches `reps` back-to-back passes of the whole trunk (every 3x3
+ * convolution layer, as one persistent kernel where the engine uses one)
+ * over the activations left by the last mg_forward_device of n positions.
+ * A measurement hook like mg_launch_conv; no reference counterpart. */
+int mg_launch_trunk(mg_engine* e, int n, int reps);
+
 /* Number of kernel launches one mg_forward_device of n positions makes. */
 int mg_launches_per_forward(mg_engine* e, int n);
 

@@ -176,3 +176,25 @@ def test_packed_wire_format_matches_fp32_planes(gpu_engine_factory, eigen_compat
     p1, v1, l1 = e.forward(x)
     p2, v2, l2 = e.forward_packed(bits, len(x), want_logits=True)
     assert np.array_equal(l1, l2) and np.array_equal(v1, v2) and np.array_equal(p1, p2)
+
+
+@pytest.mark.parametrize("board,n", [(19, 512), (19, 300), (9, 1024), (19, 24), (9, 5)])
+def test_persistent_trunk_matches_per_layer_launches(gpu_engine_factory, monkeypatch, board, n):
+    """The all-layers persistent launch (per-CTA progress counters between
+    layers) against one launch per layer of the same kernel: bit-identical.
+    19x19 batch 512 / 300 and 9x9 batch 1024 run as one launch; the small
+    batches fall back to one launch per layer in both engines."""
+    sd = weights.make_state_dict(board, 128, 10, seed=5, variant="perturbed")
+    x = host_lib.random_positions(board, n, 99, 250 if board == 19 else 60)
+    monkeypatch.setenv("MG_PIX_TRUNK", "0")
+    per_layer = gpu_engine_factory(sd, "bf16")
+    monkeypatch.delenv("MG_PIX_TRUNK")
+    trunk = gpu_engine_factory(sd, "bf16")
+    p0, v0, l0 = per_layer.forward(x)
+    for _ in range(3):  # repeated launches reuse the progress counters
+        p1, v1, l1 = trunk.forward(x)
+        assert np.array_equal(l0, l1) and np.array_equal(v0, v1) and np.array_equal(p0, p1)
+    rows = np.array([0, n // 2, n - 1])
+    _, ov, ol = _oracle_rows(sd, x, rows)
+    assert np.abs(l1[rows] - ol).max() < TOL["bf16"]
+    assert np.abs(v1[rows] - ov).max() < TOL["bf16"]
