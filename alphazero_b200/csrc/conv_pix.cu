@@ -79,9 +79,9 @@ constexpr int kMaxLayers = 44;      // layers per launch (kernel parameter space
 struct PixLayer {
     const float* bias;       // [128]
     const uint16_t* res_hi;  // residual stream [m_total][128] hi plane, or nullptr
-    const uint16_t* res_lo;  // and its fp16 remainder plane
+    const uint16_t* res_lo;  // and its fp16 remainder plane (16-pixel blocks, see lo_block)
     uint16_t* out16;         // output [m_total][128] (hi plane), or nullptr
-    uint16_t* out_lo;        // its fp16 remainder plane, or nullptr
+    uint16_t* out_lo;        // its fp16 remainder plane (16-pixel blocks), or nullptr
     int cin;                 // 64 or 128
     int xmap;                // activation tensor map of the input slabs (0..2)
     int wmap;                // weight tensor map (0 or 1)
@@ -154,6 +154,16 @@ __device__ __forceinline__ float from16<true>(uint16_t h) {
 }
 __device__ __forceinline__ float lo_value(uint16_t l) { return __half2float(__ushort_as_half(l)); }
 __device__ __forceinline__ uint16_t lo_bits(float r) { return __half_as_ushort(__float2half_rn(r)); }
+
+// The lo plane is read and written only by the epilogue, one channel per
+// lane and 16 pixels at a time, so it is stored in 16-pixel blocks:
+// element (pixel px, channel c) at (px / 16) * 16 * 128 + c * 16 + px % 16.
+// A lane's 16 values of a chunk are then 32 contiguous bytes (two 16-byte
+// accesses instead of sixteen 2-byte ones).  Chunks start at multiples of
+// 16 pixels; the plane holds whole blocks (rows rounded up to 16).
+__device__ __forceinline__ size_t lo_block(int px0, int co) {
+    return (size_t)(px0 >> 4) * (16 * kCo) + (size_t)co * 16;
+}
 
 // n / d for 0 <= n < 2^23 and d <= 1200 (the launcher checks both).
 __device__ __forceinline__ int div_magic(int n, uint64_t magic) {
@@ -229,23 +239,20 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
     const bool has_lo = out_lo != nullptr;
     // Residual of the next chunk (tile order position lq, chunk lc),
     // loaded one chunk ahead into registers.
-    uint16_t nh[kChunk], nl[kChunk];
+    uint16_t nh[kChunk];
+    uint4 nl0, nl1;  // lo values of pixels 0-7 and 8-15, two per word
     auto load_res = [&](int px) {
         const uint16_t* ph = res_hi + (size_t)px * kCo + co;
-        const uint16_t* pl = res_lo + (size_t)px * kCo + co;
+        const uint16_t* pl = res_lo + lo_block(px, co);
+        nl0 = ld_cg_v4_early(pl);
+        nl1 = ld_cg_v4_early(pl + 8);
         if (px + kChunk <= G.m_total) {
 #pragma unroll
-            for (int j = 0; j < kChunk; ++j) {
-                nh[j] = ld_cg_u16_early(ph + j * kCo);
-                nl[j] = ld_cg_u16_early(pl + j * kCo);
-            }
+            for (int j = 0; j < kChunk; ++j) nh[j] = ld_cg_u16_early(ph + j * kCo);
         } else {
 #pragma unroll
-            for (int j = 0; j < kChunk; ++j) {
-                const bool in = px + j < G.m_total;
-                nh[j] = in ? ld_cg_u16_early(ph + j * kCo) : (uint16_t)0;
-                nl[j] = in ? ld_cg_u16_early(pl + j * kCo) : (uint16_t)0;
-            }
+            for (int j = 0; j < kChunk; ++j)
+                nh[j] = px + j < G.m_total ? ld_cg_u16_early(ph + j * kCo) : (uint16_t)0;
         }
     };
     // Advances (lq, lc) to this warp's next chunk of the layer.
@@ -288,9 +295,11 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
             tmem_ld_16cols(tcol + (uint32_t)(c * kChunk), v);
             float f[16];
             if (has_res) {
+                const uint32_t lw[8] = {nl0.x, nl0.y, nl0.z, nl0.w, nl1.x, nl1.y, nl1.z, nl1.w};
 #pragma unroll
                 for (int j = 0; j < kChunk; ++j)
-                    f[j] = from16<FP16>(nh[j]) + lo_value(nl[j]);
+                    f[j] = from16<FP16>(nh[j]) +
+                           lo_value((uint16_t)(lw[j >> 1] >> (16 * (j & 1))));
                 if (lvalid) {  // next chunk's residual, in flight during this one
                     int m1, len1;
                     tile_rows(G, blockIdx.x, tile_at(blockIdx.x, lq, nt), m1, len1);
@@ -318,15 +327,20 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
             }
             if (!HEAD) {
                 uint16_t* oh = out16 + (size_t)px0 * kCo + co;
-                uint16_t* ol = out_lo + (size_t)px0 * kCo + co;
                 const int nrow = min(kChunk, G.m_total - px0);
+                uint32_t lw[8];
 #pragma unroll
                 for (int j = 0; j < kChunk; ++j) {
-                    if (j < nrow) {
-                        const uint16_t h = to16<FP16>(f[j]);
-                        oh[j * kCo] = h;
-                        if (has_lo) ol[j * kCo] = lo_bits(f[j] - from16<FP16>(h));
-                    }
+                    const uint16_t h = to16<FP16>(f[j]);
+                    if (j < nrow) oh[j * kCo] = h;
+                    // rows past the end (f = 0) fill the last block
+                    const uint32_t lb = lo_bits(f[j] - from16<FP16>(h));
+                    lw[j >> 1] = (j & 1) ? (lw[j >> 1] | (lb << 16)) : lb;
+                }
+                if (has_lo) {
+                    uint4* ol = reinterpret_cast<uint4*>(out_lo + lo_block(px0, co));
+                    ol[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                    ol[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
                 }
             } else {
                 // Policy / value 1x1 convs of the chunk's 16 pixels:

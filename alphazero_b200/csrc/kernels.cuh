@@ -65,8 +65,10 @@ struct ConvLayer {
     // hi = x rounded to the operand type (the next layer reads it as its
     // input), lo = the remainder x - hi rounded to fp16.
     const void* res_hi;     // [m_total][cout] operand type or nullptr (may equal out16)
-    const uint16_t* res_lo; // [m_total][cout] fp16 (may equal out_lo)
-    uint16_t* out_lo;       // [m_total][cout] fp16 remainder of out16, or nullptr
+    // lo is stored in 16-pixel blocks, element (px, c) at
+    // (px / 16) * 16 * cout + c * 16 + px % 16, rows rounded up to 16.
+    const uint16_t* res_lo; // fp16, 16-pixel blocks (may equal out_lo)
+    uint16_t* out_lo;       // fp16 remainder of out16, 16-pixel blocks, or nullptr
     const float* head_w;    // [3][cout] or nullptr: fused head projection
     const float* head_b;    // [3]
     float* feat;            // [positions][3*B*B]

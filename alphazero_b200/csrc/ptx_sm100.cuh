@@ -128,6 +128,15 @@ __device__ __forceinline__ uint16_t ld_cg_u16_early(const uint16_t* p) {
     return v;
 }
 
+// 16-byte global load cached in L2 only, issued where it is written.
+__device__ __forceinline__ uint4 ld_cg_v4_early(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start
 // its prologue, and wait until the previous kernel's results are visible.
 // Both are no-ops for kernels launched without the programmatic attribute.
