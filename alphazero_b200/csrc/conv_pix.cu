@@ -319,7 +319,7 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
                 onb = (y < G.board) && (qq - y * G.rs < G.board);
             }
             const uint32_t board_mask = __ballot_sync(0xffffffffu, onb) & 0xffffu;
-            tmem_ld_wait();
+            tmem_ld_wait(v);
 #pragma unroll
             for (int j = 0; j < kChunk; ++j) {
                 const float x = __uint_as_float(v[j]) + bias + f[j];

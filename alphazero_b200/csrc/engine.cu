@@ -118,7 +118,7 @@ struct mg_engine {
     // an fp16 remainder plane (lo), which lives in d_x's storage there.
     void* d_t = nullptr;      // block-internal activation, operand type
     float* d_feat = nullptr;  // head features [positions][3*hw]
-    float* d_fc = nullptr;    // FC outputs [positions][actions + hidden]
+    float* d_fc = nullptr;    // FC partial sums [kHeadsFcSplits][positions][actions + hidden]
     float* d_states = nullptr;
     float* d_probs = nullptr;
     float* d_logits = nullptr;
@@ -366,7 +366,8 @@ struct mg_engine {
         d_x16 = dalloc<uint16_t>(rows * cpad, "cudaMalloc(act x16)");
         d_t = dalloc<uint8_t>(rows * cpad * elem, "cudaMalloc(act t)");
         d_feat = dalloc<float>((size_t)max_batch * 3 * hw, "cudaMalloc(feat)");
-        d_fc = dalloc<float>((size_t)max_batch * (actions + net.hidden), "cudaMalloc(fc)");
+        d_fc = dalloc<float>((size_t)kHeadsFcSplits * max_batch * (actions + net.hidden),
+                             "cudaMalloc(fc)");
         d_states = dalloc<float>((size_t)max_batch * planes * hw, "cudaMalloc(states)");
         ck(cudaMemset(d_states, 0, (size_t)max_batch * planes * hw * sizeof(float)),
            "cudaMemset(states)");
@@ -1052,7 +1053,7 @@ size_t noalloc_layout(const mg_engine* e, int n, unsigned char* base, NoAllocBuf
     const size_t o_x16 = take(rows * e->cpad * 2);
     const size_t o_t = take(rows * e->cpad * elem);
     const size_t o_feat = take((size_t)n * 3 * e->hw * 4);
-    const size_t o_fc = take((size_t)n * (e->actions + e->net.hidden) * 4);
+    const size_t o_fc = take((size_t)kHeadsFcSplits * n * (e->actions + e->net.hidden) * 4);
     const size_t o_log = take((size_t)n * e->actions * 4);
     const size_t o_err = take(sizeof(int));
     if (base != nullptr && off <= kNoAllocArenaBytes) {

@@ -155,8 +155,12 @@ struct HeadFc {
     const float* v2_w;  // [hidden]
     const float* v2_b;  // [1]
 };
+// The FC sums run in kHeadsFcSplits fixed K slices; scratch holds their
+// partial sums, and then (slice 0's rows) the finished FC outputs.
+constexpr int kHeadsFcSplits = 2;
 cudaError_t launch_heads_fc(const float* feat, const HeadFc& h, int positions,
-                            float* scratch /* [positions][actions + hidden] */, float* probs,
+                            float* scratch /* [kHeadsFcSplits][positions][actions + hidden] */,
+                            float* probs,
                             float* logits, float* value, cudaStream_t stream);
 
 }  // namespace mgb

@@ -299,6 +299,17 @@ __device__ __forceinline__ void tmem_ld_16cols(uint32_t taddr, uint32_t (&v)[16]
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// The same wait, naming the registers a tcgen05.ld writes: as far as the
+// compiler knows they are produced here, so no use of them can be
+// scheduled above the wait.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&v)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]),
+                   "+r"(v[6]), "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]),
+                   "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+                 :
+                 : "memory");
+}
 
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA
 // with 128-byte swizzling: rows of 128 bytes (64 16-bit elements), 8-row

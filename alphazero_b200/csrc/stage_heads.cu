@@ -145,34 +145,41 @@ __global__ void head_projection_kernel(const float* __restrict__ trunk, int posi
     }
 }
 
-constexpr int kFcTM = 32;  // positions per tile
-constexpr int kFcTO = 32;  // outputs per tile
-constexpr int kFcTK = 64;  // K slice
+constexpr int kFcTN = 64;  // positions per tile
+constexpr int kFcTO = 64;  // outputs per tile
+constexpr int kFcTK = 32;  // K per shared-memory stage
 
-// out[n][o] = sum_k feat[n][k] * W[o][k] + b[o] for a 32 x 32 tile, each of
-// 256 threads owning 2 positions x 2 outputs.  K slices of 64 are staged in
-// shared memory while the next slice is already being fetched into
-// registers.  Output tiles that lie wholly in the policy (o < actions) or
-// value (o >= actions) rows only walk their own K block.
+// Partial sums of out[n][o] = sum_k feat[n][k] * W[o][k] over K slice
+// blockIdx.z (of kHeadsFcSplits fixed slices) for a 64 x 64 tile; 256
+// threads each own 4 positions x 4 outputs and read them from shared
+// memory as float4s (2 shared loads per 16 FMAs).  K stages of 32 are
+// double-buffered in shared memory while the next stage is fetched into
+// registers (coalesced: a warp reads 32 consecutive k of one row).  Output
+// tiles that lie wholly in the policy (o < actions) or value (o >= actions)
+// rows only walk their own K block.  The slicing depends on nothing but
+// the network, so a position's sums do not depend on the batch it is in.
 __global__ void __launch_bounds__(256) heads_fc_kernel(const float* __restrict__ feat, HeadFc h,
                                                        int positions, float* __restrict__ out) {
-    __shared__ float sF[kFcTK][kFcTM + 1];
-    __shared__ float sW[kFcTK][kFcTO + 1];
+    __shared__ __align__(16) float sF[2][kFcTK][kFcTN + 4];
+    __shared__ __align__(16) float sW[2][kFcTK][kFcTO + 4];
     const int K = 3 * h.hw;
     const int O = h.actions + h.hidden;
-    const int n0 = blockIdx.x * kFcTM;
+    const int n0 = blockIdx.x * kFcTN;
     const int o0 = blockIdx.y * kFcTO;
-    const int kbeg = (o0 >= h.actions) ? 2 * h.hw : 0;
-    const int kend = (o0 + kFcTO <= h.actions) ? 2 * h.hw : K;
+    const int kb = (o0 >= h.actions) ? 2 * h.hw : 0;
+    const int ke = (o0 + kFcTO <= h.actions) ? 2 * h.hw : K;
+    const int slice = (ke - kb + kHeadsFcSplits - 1) / kHeadsFcSplits;
+    const int kbeg = kb + blockIdx.z * slice;
+    const int kend = min(ke, kbeg + slice);
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    // Each thread stages 8 feature and 8 weight values per slice: element
-    // (row r = idx / 64, k = idx % 64) for idx = threadIdx.x + i * 256.
+    // Each thread stages 8 feature and 8 weight values per stage: element
+    // (row r = idx / 32, k = idx % 32) for idx = threadIdx.x + i * 256.
     float pF[8], pW[8];
     auto fetch = [&](int k0) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int idx = threadIdx.x + i * 256;
-            const int r = idx >> 6, k = idx & 63;
+            const int r = idx >> 5, k = idx & 31;
             const int kk = k0 + k;
             const bool kin = kk < kend;
             const int n = n0 + r, o = o0 + r;
@@ -180,51 +187,74 @@ __global__ void __launch_bounds__(256) heads_fc_kernel(const float* __restrict__
             pW[i] = (kin && o < O) ? h.w[(size_t)o * K + kk] : 0.f;
         }
     };
-    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-    fetch(kbeg);
-    for (int k0 = kbeg; k0 < kend; k0 += kFcTK) {
+    auto stage = [&](int buf) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int idx = threadIdx.x + i * 256;
-            const int r = idx >> 6, k = idx & 63;
-            sF[k][r] = pF[i];
-            sW[k][r] = pW[i];
+            const int r = idx >> 5, k = idx & 31;
+            sF[buf][k][r] = pF[i];
+            sW[buf][k][r] = pW[i];
         }
-        __syncthreads();
-        if (k0 + kFcTK < kend) fetch(k0 + kFcTK);
-#pragma unroll 16
-        for (int k = 0; k < kFcTK; ++k) {
-            const float a0 = sF[k][ty * 2], a1 = sF[k][ty * 2 + 1];
-            const float w0 = sW[k][tx * 2], w1 = sW[k][tx * 2 + 1];
-            acc[0][0] = fmaf(a0, w0, acc[0][0]);
-            acc[0][1] = fmaf(a0, w1, acc[0][1]);
-            acc[1][0] = fmaf(a1, w0, acc[1][0]);
-            acc[1][1] = fmaf(a1, w1, acc[1][1]);
-        }
+    };
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    int buf = 0;
+    if (kbeg < kend) {
+        fetch(kbeg);
+        stage(0);
         __syncthreads();
     }
+    for (int k0 = kbeg; k0 < kend; k0 += kFcTK, buf ^= 1) {
+        const bool more = k0 + kFcTK < kend;
+        if (more) fetch(k0 + kFcTK);
+#pragma unroll 8
+        for (int k = 0; k < kFcTK; ++k) {
+            const float4 a = *reinterpret_cast<const float4*>(&sF[buf][k][ty * 4]);
+            const float4 w = *reinterpret_cast<const float4*>(&sW[buf][k][tx * 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int n = n0 + ty * 2 + i;
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+        }
+        // The other buffer was last read in the previous stage, which every
+        // thread has finished (the barrier at the end of that stage).
+        if (more) stage(buf ^ 1);
+        __syncthreads();
+    }
+    float* o_base = out + (size_t)blockIdx.z * positions * O;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int n = n0 + ty * 4 + i;
         if (n >= positions) continue;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int o = o0 + tx * 2 + j;
-            if (o < O) out[(size_t)n * O + o] = acc[i][j] + h.b[o];
+        for (int j = 0; j < 4; ++j) {
+            const int o = o0 + tx * 4 + j;
+            if (o < O) o_base[(size_t)n * O + o] = acc[i][j];
         }
     }
 }
 
 // One warp per position: softmax of the logits and the value head's last
 // two steps (ReLU of FC1, FC2, tanh).
-__global__ void heads_finish_kernel(const float* __restrict__ fc, HeadFc h, int positions,
+__global__ void heads_finish_kernel(float* __restrict__ fc, HeadFc h, int positions,
                                     float* __restrict__ probs, float* __restrict__ logits,
                                     float* __restrict__ value) {
     const int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (n >= positions) return;
     const int A = h.actions, O = h.actions + h.hidden;
-    const float* l = fc + (size_t)n * O;
+    // Bias plus the K-slice partial sums, always added in the same order.
+    float* l = fc + (size_t)n * O;
+    for (int o = lane; o < O; o += 32) {
+        float x = h.b[o];
+        for (int sl = 0; sl < kHeadsFcSplits; ++sl) x += fc[((size_t)sl * positions + n) * O + o];
+        l[o] = x;
+    }
+    __syncwarp();
     float mx = -INFINITY;
     for (int a = lane; a < A; a += 32) mx = fmaxf(mx, l[a]);
     mx = warp_max(mx);
@@ -314,7 +344,8 @@ cudaError_t launch_head_projection(const float* trunk, int positions, int c, con
 cudaError_t launch_heads_fc(const float* feat, const HeadFc& h, int positions, float* scratch,
                             float* probs, float* logits, float* value, cudaStream_t stream) {
     if (positions == 0) return cudaSuccess;
-    dim3 grid((positions + kFcTM - 1) / kFcTM, (h.actions + h.hidden + kFcTO - 1) / kFcTO);
+    dim3 grid((positions + kFcTN - 1) / kFcTN, (h.actions + h.hidden + kFcTO - 1) / kFcTO,
+              kHeadsFcSplits);
     heads_fc_kernel<<<grid, 256, 0, stream>>>(feat, h, positions, scratch);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
