@@ -17,7 +17,7 @@
 //
 // The accumulator is [co lanes][px columns] in TMEM, double-buffered across
 // tiles (2 x 256 columns).  Each epilogue warp works on its own: it owns 32
-// channels (its TMEM lanes) of every other 16-pixel chunk and moves them
+// channels (its TMEM lanes) of every third 16-pixel chunk and moves them
 // straight between registers and global memory (lane = channel, so each
 // 16-bit access of a warp covers 64 contiguous bytes of a pixel row).  The
 // residual stream is a pair of 16-bit planes, x = hi + lo with hi = x
@@ -28,10 +28,11 @@
 // trunk layer the fp32 sums go through shared memory to the policy / value
 // 1x1 head projection instead.
 //
-// Warp roles (352 threads): warp 0 weight TMA producer, warp 1 TMEM
-// allocator + MMA issuer, warps 2-9 epilogue (warp w reads TMEM lanes
-// [32*(w%4), +32) of chunks (w-2)/4, (w-2)/4 + 2, ...), warp 10 activation
-// slab TMA producer (two slab buffers).  All waits are bounded.
+// Warp roles (480 threads): warp 0 weight TMA producer, warp 1 TMEM
+// allocator + MMA issuer, warps 2-13 epilogue (warp w reads TMEM lanes
+// [32*(w%4), +32) of chunks (w-2)/4, (w-2)/4 + 3, ...; three warps per lane
+// quarter hide more of each other's latency than two did), warp 14
+// activation slab TMA producer (two slab buffers).  All waits are bounded.
 //
 // Work split: CTA b owns the contiguous pixel range [b*span, (b+1)*span) in
 // every layer, cut into equal tiles of at most 256 pixels, so every SM gets
@@ -41,7 +42,7 @@
 // Several layers in one launch (a cooperative launch, so every CTA is
 // resident): a tile of layer l reads layer l-1's rows [m0 - RS - 1, m0 + len
 // + RS + 1), i.e. the CTA's own neighbouring tiles and, at the ends of its
-// range, the nearest tiles of the neighbouring CTAs.  After all 8 epilogue
+// range, the nearest tiles of the neighbouring CTAs.  After all 12 epilogue
 // warps have stored a tile, the CTA publishes its count of finished tiles
 // (release, GPU scope); the slab producer waits (acquire) until the tiles
 // it needs are counted before loading a slab.  The same wait covers the
@@ -67,11 +68,12 @@ constexpr int kBK = 64;         // K per stage / slab channel block
 constexpr int kMaxPx = 256;     // MMA N limit
 constexpr int kStages = 5;      // weight ring depth
 constexpr int kSlabs = 2;       // activation slab ring depth
-constexpr int kThreads = 352;
+constexpr int kEpiWarps = 12;   // epilogue warps: kPar per TMEM lane quarter
+constexpr int kPar = kEpiWarps / 4;
+constexpr int kThreads = 32 * (3 + kEpiWarps);
 constexpr int kChunk = 16;      // pixels per epilogue chunk
 constexpr uint32_t kWBytes = kCo * kBK * 2;            // 16 KB weight stage
 constexpr int kSlot = kChunk * 32;  // one warp's chunk: 16 pixels x 32 channels
-constexpr int kEpiWarps = 8;
 constexpr int kMagicShift = 40;     // n / d == (n * ceil(2^40 / d)) >> 40 here
 constexpr int kMaxLayers = 44;      // layers per launch (kernel parameter space)
 
@@ -217,8 +219,8 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
                                                uint32_t tmem_base, float* hslot, const float* shead,
                                                int warp, int lane) {
     const int quarter = warp & 3;  // channels [32*quarter, +32)
-    const int ew = warp - 2;       // 0..7
-    const int par = ew >> 2;       // chunks par, par+2, ...
+    const int ew = warp - 2;       // 0..kEpiWarps-1
+    const int par = ew >> 2;       // chunks par, par+kPar, ...
     const int co = quarter * 32 + lane;
     const int hw = G.board * G.board;
     int* const err = a.err;
@@ -257,7 +259,7 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
     };
     // Advances (lq, lc) to this warp's next chunk of the layer.
     auto next_chunk = [&](int& lq, int& lc) {
-        lc += 2;
+        lc += kPar;
         while (lq < nt) {
             int m, n;
             tile_rows(G, blockIdx.x, tile_at(blockIdx.x, lq, nt), m, n);
@@ -267,7 +269,7 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
         }
         return false;
     };
-    int lq = 0, lc = par - 2;
+    int lq = 0, lc = par - kPar;
     bool lvalid = next_chunk(lq, lc);
     if (has_res && lvalid) {
         int m, n;
@@ -289,7 +291,7 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
         const uint32_t tcol =
             tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kMaxPx);
 #pragma unroll 1
-        for (int c = par; c < nchunks; c += 2) {
+        for (int c = par; c < nchunks; c += kPar) {
             const int px0 = m0 + c * kChunk;
             uint32_t v[16];
             tmem_ld_16cols(tcol + (uint32_t)(c * kChunk), v);
@@ -389,7 +391,7 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
         tc_fence_before();
         if (progress != nullptr) {
             // This warp's stores of the tile are done; the last of the
-            // 8 warps publishes the CTA's count of finished tiles.
+            // epilogue warps publishes the CTA's count of finished tiles.
             fence_proxy_async_global();
             __threadfence();
             __syncwarp();
@@ -619,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ---------------- epilogue (warps 2..9) ----------------
-        // Each warp finishes its 32 channels (its TMEM lanes) of every other
+        // Each warp finishes its 32 channels (its TMEM lanes) of every third
         // chunk on its own, straight between registers and global memory.
         // Only the head-projection layer, which sums over all 128 channels,
         // couples the warps (through shared memory).
