@@ -157,7 +157,7 @@ struct HeadFc {
 };
 // The FC sums run in kHeadsFcSplits fixed K slices; scratch holds their
 // partial sums, and then (slice 0's rows) the finished FC outputs.
-constexpr int kHeadsFcSplits = 2;
+constexpr int kHeadsFcSplits = 6;
 cudaError_t launch_heads_fc(const float* feat, const HeadFc& h, int positions,
                             float* scratch /* [kHeadsFcSplits][positions][actions + hidden] */,
                             float* probs,

@@ -20,18 +20,67 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, ActType t) {
 // planes of the row's pixel (strided across planes, coalesced across rows)
 // and writes them as one 16-byte (16-bit types) or 32-byte (fp32) vector;
 // channels >= planes, frame pixels and absent positions are zero.
+// Frame geometry of a staging launch with the divisions by IS and RS done as
+// multiply-shifts: n / d == (n * ceil(2^40 / d)) >> 40 for every row index
+// below 2^23 and d <= 1200 (checked by the launchers).
+struct StageGeom {
+    FrameGeom g;
+    uint64_t is_magic, rs_magic;
+    int gshift;  // log2(cpad / 8)
+};
+
+StageGeom stage_geom(const FrameGeom& g, int cpad) {
+    StageGeom s;
+    s.g = g;
+    s.is_magic = ((1ull << 40) + (uint64_t)g.is - 1) / (uint64_t)g.is;
+    s.rs_magic = ((1ull << 40) + (uint64_t)g.rs - 1) / (uint64_t)g.rs;
+    s.gshift = 0;
+    while ((8 << s.gshift) < cpad) ++s.gshift;
+    return s;
+}
+
+bool stage_geom_ok(const FrameGeom& g, int cpad, int rows) {
+    return cpad >= 8 && (cpad & (cpad - 1)) == 0 && g.is <= 1200 && rows < (1 << 23);
+}
+
+__device__ __forceinline__ int stage_div(int n, uint64_t magic) {
+    return (int)(((uint64_t)(uint32_t)n * magic) >> 40);
+}
+
+// Row m = idx >> gshift, channels [c8, c8 + 8) of a staging thread; returns
+// false for a thread past the end.  Groups at or past `planes` only hold
+// zeros and are written here without the frame arithmetic.
+template <ActType T>
+__device__ __forceinline__ bool stage_thread(const StageGeom& sg, int rows, int planes, int cpad,
+                                             void* out, int& m, int& c8) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    m = idx >> sg.gshift;
+    c8 = (idx - (m << sg.gshift)) * 8;
+    if (m >= rows) return false;
+    if (c8 >= planes) {
+        if (T == ActType::FP32) {
+            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)m * cpad + c8);
+            o[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+            o[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + (size_t)m * cpad + c8) =
+                make_uint4(0u, 0u, 0u, 0u);
+        }
+        return false;
+    }
+    return true;
+}
+
 template <ActType T>
 __global__ void stage_input_kernel(const float* __restrict__ states, int n_valid, int rows,
-                                   int planes, FrameGeom g, int cpad, int eigen_order,
+                                   int planes, StageGeom sg, int cpad, int eigen_order,
                                    void* __restrict__ out) {
-    const int groups = cpad >> 3;
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    const int m = idx / groups;
-    const int c8 = (idx - m * groups) * 8;
-    if (m >= rows) return;
-    const int n = m / g.is;
+    int m, c8;
+    if (!stage_thread<T>(sg, rows, planes, cpad, out, m, c8)) return;
+    const FrameGeom& g = sg.g;
+    const int n = stage_div(m, sg.is_magic);
     const int q = m - n * g.is;
-    const int y = q / g.rs;
+    const int y = stage_div(q, sg.rs_magic);
     const int x = q - y * g.rs;
     const bool live = (n < n_valid) && (y < g.board) && (x < g.board);
     const int hw = g.board * g.board;
@@ -63,16 +112,14 @@ __global__ void stage_input_kernel(const float* __restrict__ states, int n_valid
 // words_per_pos words.
 template <ActType T>
 __global__ void stage_bits_kernel(const uint32_t* __restrict__ bits, int words_per_pos, int n_valid,
-                                  int rows, int planes, FrameGeom g, int cpad, int eigen_order,
+                                  int rows, int planes, StageGeom sg, int cpad, int eigen_order,
                                   void* __restrict__ out) {
-    const int groups = cpad >> 3;
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    const int m = idx / groups;
-    const int c8 = (idx - m * groups) * 8;
-    if (m >= rows) return;
-    const int n = m / g.is;
+    int m, c8;
+    if (!stage_thread<T>(sg, rows, planes, cpad, out, m, c8)) return;
+    const FrameGeom& g = sg.g;
+    const int n = stage_div(m, sg.is_magic);
     const int q = m - n * g.is;
-    const int y = q / g.rs;
+    const int y = stage_div(q, sg.rs_magic);
     const int x = q - y * g.rs;
     const bool live = (n < n_valid) && (y < g.board) && (x < g.board);
     const int hw = g.board * g.board;
@@ -238,39 +285,54 @@ __global__ void __launch_bounds__(256) heads_fc_kernel(const float* __restrict__
     }
 }
 
-// One warp per position: softmax of the logits and the value head's last
-// two steps (ReLU of FC1, FC2, tanh).
-__global__ void heads_finish_kernel(float* __restrict__ fc, HeadFc h, int positions,
-                                    float* __restrict__ probs, float* __restrict__ logits,
-                                    float* __restrict__ value) {
-    const int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (n >= positions) return;
+// One 128-thread block per position: the FC outputs (bias plus the K-slice
+// partial sums, added in a fixed order), a max-subtracted softmax of the
+// logits, and the value head's last two steps (ReLU of FC1, FC2, tanh).
+constexpr int kFinishThreads = 128;
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
+    v = is_max ? warp_max(v) : warp_sum(v);
+    const int w = threadIdx.x >> 5;
+    __syncthreads();  // red may still be read by the previous reduction
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    v = red[0];
+#pragma unroll
+    for (int i = 1; i < kFinishThreads / 32; ++i) v = is_max ? fmaxf(v, red[i]) : v + red[i];
+    return v;
+}
+
+__global__ void __launch_bounds__(kFinishThreads)
+    heads_finish_kernel(float* __restrict__ fc, HeadFc h, int positions, float* __restrict__ probs,
+                        float* __restrict__ logits, float* __restrict__ value) {
+    __shared__ float red[kFinishThreads / 32];
+    const int n = blockIdx.x;
     const int A = h.actions, O = h.actions + h.hidden;
-    // Bias plus the K-slice partial sums, always added in the same order.
+    // Finished outputs overwrite slice 0's row of this position.
     float* l = fc + (size_t)n * O;
-    for (int o = lane; o < O; o += 32) {
+    for (int o = threadIdx.x; o < O; o += kFinishThreads) {
         float x = h.b[o];
         for (int sl = 0; sl < kHeadsFcSplits; ++sl) x += fc[((size_t)sl * positions + n) * O + o];
         l[o] = x;
     }
-    __syncwarp();
+    __syncthreads();
     float mx = -INFINITY;
-    for (int a = lane; a < A; a += 32) mx = fmaxf(mx, l[a]);
-    mx = warp_max(mx);
+    for (int a = threadIdx.x; a < A; a += kFinishThreads) mx = fmaxf(mx, l[a]);
+    mx = block_reduce(mx, true, red);
     float sum = 0.f;
-    for (int a = lane; a < A; a += 32) sum += expf(l[a] - mx);
-    sum = warp_sum(sum);
+    for (int a = threadIdx.x; a < A; a += kFinishThreads) sum += expf(l[a] - mx);
+    sum = block_reduce(sum, false, red);
     const float inv = 1.0f / sum;
-    for (int a = lane; a < A; a += 32) {
+    for (int a = threadIdx.x; a < A; a += kFinishThreads) {
         const float la = l[a];
         probs[(size_t)n * A + a] = expf(la - mx) * inv;
         logits[(size_t)n * A + a] = la;
     }
     float v = 0.f;
-    for (int j = lane; j < h.hidden; j += 32) v = fmaf(fmaxf(l[A + j], 0.f), h.v2_w[j], v);
-    v = warp_sum(v);
-    if (lane == 0) value[n] = tanhf(v + h.v2_b[0]);
+    for (int j = threadIdx.x; j < h.hidden; j += kFinishThreads)
+        v = fmaf(fmaxf(l[A + j], 0.f), h.v2_w[j], v);
+    v = block_reduce(v, false, red);
+    if (threadIdx.x == 0) value[n] = tanhf(v + h.v2_b[0]);
 }
 
 }  // namespace
@@ -278,25 +340,26 @@ __global__ void heads_finish_kernel(float* __restrict__ fc, HeadFc h, int positi
 cudaError_t launch_stage_input(const float* states, int n_valid, int n_pos, int planes,
                                const FrameGeom& g, int cpad, bool eigen_order, ActType t,
                                void* out, cudaStream_t stream) {
-    if (cpad % 8 != 0) return cudaErrorInvalidValue;
     const long threads_total = (long)n_pos * g.is * (cpad / 8);
     const int threads = 256;
     const long blocks = (threads_total + threads - 1) / threads;
     if (blocks == 0) return cudaSuccess;
     const int rows = n_pos * g.is;
+    if (!stage_geom_ok(g, cpad, rows)) return cudaErrorInvalidValue;
+    const StageGeom sg = stage_geom(g, cpad);
     const int eo = eigen_order ? 1 : 0;
     switch (t) {
         case ActType::BF16:
             stage_input_kernel<ActType::BF16><<<(unsigned)blocks, threads, 0, stream>>>(
-                states, n_valid, rows, planes, g, cpad, eo, out);
+                states, n_valid, rows, planes, sg, cpad, eo, out);
             break;
         case ActType::FP16:
             stage_input_kernel<ActType::FP16><<<(unsigned)blocks, threads, 0, stream>>>(
-                states, n_valid, rows, planes, g, cpad, eo, out);
+                states, n_valid, rows, planes, sg, cpad, eo, out);
             break;
         case ActType::FP32:
             stage_input_kernel<ActType::FP32><<<(unsigned)blocks, threads, 0, stream>>>(
-                states, n_valid, rows, planes, g, cpad, eo, out);
+                states, n_valid, rows, planes, sg, cpad, eo, out);
             break;
     }
     return cudaGetLastError();
@@ -305,25 +368,26 @@ cudaError_t launch_stage_input(const float* states, int n_valid, int n_pos, int 
 cudaError_t launch_stage_bits(const uint32_t* bits, int words_per_pos, int n_valid, int n_pos,
                               int planes, const FrameGeom& g, int cpad, bool eigen_order, ActType t,
                               void* out, cudaStream_t stream) {
-    if (cpad % 8 != 0) return cudaErrorInvalidValue;
     const long threads_total = (long)n_pos * g.is * (cpad / 8);
     const int threads = 256;
     const long blocks = (threads_total + threads - 1) / threads;
     if (blocks == 0) return cudaSuccess;
     const int rows = n_pos * g.is;
+    if (!stage_geom_ok(g, cpad, rows)) return cudaErrorInvalidValue;
+    const StageGeom sg = stage_geom(g, cpad);
     const int eo = eigen_order ? 1 : 0;
     switch (t) {
         case ActType::BF16:
             stage_bits_kernel<ActType::BF16><<<(unsigned)blocks, threads, 0, stream>>>(
-                bits, words_per_pos, n_valid, rows, planes, g, cpad, eo, out);
+                bits, words_per_pos, n_valid, rows, planes, sg, cpad, eo, out);
             break;
         case ActType::FP16:
             stage_bits_kernel<ActType::FP16><<<(unsigned)blocks, threads, 0, stream>>>(
-                bits, words_per_pos, n_valid, rows, planes, g, cpad, eo, out);
+                bits, words_per_pos, n_valid, rows, planes, sg, cpad, eo, out);
             break;
         case ActType::FP32:
             stage_bits_kernel<ActType::FP32><<<(unsigned)blocks, threads, 0, stream>>>(
-                bits, words_per_pos, n_valid, rows, planes, g, cpad, eo, out);
+                bits, words_per_pos, n_valid, rows, planes, sg, cpad, eo, out);
             break;
     }
     return cudaGetLastError();
@@ -349,9 +413,8 @@ cudaError_t launch_heads_fc(const float* feat, const HeadFc& h, int positions, f
     heads_fc_kernel<<<grid, 256, 0, stream>>>(feat, h, positions, scratch);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const int warps_per_block = 8;
-    heads_finish_kernel<<<(positions + warps_per_block - 1) / warps_per_block, warps_per_block * 32,
-                          0, stream>>>(scratch, h, positions, probs, logits, value);
+    heads_finish_kernel<<<positions, kFinishThreads, 0, stream>>>(scratch, h, positions, probs,
+                                                                  logits, value);
     return cudaGetLastError();
 }
 
