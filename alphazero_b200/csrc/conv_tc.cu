@@ -6,13 +6,18 @@
 //   K = 9 taps * input channels.
 // Because of the framed layout, the A tile of tap (dy, dx) for output rows
 // [m0, m0 + 128) is simply rows [m0 + dy*RS + dx, ... + 128) of the input
-// activation matrix, so every K block is one 2-D TMA box (64 channels x 128
-// rows, 128-byte swizzle) with no gather and no im2col buffer.  Weights are
-// [cout][9][cin], so a K block of B is a (64 x bn) box at column
-// tap*cin + channel block.
+// activation matrix.  Per 64-channel block the producer loads ONE slab of
+// the tile's rows plus a halo of RS + 1 rows on each side (one TMA box,
+// 128-byte swizzle), and the 9 taps read it through A descriptors whose
+// start row is shifted by dy*RS + dx (the MMA derives the swizzle phase from
+// the absolute shared-memory address, as TMA does when it writes the slab):
+// activations cross L2 -> SMEM once per block instead of nine times.
+// Weights are [cout][9][cin], so a K block of B is a (64 x bn) box at column
+// tap*cin + channel block; B stages stream through a ring.
 //
 // One persistent CTA per SM, warp-specialised:
-//   warp 0     TMA producer (one thread) filling a STAGES-deep smem ring;
+//   warp 0     TMA producer (one thread): two slab buffers and a
+//              STAGES-deep ring of B stages;
 //   warp 1     TMEM allocator and MMA issuer (one thread): 4 x
 //              tcgen05.mma.kind::f16 (128 x bn x 16) per K block, fp32
 //              accumulators in TMEM, double-buffered across tiles;
@@ -43,15 +48,18 @@ constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
 
 template <int BN>
 struct TcConfig {
-    static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-    static constexpr uint32_t kABytes = kBM * kBK * 2;
+    static constexpr int kStages = BN == 256 ? 5 : (BN == 128 ? 8 : 12);
     static constexpr uint32_t kBBytes = BN * kBK * 2;
-    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr uint32_t kTmemCols = 2 * BN;
-    // ring + barriers + tmem slot + bias (256 floats) + head weights
-    // (3 x 256 floats) + head exchange (2 x 128 x 3 floats) + 1 KB alignment slack
-    static constexpr int kSmem = kStages * kStageBytes + 256 + 1024 + 3072 + 3072 + 1024;
+    // B ring + barriers and tmem slot (512) + bias (256 floats) + head weights
+    // (3 x 256 floats) + head exchange (2 x 128 x 3 floats) + 1 KB alignment
+    // slack; the two slabs come on top (slab_bytes).
+    static constexpr int kSmemFixed = kStages * kBBytes + 512 + 1024 + 3072 + 3072 + 1024;
 };
+
+// Rows of an activation slab: the tile's 128 rows plus RS + 1 on each side,
+// rounded up to 16.
+__host__ __device__ constexpr int tc_slab_rows(int rs) { return (kBM + 2 * (rs + 1) + 15) / 16 * 16; }
 
 struct TcArgs {
     int m_total;
@@ -108,15 +116,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + S * Cfg::kABytes;
+    const int halo = a.rs + 1;
+    const uint32_t slab_bytes = (uint32_t)tc_slab_rows(a.rs) * 128u;
+    uint8_t* sSlab = smem;                   // 2 slabs (multiples of 2 KB: atoms stay aligned)
+    uint8_t* sB = smem + 2 * slab_bytes;     // S B stages
     uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
     uint64_t* full = bars;
     uint64_t* empty = bars + S;
     uint64_t* tfull = bars + 2 * S;
     uint64_t* tempty = bars + 2 * S + 2;
     uint64_t* done = bars + 2 * S + 4;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+    uint64_t* sfull = bars + 2 * S + 5;
+    uint64_t* sempty = sfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + 2);
     float* sbias = reinterpret_cast<float*>(tmem_slot + 4);
     float* shead = sbias + 256;  // [3][cout] fused head projection weights
     float* sxchg = shead + 768;  // [2][128][3] head partial-sum exchange
@@ -132,6 +144,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&tfull[i]), 1);
             mbar_init(smem_u32(&tempty[i]), 8);
+            mbar_init(smem_u32(&sfull[i]), 1);
+            mbar_init(smem_u32(&sempty[i]), 1);
         }
         mbar_init(smem_u32(done), 1);
         fence_barrier_init();
@@ -153,46 +167,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     griddep_wait();
 
     const int cblocks = a.cin / kBK;
-    const int kblocks = 9 * cblocks;
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             prefetch_tensormap(&tmA);
             prefetch_tensormap(&tmB);
-            int it = 0;
+            int it = 0, is = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
                 const int mt = tile / a.nsplit;
                 const int n0 = (tile - mt * a.nsplit) * BN;
                 const int m0 = mt * kBM;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
-                    const int tap = kb / cblocks;
-                    const int cb = kb - tap * cblocks;
-                    const int off = (tap / 3 - 1) * a.rs + (tap % 3 - 1);
-                    const int s = it % S;
-                    const uint32_t ph = ((it / S) & 1) ^ 1;
-                    if (!mbar_wait(smem_u32(&empty[s]), ph, a.err, kErrWaitProducer)) {
+                for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
+                    // the tile's halo slab of this channel block (rows before
+                    // the first or past the last come back as zeros)
+                    const int sb = is & 1;
+                    if (!mbar_wait(smem_u32(&sempty[sb]), ((is >> 1) & 1) ^ 1, a.err,
+                                   kErrWaitProducer)) {
                         ok = false;
                         break;
                     }
-                    const uint32_t fb = smem_u32(&full[s]);
-                    mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-                    tma_load_2d(smem_u32(sA + s * Cfg::kABytes), &tmA, fb, cb * kBK, m0 + off);
-                    tma_load_2d(smem_u32(sB + s * Cfg::kBBytes), &tmB, fb, tap * a.cin + cb * kBK,
-                                n0);
+                    mbar_arrive_expect_tx(smem_u32(&sfull[sb]), slab_bytes);
+                    tma_load_2d(smem_u32(sSlab + sb * slab_bytes), &tmA, smem_u32(&sfull[sb]),
+                                cb * kBK, m0 - halo);
+                    for (int tap = 0; tap < 9; ++tap, ++it) {
+                        const int s = it % S;
+                        const uint32_t ph = ((it / S) & 1) ^ 1;
+                        if (!mbar_wait(smem_u32(&empty[s]), ph, a.err, kErrWaitProducer)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t fb = smem_u32(&full[s]);
+                        mbar_arrive_expect_tx(fb, Cfg::kBBytes);
+                        tma_load_2d(smem_u32(sB + s * Cfg::kBBytes), &tmB, fb,
+                                    tap * a.cin + cb * kBK, n0);
+                    }
                 }
             }
-            // Drain: every copy issued into the ring has landed before exit.
+            // Drain: every copy issued has landed before exit.
             for (int j = (it > S ? it - S : 0); j < it; ++j)
                 mbar_wait(smem_u32(&full[j % S]), (j / S) & 1, a.err, kErrWaitDrain);
+            for (int j = (is > 2 ? is - 2 : 0); j < is; ++j)
+                mbar_wait(smem_u32(&sfull[j & 1]), (j >> 1) & 1, a.err, kErrWaitDrain);
         }
         __syncwarp();
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16(kBM, BN, !FP16);
-            int it = 0, t = 0;
+            int it = 0, is = 0, t = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++t) {
                 const int acc = t & 1;
@@ -202,22 +226,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
-                    const int s = it % S;
-                    if (!mbar_wait(smem_u32(&full[s]), (it / S) & 1, a.err, kErrWaitMma)) {
+                for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
+                    const int sb = is & 1;
+                    if (!mbar_wait(smem_u32(&sfull[sb]), (is >> 1) & 1, a.err, kErrWaitMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * Cfg::kABytes));
-                    const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * Cfg::kBBytes));
+                    const uint32_t slab = smem_u32(sSlab + sb * slab_bytes);
+                    for (int tap = 0; tap < 9; ++tap, ++it) {
+                        const int s = it % S;
+                        if (!mbar_wait(smem_u32(&full[s]), (it / S) & 1, a.err, kErrWaitMma)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        // A: the slab from the tap's shifted start row (whole
+                        // 128-byte rows, so no descriptor base offset)
+                        const int r0 = halo + (tap / 3 - 1) * a.rs + (tap % 3 - 1);
+                        const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * Cfg::kBBytes));
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k) {
-                        // advance 16 elements (32 bytes) along K inside the swizzle atom
-                        mma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
-                                (kb | k) != 0);
+                        for (int k = 0; k < kBK / 16; ++k) {
+                            // advance 16 elements (32 bytes) along K inside the swizzle atom
+                            const uint64_t ad =
+                                smem_desc_sw128(slab + (uint32_t)r0 * 128u + 32u * k);
+                            mma_f16(d, ad, bd + (uint64_t)(2 * k), idesc, (cb | tap | k) != 0);
+                        }
+                        mma_commit(smem_u32(&empty[s]));
                     }
-                    mma_commit(smem_u32(&empty[s]));
+                    if (ok) mma_commit(smem_u32(&sempty[sb]));
                 }
                 if (ok) mma_commit(smem_u32(&tfull[acc]));
             }
@@ -387,7 +424,8 @@ cudaError_t launch_bn(const ConvLayer& L, const CUtensorMap& tmA, const CUtensor
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cfg.dynamicSmemBytes = (size_t)Cfg::kSmemFixed + 2 * tc_slab_rows(L.g.rs) * 128;
+    if (cfg.dynamicSmemBytes > 227 * 1024 || tc_slab_rows(L.g.rs) > 256) return cudaErrorInvalidValue;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -435,7 +473,7 @@ bool encode_2d(CUtensorMap* map, bool fp16, const void* base, uint64_t inner, ui
 template <int BN, bool FP16>
 cudaError_t configure_one() {
     return cudaFuncSetAttribute(conv3x3_tc_kernel<BN, FP16>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, TcConfig<BN>::kSmem);
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
 }
 
 }  // namespace
@@ -450,11 +488,12 @@ cudaError_t configure_conv_tc() {
     return configure_one<256, true>();
 }
 
-int conv_tc_smem_bytes(int bn) {
+int conv_tc_smem_bytes(int bn, int rs) {
+    const int slabs = 2 * tc_slab_rows(rs) * 128;
     switch (bn) {
-        case 64: return TcConfig<64>::kSmem;
-        case 128: return TcConfig<128>::kSmem;
-        case 256: return TcConfig<256>::kSmem;
+        case 64: return TcConfig<64>::kSmemFixed + slabs;
+        case 128: return TcConfig<128>::kSmemFixed + slabs;
+        case 256: return TcConfig<256>::kSmemFixed + slabs;
         default: return -1;
     }
 }
@@ -465,7 +504,12 @@ bool make_conv_tensor_maps(const ConvLayer& L, int bn, bool fp16, CUtensorMap* t
         *why = "unsupported channel counts for the tensor-core convolution";
         return false;
     }
-    if (!encode_2d(tmA, fp16, L.in, (uint64_t)L.cin, (uint64_t)L.m_total, kBK, kBM, why))
+    if (tc_slab_rows(L.g.rs) > 256) {
+        *why = "board too large for the tensor-core convolution's halo slab";
+        return false;
+    }
+    if (!encode_2d(tmA, fp16, L.in, (uint64_t)L.cin, (uint64_t)L.m_total, kBK,
+                   (uint32_t)tc_slab_rows(L.g.rs), why))
         return false;
     return encode_2d(tmB, fp16, L.weight, (uint64_t)9 * L.cin, (uint64_t)L.cout, kBK,
                      (uint32_t)bn, why);

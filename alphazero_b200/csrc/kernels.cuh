@@ -85,8 +85,9 @@ cudaError_t launch_conv_tc(const ConvLayer& layer, const CUtensorMap& tmA, const
 bool make_conv_tensor_maps(const ConvLayer& layer, int bn, bool fp16, CUtensorMap* tmA,
                            CUtensorMap* tmB, const char** why);
 
-// Shared-memory bytes the tensor-core kernel needs for a tile width bn.
-int conv_tc_smem_bytes(int bn);
+// Shared-memory bytes the tensor-core kernel needs for a tile width bn on a
+// board with row stride rs.
+int conv_tc_smem_bytes(int bn, int rs);
 
 // Sets the shared-memory opt-in of every tensor-core kernel instantiation on
 // the current device (a per-device attribute; call once per device before
