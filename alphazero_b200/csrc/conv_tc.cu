@@ -21,9 +21,11 @@
 //   warp 1     TMEM allocator and MMA issuer (one thread): 4 x
 //              tcgen05.mma.kind::f16 (128 x bn x 16) per K block, fp32
 //              accumulators in TMEM, double-buffered across tiles;
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator, folded-BN bias,
-//              fp32 residual add, ReLU, frame masking, fp32 and/or 16-bit
-//              stores, and optionally the fused policy/value 1x1 head
+//   warps 2-9  epilogue: tcgen05.ld of the accumulator, folded-BN bias,
+//              residual add (the stream is a 16-bit hi plane, the operand,
+//              plus an fp16 remainder plane lo, both pixel-major), ReLU,
+//              frame masking, the sum re-split into hi and lo and stored
+//              with 16-byte accesses, and optionally the fused policy/value 1x1 head
 //              projection (one thread owns one pixel row, so when a tile
 //              spans all output channels it sees the whole channel vector).
 // The epilogue of tile t overlaps the main loop of tile t+1.
@@ -69,9 +71,10 @@ struct TcArgs {
     int cout;
     int rs, is, board;
     const float* bias;
-    const float* res32;
-    float* out32;
-    void* out16;
+    const uint16_t* res_hi;  // residual stream x = hi + lo, pixel-major [m_total][cout]
+    const uint16_t* res_lo;
+    uint16_t* out16;         // output hi plane (operand type) or nullptr
+    uint16_t* out_lo;        // output lo plane (fp16 remainder) or nullptr
     const float* head_w;
     const float* head_b;
     float* feat;
@@ -293,14 +296,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pix = y * a.board + x;
             }
             const size_t off = (size_t)m * a.cout + cbase;
-            const bool has_res = a.res32 != nullptr && in_range;
-            // The first chunk's residual is requested before the accumulator
-            // is ready; each later chunk's is requested one chunk ahead.
-            float4 r[8];
+            const bool has_res = a.res_hi != nullptr && in_range;
+            // The first chunk's residual (32 hi and 32 lo values, 4 + 4
+            // 16-byte loads) is requested before the accumulator is ready;
+            // each later chunk's one chunk ahead.  Ordinary L1-cached loads:
+            // a lane's 16 bytes are half a sector whose other half the
+            // next load reads (each row is read before it is overwritten in
+            // place, and never read again by this kernel).
+            uint4 rh[4], rl[4];
             if (has_res) {
-                const float4* rp = reinterpret_cast<const float4*>(a.res32 + off);
+                const uint4* ph = reinterpret_cast<const uint4*>(a.res_hi + off);
+                const uint4* pl = reinterpret_cast<const uint4*>(a.res_lo + off);
 #pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4) r[q4] = rp[q4];
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    rh[q4] = ph[q4];
+                    rl[q4] = pl[q4];
+                }
             }
             const bool ok = mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, a.err, kErrWaitEpilogue);
             // Leave together: no epilogue warp may be left at a named barrier.
@@ -321,36 +332,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + sbias[cbase + c0 + j];
                 if (has_res) {
 #pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4) {
-                        f[q4 * 4 + 0] += r[q4].x;
-                        f[q4 * 4 + 1] += r[q4].y;
-                        f[q4 * 4 + 2] += r[q4].z;
-                        f[q4 * 4 + 3] += r[q4].w;
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const uint32_t hw4[4] = {rh[q4].x, rh[q4].y, rh[q4].z, rh[q4].w};
+                        const uint32_t lw4[4] = {rl[q4].x, rl[q4].y, rl[q4].z, rl[q4].w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 hv = P::unpack(hw4[e]);
+                            const float2 lv = __half22float2(*reinterpret_cast<const __half2*>(&lw4[e]));
+                            f[q4 * 8 + 2 * e] += hv.x + lv.x;
+                            f[q4 * 8 + 2 * e + 1] += hv.y + lv.y;
+                        }
                     }
                     if (c + 1 < kChunks) {
-                        const float4* rp = reinterpret_cast<const float4*>(a.res32 + off + c0 + 32);
+                        const uint4* ph = reinterpret_cast<const uint4*>(a.res_hi + off + c0 + 32);
+                        const uint4* pl = reinterpret_cast<const uint4*>(a.res_lo + off + c0 + 32);
 #pragma unroll
-                        for (int q4 = 0; q4 < 8; ++q4) r[q4] = rp[q4];
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            rh[q4] = ph[q4];
+                            rl[q4] = pl[q4];
+                        }
                     }
                 }
 #pragma unroll
                 for (int j = 0; j < 32; ++j) f[j] = board_px ? fmaxf(f[j], 0.0f) : 0.0f;
-                if (a.out32 != nullptr) {
-                    float4* op = reinterpret_cast<float4*>(a.out32 + off + c0);
-#pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4)
-                        op[q4] = make_float4(f[q4 * 4], f[q4 * 4 + 1], f[q4 * 4 + 2], f[q4 * 4 + 3]);
-                }
                 if (a.out16 != nullptr) {
-                    uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out16) + off + c0);
+                    uint4* oh = reinterpret_cast<uint4*>(a.out16 + off + c0);
+                    uint4* ol = reinterpret_cast<uint4*>(a.out_lo + off + c0);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
-                        uint4 w;
-                        w.x = P::pack(f[q4 * 8 + 0], f[q4 * 8 + 1]);
-                        w.y = P::pack(f[q4 * 8 + 2], f[q4 * 8 + 3]);
-                        w.z = P::pack(f[q4 * 8 + 4], f[q4 * 8 + 5]);
-                        w.w = P::pack(f[q4 * 8 + 6], f[q4 * 8 + 7]);
-                        op[q4] = w;
+                        uint32_t hw4[4], lw4[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float x0 = f[q4 * 8 + 2 * e], x1 = f[q4 * 8 + 2 * e + 1];
+                            hw4[e] = P::pack(x0, x1);
+                            const float2 hv = P::unpack(hw4[e]);
+                            const __half2 lv = __floats2half2_rn(x0 - hv.x, x1 - hv.y);
+                            lw4[e] = *reinterpret_cast<const uint32_t*>(&lv);
+                        }
+                        oh[q4] = make_uint4(hw4[0], hw4[1], hw4[2], hw4[3]);
+                        if (a.out_lo != nullptr) ol[q4] = make_uint4(lw4[0], lw4[1], lw4[2], lw4[3]);
                     }
                 }
                 if (a.head_w != nullptr) {
@@ -411,9 +431,14 @@ cudaError_t launch_bn(const ConvLayer& L, const CUtensorMap& tmA, const CUtensor
     a.is = L.g.is;
     a.board = L.g.board;
     a.bias = L.bias;
-    a.res32 = L.res32;
-    a.out32 = L.out32;
-    a.out16 = L.out16;
+    // The residual stream is the hi / lo pair (16-bit operands only).
+    if (L.res32 != nullptr || L.out32 != nullptr || (L.res_hi == nullptr) != (L.res_lo == nullptr) ||
+        (L.out_lo != nullptr && L.out16 == nullptr))
+        return cudaErrorInvalidValue;
+    a.res_hi = static_cast<const uint16_t*>(L.res_hi);
+    a.res_lo = L.res_lo;
+    a.out16 = static_cast<uint16_t*>(L.out16);
+    a.out_lo = L.out_lo;
     a.head_w = L.head_w;
     a.head_b = L.head_b;
     a.feat = L.feat;

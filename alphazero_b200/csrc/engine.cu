@@ -422,16 +422,21 @@ struct mg_engine {
 
     // Whether the last trunk layer computes the head projection in its
     // epilogue (tensor-core path with one tile spanning all channels).
+    // In the 16-bit modes the last trunk layer always computes the head
+    // projection in its epilogue (one tile spans every channel); the fp32
+    // verification mode runs it as a separate pass.
     bool fused_heads(int bucket) const {
-        if (precision == MG_PREC_FP32) return false;
-        return use_pix() || choose_bn(bucket * g.is) == cpad;
+        (void)bucket;
+        return precision != MG_PREC_FP32;
     }
 
-    // Buffers of layer li on the 128-channel 16-bit path, whose residual
-    // stream is the pair (hi, lo): input conv stage -> (hi, lo); conv1 of a
-    // block hi -> t; conv2 t + (hi, lo) -> (hi, lo) in place.
-    void wire_pix_layer(ConvLayer& L, int li, const void* stage, void* hi, uint16_t* lo,
-                        void* t) const {
+    // Buffers of layer li in the 16-bit modes, whose residual stream is the
+    // pair (hi, lo): input conv stage -> (hi, lo); conv1 of a block hi -> t;
+    // conv2 t + (hi, lo) -> (hi, lo) in place.  (The lo plane's layout is
+    // the convolution kernel's own: 16-pixel blocks for the 128-channel
+    // kernel, pixel-major for the other; all layers of a network use one.)
+    void wire_hilo_layer(ConvLayer& L, int li, const void* stage, void* hi, uint16_t* lo,
+                         void* t) const {
         if (li == 0) {
             L.in = stage;
             L.out16 = hi;
@@ -458,8 +463,8 @@ struct mg_engine {
         L.err = d_err;
         const bool f32 = precision == MG_PREC_FP32;
         L.weight = f32 ? (const void*)d_w32[li] : (const void*)d_w16[li];
-        if (use_pix()) {
-            wire_pix_layer(L, li, d_stage, d_x16, reinterpret_cast<uint16_t*>(d_x), d_t);
+        if (!f32) {
+            wire_hilo_layer(L, li, d_stage, d_x16, reinterpret_cast<uint16_t*>(d_x), d_t);
         } else if (li == 0) {  // input conv: staged planes -> x
             L.in = d_stage;
             L.out32 = d_x;
@@ -498,7 +503,8 @@ struct mg_engine {
                "conv3x3_pix launch");
             return;
         }
-        const int bn = choose_bn(L.m_total);
+        // the head-projection layer's tile spans every channel
+        const int bn = li == n_convs - 1 ? cpad : choose_bn(L.m_total);
         CUtensorMap ta, tb;
         const char* why = "";
         if (!make_conv_tensor_maps(L, bn, fp16, &ta, &tb, &why)) throw std::runtime_error(why);
@@ -526,6 +532,9 @@ struct mg_engine {
     }
 
     void enqueue_trunk_heads(int bucket) {
+        if (precision != MG_PREC_FP32 && cpad > 256)
+            throw std::runtime_error(
+                "the bf16/fp16 modes support networks of up to 256 filters; use fp32");
         enqueue_trunk(bucket);
         if (!fused_heads(bucket))
             ck(launch_head_projection(d_x, bucket, cpad, g, d_head_w, d_head_b, d_feat, stream),
@@ -1113,8 +1122,8 @@ extern "C" int mg_forward_device_noalloc(mg_engine* e, const float* d_states, in
             L.bias = e->d_bias[li];
             L.err = b.err;
             L.weight = f32 ? (const void*)e->d_w32[li] : (const void*)e->d_w16[li];
-            if (e->use_pix()) {
-                e->wire_pix_layer(L, li, b.stage, b.x16, reinterpret_cast<uint16_t*>(b.x32), b.t);
+            if (!f32) {
+                e->wire_hilo_layer(L, li, b.stage, b.x16, reinterpret_cast<uint16_t*>(b.x32), b.t);
             } else if (li == 0) {
                 L.in = b.stage;
                 L.out32 = b.x32;
@@ -1145,7 +1154,7 @@ extern "C" int mg_forward_device_noalloc(mg_engine* e, const float* d_states, in
                    "conv3x3_pix launch");
             } else {
                 const bool fp16 = e->precision == MG_PREC_FP16;
-                const int bn = e->choose_bn(L.m_total);
+                const int bn = li == e->n_convs - 1 ? e->cpad : e->choose_bn(L.m_total);
                 CUtensorMap ta, tb;
                 const char* why = "";
                 if (!make_conv_tensor_maps(L, bn, fp16, &ta, &tb, &why))
