@@ -76,6 +76,7 @@ constexpr uint32_t kWBytes = kCo * kBK * 2;            // 16 KB weight stage
 constexpr int kSlot = kChunk * 32;  // one warp's chunk: 16 pixels x 32 channels
 constexpr int kMagicShift = 40;     // n / d == (n * ceil(2^40 / d)) >> 40 here
 constexpr int kMaxLayers = 44;      // layers per launch (kernel parameter space)
+constexpr int kMaxBufs = 4;         // TMEM accumulator buffers (512 columns / tile width)
 
 // One layer of a launch.
 struct PixLayer {
@@ -100,6 +101,7 @@ struct PixArgs {
     int npx;            // pixels per tile (multiple of 16, <= 256; the last tile may be shorter)
     int rs, is, board;
     int slab_rows;                // rows per slab (multiple of 16)
+    int nbuf;                     // TMEM accumulator buffers, npx columns each
     uint64_t is_magic, rs_magic;  // ceil(2^40 / is), ceil(2^40 / rs)
     int n_layers;
     int* err;
@@ -114,7 +116,7 @@ struct PixArgs {
 // it is not re-read after every store the way fields reached through a
 // reference to the parameter block can be.
 struct Geo {
-    int m_total, span, npx, rs, is, board;
+    int m_total, span, npx, rs, is, board, nbuf;
     uint64_t is_magic, rs_magic;
 };
 
@@ -126,6 +128,7 @@ __device__ __forceinline__ Geo geo_of(const PixArgs& a) {
     g.rs = a.rs;
     g.is = a.is;
     g.board = a.board;
+    g.nbuf = a.nbuf;
     g.is_magic = a.is_magic;
     g.rs_magic = a.rs_magic;
     return g;
@@ -281,15 +284,16 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
         int m0, len;
         tile_rows(G, blockIdx.x, tile_at(blockIdx.x, q, nt), m0, len);
         const int nchunks = (len + kChunk - 1) / kChunk;
-        const int acc = t & 1;
-        ok = mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, err, kErrWaitEpilogue);
+        const int acc = t % G.nbuf;
+        const int use = t / G.nbuf;  // earlier tiles of this accumulator buffer
+        ok = mbar_wait(smem_u32(&tfull[acc]), use & 1, err, kErrWaitEpilogue);
         if (HEAD ? bar_any(bar_a, 128, !ok) : __any_sync(0xffffffffu, !ok)) {
             ok = false;
             break;
         }
         tc_fence_after();
         const uint32_t tcol =
-            tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kMaxPx);
+            tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * G.npx);
 #pragma unroll 1
         for (int c = par; c < nchunks; c += kPar) {
             const int px0 = m0 + c * kChunk;
@@ -397,7 +401,7 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
             __syncwarp();
             if (lane == 0) {
                 const unsigned before = atom_add_acq_rel_cta(smem_u32(&tcount[acc]), 1u);
-                if (before == (unsigned)(kEpiWarps * (t >> 1) + kEpiWarps - 1))
+                if (before == (unsigned)(kEpiWarps * use + kEpiWarps - 1))
                     red_max_release_gpu(&progress[blockIdx.x], (unsigned)(l * nt + q + 1));
             }
         }
@@ -439,11 +443,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* sfull = bars + 2 * kStages;
     uint64_t* sempty = sfull + kSlabs;
     uint64_t* tfull = sempty + kSlabs;
-    uint64_t* tempty = tfull + 2;
-    uint64_t* done = tempty + 2;
+    uint64_t* tempty = tfull + kMaxBufs;
+    uint64_t* done = tempty + kMaxBufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-    uint32_t* tcount = tmem_slot + 1;                        // [2] epilogue warps done, per buffer
-    float* shead = reinterpret_cast<float*>(tmem_slot + 4);  // [3][128]
+    uint32_t* tcount = tmem_slot + 1;  // [kMaxBufs] epilogue warps done, per buffer
+    float* shead = reinterpret_cast<float*>(tmem_slot + 8);  // [3][128]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -460,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&sfull[i]), 1);
             mbar_init(smem_u32(&sempty[i]), 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kMaxBufs; ++i) {
             mbar_init(smem_u32(&tfull[i]), 1);
             mbar_init(smem_u32(&tempty[i]), kEpiWarps);
             tcount[i] = 0;
@@ -576,13 +580,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tile_rows(G, blockIdx.x, tile_at(blockIdx.x, q, nt), m0, len);
                     // MMA N = the tile's pixels rounded up to 16
                     const uint32_t idesc = idesc_f16(kCo, (len + 15) & ~15, !FP16);
-                    const int acc = t & 1;
-                    if (!mbar_wait(smem_u32(&tempty[acc]), ((t >> 1) & 1) ^ 1, err, kErrWaitMma)) {
+                    const int acc = t % G.nbuf;
+                    if (!mbar_wait(smem_u32(&tempty[acc]), ((t / G.nbuf) & 1) ^ 1, err, kErrWaitMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d = tmem_base + (uint32_t)(acc * kMaxPx);
+                    const uint32_t d = tmem_base + (uint32_t)(acc * G.npx);
                     for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
                         const int sb = is % kSlabs;
                         if (!mbar_wait(smem_u32(&sfull[sb]), (is / kSlabs) & 1, err, kErrWaitMma)) {
@@ -651,7 +655,7 @@ int slab_rows_for(int npx, int rs) {
 size_t pix_smem_bytes(int npx, int rs) {
     const size_t slab = (size_t)slab_rows_for(npx, rs) * 128;
     return (size_t)kStages * kWBytes + kSlabs * slab + (size_t)kEpiWarps * kSlot * 4 +
-           (2 * kStages + 2 * kSlabs + 4 + 1) * 8 + 16 + 3 * kCo * 4 + 1024;
+           (2 * kStages + 2 * kSlabs + 2 * kMaxBufs + 1) * 8 + 32 + 3 * kCo * 4 + 1024;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -720,6 +724,7 @@ cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16
     a.is = F.g.is;
     a.board = F.g.board;
     a.slab_rows = slab_rows_for(npx, F.g.rs);
+    a.nbuf = 512 / npx < kMaxBufs ? 512 / npx : kMaxBufs;
     a.is_magic = ((1ull << kMagicShift) + (uint64_t)F.g.is - 1) / (uint64_t)F.g.is;
     a.rs_magic = ((1ull << kMagicShift) + (uint64_t)F.g.rs - 1) / (uint64_t)F.g.rs;
     a.n_layers = n;
