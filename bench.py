@@ -396,7 +396,10 @@ def run_b200(args, wl):
                      "traffic": traffic,
                      "kernel": "trunk: all 3x3 conv layers (conv3x3_pix_kernel, persistent)",
                      "flops_per_launch": trunk_flops, "launch_ms": trunk_ms,
-                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops, burst)"},
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops, burst)",
+                     "peak_sustained": peaks["bf16_tflops_sustained"],
+                     "frac_sustained": achieved / peaks["bf16_tflops_sustained"],
+                     "timed_launches_ms": trunk_ms * reps},
         "tflops_whole_forward": value * flops_per_position(board, filters, blocks) / 1e12,
         "clocks": clocks.summary(),
     }
