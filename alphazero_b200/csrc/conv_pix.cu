@@ -106,6 +106,7 @@ struct PixArgs {
     int n_layers;
     int* err;
     unsigned* progress;  // [grid] tiles finished per CTA (several layers), else nullptr
+    int withhold_cta;    // test hook: this CTA never publishes its progress (-1: none)
     const float* head_w;  // [3][128] or nullptr (fused head projection)
     const float* head_b;
     float* feat;
@@ -401,7 +402,8 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
             __syncwarp();
             if (lane == 0) {
                 const unsigned before = atom_add_acq_rel_cta(smem_u32(&tcount[acc]), 1u);
-                if (before == (unsigned)(kEpiWarps * use + kEpiWarps - 1))
+                if (before == (unsigned)(kEpiWarps * use + kEpiWarps - 1) &&
+                    (int)blockIdx.x != a.withhold_cta)
                     red_max_release_gpu(&progress[blockIdx.x], (unsigned)(l * nt + q + 1));
             }
         }
@@ -700,7 +702,7 @@ bool layer_ok(const ConvLayer& L, const ConvLayer& first) {
 // to back from layers[1].weight.  With several layers, progress must point
 // at grid_limit counters.
 cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16, int grid_limit,
-                          unsigned* progress, cudaStream_t stream) {
+                          unsigned* progress, cudaStream_t stream, int withhold_cta = -1) {
     if (n < 1 || n > kMaxLayers || (n > 1 && progress == nullptr)) return cudaErrorInvalidValue;
     const ConvLayer& F = layers[0];
     // Balanced ranges: each CTA takes span pixels (a multiple of 16) cut into
@@ -730,6 +732,7 @@ cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16
     a.n_layers = n;
     a.err = F.err;
     a.progress = n > 1 ? progress : nullptr;
+    a.withhold_cta = n > 1 ? withhold_cta : -1;
     a.head_w = nullptr;
     a.head_b = nullptr;
     a.feat = nullptr;
@@ -864,7 +867,8 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
 }
 
 cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool fp16,
-                             int grid_limit, unsigned* progress, cudaStream_t stream) {
+                             int grid_limit, unsigned* progress, cudaStream_t stream,
+                             int withhold_cta) {
     // With few tiles per CTA a tile of the next layer depends on most of the
     // CTA's range and its neighbours' of the layer before, so one launch per
     // layer (programmatic dependent launches) is faster than the cross-CTA
@@ -883,7 +887,7 @@ cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool f
     for (int l0 = 0; l0 < n; l0 += kMaxLayers) {
         const int cnt = n - l0 < kMaxLayers ? n - l0 : kMaxLayers;
         cudaError_t e = launch_layers(layers + l0, cnt, max_npx, fp16, grid_limit,
-                                      cnt > 1 ? progress : nullptr, stream);
+                                      cnt > 1 ? progress : nullptr, stream, withhold_cta);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

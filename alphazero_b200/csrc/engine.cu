@@ -82,6 +82,7 @@ struct mg_engine {
     int pix_mode = 1;      // 1: pixels-on-N kernel for 128-channel layers
     int pix_npx = 0;       // pixels per tile override (0 = heuristic)
     int pix_trunk = 1;     // 1: all 128-channel trunk layers as one persistent launch
+    int withhold_cta = -1;  // test hook (MG_TEST_WITHHOLD_PROGRESS): see launch_trunk_pix
     bool use_graphs = true;
     cudaStream_t stream = nullptr;
     std::string err;
@@ -518,7 +519,8 @@ struct mg_engine {
             std::vector<ConvLayer> layers(n_convs);
             for (int li = 0; li < n_convs; ++li) layers[li] = layer_desc(li, bucket);
             ck(launch_trunk_pix(layers.data(), n_convs, choose_npx(bucket * g.is),
-                                precision == MG_PREC_FP16, num_sms, d_progress, stream),
+                                precision == MG_PREC_FP16, num_sms, d_progress, stream,
+                                withhold_cta),
                "conv3x3_pix trunk launch");
         } else {
             for (int li = 0; li < n_convs; ++li) launch_conv(li, bucket);
@@ -679,6 +681,7 @@ mg_engine* mg_create(int device, int flags) {
     if (const char* s = std::getenv("MG_PIX")) e->pix_mode = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_NPX")) e->pix_npx = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_TRUNK")) e->pix_trunk = std::atoi(s);
+    if (const char* s = std::getenv("MG_TEST_WITHHOLD_PROGRESS")) e->withhold_cta = std::atoi(s);
     return e.release();
 }
 
