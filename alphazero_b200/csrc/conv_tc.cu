@@ -236,7 +236,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t slab = smem_u32(sSlab + sb * slab_bytes);
+                    // Descriptor of the slab's first row; a tap's shifted
+                    // start adds its byte offset / 16 to the address field
+                    // (no carry: every start lies inside shared memory).
+                    const uint64_t ad0 = smem_desc_sw128(smem_u32(sSlab + sb * slab_bytes));
+                    // compile-time trip count: no per-tap index arithmetic
+                    // between the MMA groups
+#pragma unroll
                     for (int tap = 0; tap < 9; ++tap, ++it) {
                         const int s = it % S;
                         if (!mbar_wait(smem_u32(&full[s]), (it / S) & 1, a.err, kErrWaitMma)) {
@@ -248,13 +254,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // 128-byte rows, so no descriptor base offset)
                         const int r0 = halo + (tap / 3 - 1) * a.rs + (tap % 3 - 1);
                         const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * Cfg::kBBytes));
+                        const uint64_t ad = ad0 + (uint64_t)(r0 * 8);  // r0 * 128 B / 16
+                        // advance 16 elements (32 bytes) along K inside the swizzle atom
 #pragma unroll
-                        for (int k = 0; k < kBK / 16; ++k) {
-                            // advance 16 elements (32 bytes) along K inside the swizzle atom
-                            const uint64_t ad =
-                                smem_desc_sw128(slab + (uint32_t)r0 * 128u + 32u * k);
-                            mma_f16(d, ad, bd + (uint64_t)(2 * k), idesc, (cb | tap | k) != 0);
-                        }
+                        for (int k = 0; k < kBK / 16; ++k)
+                            mma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                                    (cb | tap | k) != 0);
                         mma_commit(smem_u32(&empty[s]));
                     }
                     if (ok) mma_commit(smem_u32(&sempty[sb]));
