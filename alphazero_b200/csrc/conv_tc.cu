@@ -50,7 +50,10 @@ constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
 
 template <int BN>
 struct TcConfig {
-    static constexpr int kStages = BN == 256 ? 5 : (BN == 128 ? 8 : 12);
+    // 4 stages at BN 256 keep the kernel under 196 KB of shared memory, so
+    // the carve-out leaves more L1 to the epilogue (measured 8% faster
+    // than 5 stages on 19x19 b20c256 batch 1024).
+    static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 8 : 12);
     static constexpr uint32_t kBBytes = BN * kBK * 2;
     static constexpr uint32_t kTmemCols = 2 * BN;
     // B ring + barriers and tmem slot (512) + bias (256 floats) + head weights
