@@ -66,8 +66,9 @@ namespace {
 constexpr int kCo = 128;        // output channels (MMA M)
 constexpr int kBK = 64;         // K per stage / slab channel block
 constexpr int kMaxPx = 256;     // MMA N limit
-// Weight ring depth.  Deeper rings measured slower: past 196 KB of shared
-// memory the carve-out leaves the epilogue's residual loads less L1.
+// Weight ring depth, measured: 4 beats 3 and 5 by about 1.5%; 6 and 7 take
+// the kernel past 196 KB of shared memory, where the carve-out leaves the
+// epilogue's residual loads much less L1, and lose 5-10%.
 constexpr int kStages = 4;
 constexpr int kSlabs = 2;       // activation slab ring depth
 constexpr int kEpiWarps = 12;   // epilogue warps: kPar per TMEM lane quarter
