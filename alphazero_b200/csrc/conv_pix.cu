@@ -13,7 +13,7 @@
 // nine times.  (The MMA derives the 128-byte swizzle phase from the absolute
 // shared-memory address, as TMA does when it writes the slab, so a start
 // address moved by whole 128-byte rows needs no descriptor base offset.)
-// Weight K blocks (128 x 64) stream through a 5-deep ring.
+// Weight K blocks (128 x 64) stream through a 4-deep ring.
 //
 // The accumulator is [co lanes][px columns] in TMEM, double-buffered across
 // tiles (2 x 256 columns).  Each epilogue warp works on its own: it owns 32
