@@ -4,6 +4,13 @@
                      (include/minigo_cuda.h); nvcc, static cudart.
   libminigo_host.so  CPU-only helpers (include/minigo_host.h): position
                      generator and ONNX reader; g++.
+  libminigo_evaluator.so  CudaEngine / GpuEvaluator / ShardedEvaluator
+                     (the reference's C++ interfaces over the C ABI).
+  selfplay_cuda      end-to-end self-play harness: the reference's own
+                     search (src/mcts.cpp, src/game.cpp) compiled unmodified
+                     from the reference tree with this backend's evaluator;
+                     built only where that tree is present (the binary then
+                     travels with the package).
 
 Run as ``python -m alphazero_b200.build``.  Rebuilds a library only when one
 of its sources is newer than it.
@@ -64,9 +71,21 @@ EVAL_HEADERS = [
     os.path.join(INCLUDE, "minigo_cuda.h"),
 ]
 
+SELFPLAY_SOURCES = [
+    os.path.join(HOST, "selfplay_main.cpp"),
+    os.path.join(HOST, "cuda_engine.cpp"),
+    os.path.join(HOST, "gpu_evaluator.cpp"),
+]
+SELFPLAY_HEADERS = EVAL_HEADERS + [os.path.join(HOST, "selfplay_loop.h")]
+# The reference tree the self-play harness compiles src/mcts.cpp and
+# src/game.cpp from (read in place, never copied).
+REFERENCE_TREE = os.environ.get("MGB_REFERENCE_TREE", "/root/reference")
+REFERENCE_SOURCES = ["src/mcts.cpp", "src/game.cpp"]
+
 CUDA_LIB = os.path.join(LIB, "libminigo_cuda.so")
 HOST_LIB = os.path.join(LIB, "libminigo_host.so")
 EVAL_LIB = os.path.join(LIB, "libminigo_evaluator.so")
+SELFPLAY_BIN = os.path.join(LIB, "selfplay_cuda")
 
 
 def _stale(target: str, deps: list[str]) -> bool:
@@ -119,8 +138,29 @@ def build_evaluator(force: bool = False) -> str:
     return EVAL_LIB
 
 
+def build_selfplay(force: bool = False) -> str | None:
+    """The self-play harness (selfplay_main.cpp).  Needs the reference
+    tree's search sources; returns None (and keeps any earlier build) where
+    the tree is absent."""
+    ref = [os.path.join(REFERENCE_TREE, s) for s in REFERENCE_SOURCES]
+    if not all(os.path.exists(r) for r in ref):
+        return SELFPLAY_BIN if os.path.exists(SELFPLAY_BIN) else None
+    cuda = build_cuda(force)
+    if force or _stale(SELFPLAY_BIN, SELFPLAY_SOURCES + SELFPLAY_HEADERS + ref + [cuda]):
+        tmp = SELFPLAY_BIN + ".tmp"
+        _run(["g++", "-std=c++17", "-O2", "-pthread", "-Wall", "-DMGB_USE_REFERENCE_HEADERS",
+              "-I" + os.path.join(REFERENCE_TREE, "include"), "-I" + HOST, "-o", tmp] +
+             SELFPLAY_SOURCES + ref + ["-L" + LIB, "-lminigo_cuda", "-Wl,-rpath,$ORIGIN"])
+        os.replace(tmp, SELFPLAY_BIN)
+    return SELFPLAY_BIN
+
+
 def build_all(force: bool = False) -> list[str]:
-    return [build_host(force), build_cuda(force), build_evaluator(force)]
+    out = [build_host(force), build_cuda(force), build_evaluator(force)]
+    sp = build_selfplay(force)
+    if sp is not None:
+        out.append(sp)
+    return out
 
 
 if __name__ == "__main__":

@@ -955,6 +955,17 @@ float* mg_host_input(mg_engine* e) {
     return out;
 }
 
+uint32_t* mg_host_bits(mg_engine* e) {
+    if (e == nullptr) return nullptr;
+    uint32_t* out = nullptr;
+    guarded(e, [&] {
+        e->check_ready();
+        e->ensure_buffers();
+        out = e->h_bits;
+    });
+    return out;
+}
+
 int mg_max_batch(const mg_engine* e) { return e ? e->max_batch : 0; }
 
 int mg_launch_conv(mg_engine* e, int n, int layer, int reps) {

@@ -3,6 +3,10 @@
 #include "../../include/minigo_cuda.h"
 
 #include <algorithm>
+#include <chrono>
+#if defined(__SSE2__)
+#include <emmintrin.h>
+#endif
 #include <cstring>
 #include <stdexcept>
 
@@ -25,18 +29,38 @@ void CudaEngine::check(int rc, const char* what) const {
     }
 }
 
+void CudaEngine::count_launches(int n) {
+    const int k = mg_launches_per_forward(h_, n);
+    if (k > 0) launches_.fetch_add((uint64_t)k, std::memory_order_relaxed);
+}
+
 void CudaEngine::load_model(const std::string& model_path) {
     if (mg_load_onnx(h_, model_path.c_str()) != MG_OK) throw std::runtime_error(mg_last_error(h_));
     check(mg_get_info(h_, &board_size, &input_channels, &num_filters, &num_res_blocks, &action_size_),
           "mg_get_info");
 }
 
-namespace {
-// Packs one state's binary planes into words (bit j % 32 of word j / 32);
-// false if some value is neither 0 nor 1.
-bool pack_state(const float* s, int size, uint32_t* w) {
+bool CudaEngine::pack_planes(const float* s, int size, uint32_t* w) {
     const int words = (size + 31) / 32;
-    for (int k = 0; k < words; ++k) {
+    int k = 0;
+#if defined(__SSE2__)
+    // Whole words four floats at a time: bits from (x == 1), and every
+    // lane must be 0 or 1.
+    const __m128 one = _mm_set1_ps(1.0f), zero = _mm_setzero_ps();
+    for (; k < size / 32; ++k) {
+        uint32_t v = 0;
+        int ok = 0xF;
+        for (int q = 0; q < 8; ++q) {
+            const __m128 x = _mm_loadu_ps(s + k * 32 + q * 4);
+            const __m128 is1 = _mm_cmpeq_ps(x, one);
+            v |= (uint32_t)_mm_movemask_ps(is1) << (4 * q);
+            ok &= _mm_movemask_ps(_mm_or_ps(is1, _mm_cmpeq_ps(x, zero)));
+        }
+        if (ok != 0xF) return false;
+        w[k] = v;
+    }
+#endif
+    for (; k < words; ++k) {
         uint32_t v = 0;
         const int lo = k * 32, hi = std::min(size, lo + 32);
         for (int j = lo; j < hi; ++j) {
@@ -48,7 +72,22 @@ bool pack_state(const float* s, int size, uint32_t* w) {
     }
     return true;
 }
-}  // namespace
+
+void CudaEngine::predict_bits(const uint32_t* const* bits, int n, float* policy, float* value) {
+    if (n <= 0) return;
+    uint32_t* pinned = mg_host_bits(h_);
+    if (pinned == nullptr) check(MG_E_DEVICE, "mg_host_bits");
+    const int words = words_per_position();
+    const int cap = mg_max_batch(h_);
+    for (int base = 0; base < n; base += cap) {
+        const int m = std::min(cap, n - base);
+        for (int i = 0; i < m; ++i)
+            std::memcpy(pinned + (size_t)i * words, bits[base + i], sizeof(uint32_t) * words);
+        check(mg_forward_packed(h_, pinned, m, policy + (size_t)base * action_size_, value + base, nullptr),
+              "mg_forward_packed");
+        count_launches(m);
+    }
+}
 
 void CudaEngine::predict_raw(const float* const* states, int n, int state_size, float* policy,
                              float* value) {
@@ -57,25 +96,36 @@ void CudaEngine::predict_raw(const float* const* states, int n, int state_size, 
     if (state_size != expect)
         throw std::invalid_argument("state has " + std::to_string(state_size) + " floats, expected " +
                                     std::to_string(expect));
-    // Encoded positions are binary planes: ship them bit-packed (32x fewer
-    // bytes over PCIe), unless some state is not binary.
+    // Encoded positions are binary planes: packed straight into the
+    // engine's pinned buffer and shipped bit-packed (32x fewer bytes over
+    // PCIe); a chunk with a non-binary state goes as fp32 planes instead.
     const int words = (state_size + 31) / 32;
-    bits_.resize((size_t)n * words);
-    bool binary = true;
-    for (int i = 0; i < n && binary; ++i) binary = pack_state(states[i], state_size, bits_.data() + (size_t)i * words);
-    if (binary) {
-        check(mg_forward_packed(h_, bits_.data(), n, policy, value, nullptr), "mg_forward_packed");
-        return;
-    }
-    float* pinned = mg_host_input(h_);
-    if (pinned == nullptr) throw std::runtime_error(std::string("mg_host_input: ") + mg_last_error(h_));
     const int cap = mg_max_batch(h_);
     for (int base = 0; base < n; base += cap) {
         const int m = std::min(cap, n - base);
-        for (int i = 0; i < m; ++i)
-            std::memcpy(pinned + (size_t)i * state_size, states[base + i], sizeof(float) * state_size);
-        check(mg_forward(h_, pinned, m, policy + (size_t)base * action_size_, value + base, nullptr),
-              "mg_forward");
+        uint32_t* pinned_bits = mg_host_bits(h_);
+        if (pinned_bits == nullptr) check(MG_E_DEVICE, "mg_host_bits");
+        bool binary = true;
+        const auto t0 = std::chrono::steady_clock::now();
+        for (int i = 0; i < m && binary; ++i)
+            binary = pack_planes(states[base + i], state_size, pinned_bits + (size_t)i * words);
+        pack_ns_.fetch_add((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                               std::chrono::steady_clock::now() - t0)
+                               .count(),
+                           std::memory_order_relaxed);
+        if (binary) {
+            check(mg_forward_packed(h_, pinned_bits, m, policy + (size_t)base * action_size_, value + base,
+                                    nullptr),
+                  "mg_forward_packed");
+        } else {
+            float* pinned = mg_host_input(h_);
+            if (pinned == nullptr) check(MG_E_DEVICE, "mg_host_input");
+            for (int i = 0; i < m; ++i)
+                std::memcpy(pinned + (size_t)i * state_size, states[base + i], sizeof(float) * state_size);
+            check(mg_forward(h_, pinned, m, policy + (size_t)base * action_size_, value + base, nullptr),
+                  "mg_forward");
+        }
+        count_launches(m);
     }
 }
 

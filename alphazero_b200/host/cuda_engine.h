@@ -6,6 +6,7 @@
 
 #include "minigo_api.h"
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <string>
@@ -50,17 +51,34 @@ public:
     void predict_raw(const float* const* states, int n, int state_size, float* policy,
                      float* value);
 
+    // As predict_raw for states already in the bit-packed wire format
+    // (words_per_position() words each, see pack_planes): gathered straight
+    // into the engine's pinned buffer (mg_host_bits) and shipped as is.
+    void predict_bits(const uint32_t* const* bits, int n, float* policy, float* value);
+
+    // Packs one state's binary planes (`size` floats, each 0 or 1) into
+    // (size + 31) / 32 words, element j at bit j % 32 of word j / 32; false
+    // if some value is neither 0 nor 1 (the words are then unspecified).
+    static bool pack_planes(const float* state, int size, uint32_t* words);
+    int words_per_position() const { return (input_channels * board_size * board_size + 31) / 32; }
+
     int device() const { return device_; }
     int action_size() const { return action_size_; }
+    // Kernel launches of this library made by predict / predict_batch /
+    // predict_raw so far (readable from any thread).
+    uint64_t kernel_launches() const { return launches_.load(std::memory_order_relaxed); }
+    // Host time (ns) predict_raw spent packing binary planes into bits.
+    uint64_t pack_ns() const { return pack_ns_.load(std::memory_order_relaxed); }
 
 private:
     void check(int rc, const char* what) const;
+    void count_launches(int n);
 
     mg_engine* h_ = nullptr;
     int device_ = 0;
     int action_size_ = 0;
     std::vector<float> policy_scratch_, value_scratch_;
-    std::vector<uint32_t> bits_;
+    std::atomic<uint64_t> launches_{0}, pack_ns_{0};
 };
 
 }  // namespace minigo

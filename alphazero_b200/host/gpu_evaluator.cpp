@@ -3,6 +3,7 @@
 #include "cuda_engine.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <limits>
 #include <stdexcept>
@@ -36,7 +37,19 @@ BatchEvaluator::Result GpuEvaluator::take_result(NNResultBuf& buf) {
         }
         throw std::runtime_error("batched evaluation failed: " + why);
     }
-    return {std::move(buf.policy), buf.value};
+    // Copied, not moved: the buffer keeps its capacity, so the server's next
+    // result for this client (the search reuses one buffer per thread) is a
+    // plain copy without an allocation on the server thread, and the
+    // client's copy allocates on its own thread.
+    return {buf.policy, buf.value};
+}
+
+void GpuEvaluator::enqueue(const Pending* items, size_t n) {
+    {
+        std::lock_guard<std::mutex> lock(mu_);
+        queue_.insert(queue_.end(), items, items + n);
+    }
+    cv_.notify_all();
 }
 
 BatchEvaluator::Result GpuEvaluator::evaluate_with_buf(NNResultBuf& buf,
@@ -44,11 +57,15 @@ BatchEvaluator::Result GpuEvaluator::evaluate_with_buf(NNResultBuf& buf,
     buf.done = false;
     buf.state_data = state.data();
     buf.state_size = (int)state.size();
-    {
-        std::lock_guard<std::mutex> lock(mu_);
-        queue_.push_back(&buf);
+    Pending p{&buf, nullptr};
+    if (cuda_ != nullptr) {
+        // The client blocks below until its result is back, so its
+        // thread-local words stay valid while the server reads them.
+        thread_local std::vector<uint32_t> words;
+        words.resize((state.size() + 31) / 32);
+        if (CudaEngine::pack_planes(state.data(), (int)state.size(), words.data())) p.bits = words.data();
     }
-    cv_.notify_all();
+    enqueue(&p, 1);
     {
         std::unique_lock<std::mutex> lock(buf.mu);
         buf.cv.wait(lock, [&] { return buf.done; });
@@ -66,16 +83,20 @@ std::vector<BatchEvaluator::Result> GpuEvaluator::evaluate(
     if (states.empty()) return {};
     const size_t n = states.size();
     std::vector<std::unique_ptr<NNResultBuf>> bufs(n);
-    {
-        std::lock_guard<std::mutex> lock(mu_);
-        for (size_t i = 0; i < n; ++i) {
-            bufs[i] = std::make_unique<NNResultBuf>();
-            bufs[i]->state_data = states[i].data();
-            bufs[i]->state_size = (int)states[i].size();
-            queue_.push_back(bufs[i].get());
+    std::vector<std::vector<uint32_t>> words(cuda_ != nullptr ? n : 0);
+    std::vector<Pending> items(n);
+    for (size_t i = 0; i < n; ++i) {
+        bufs[i] = std::make_unique<NNResultBuf>();
+        bufs[i]->state_data = states[i].data();
+        bufs[i]->state_size = (int)states[i].size();
+        items[i] = {bufs[i].get(), nullptr};
+        if (cuda_ != nullptr) {
+            words[i].resize((states[i].size() + 31) / 32);
+            if (CudaEngine::pack_planes(states[i].data(), (int)states[i].size(), words[i].data()))
+                items[i].bits = words[i].data();
         }
     }
-    cv_.notify_all();
+    enqueue(items.data(), n);
     std::vector<Result> out;
     out.reserve(n);
     bool failed = false;
@@ -92,17 +113,27 @@ std::vector<BatchEvaluator::Result> GpuEvaluator::evaluate(
     return out;
 }
 
-void GpuEvaluator::run_batch(std::vector<NNResultBuf*>& batch) {
+void GpuEvaluator::run_batch(std::vector<Pending>& batch) {
     const int n = (int)batch.size();
     if (cuda_ != nullptr) {
         const int a = cuda_->action_size();
-        ptrs_.resize(n);
-        for (int i = 0; i < n; ++i) ptrs_[i] = batch[i]->state_data;
+        bool packed = true;
+        for (const auto& p : batch) packed &= p.bits != nullptr && p.buf->state_size == batch[0].buf->state_size;
         policy_.resize((size_t)n * a);
         value_.resize(n);
-        cuda_->predict_raw(ptrs_.data(), n, batch[0]->state_size, policy_.data(), value_.data());
+        const auto t0 = std::chrono::steady_clock::now();
+        if (packed && batch[0].buf->state_size == cuda_->input_channels * cuda_->board_size * cuda_->board_size) {
+            bit_ptrs_.resize(n);
+            for (int i = 0; i < n; ++i) bit_ptrs_[i] = batch[i].bits;
+            cuda_->predict_bits(bit_ptrs_.data(), n, policy_.data(), value_.data());
+        } else {
+            ptrs_.resize(n);
+            for (int i = 0; i < n; ++i) ptrs_[i] = batch[i].buf->state_data;
+            cuda_->predict_raw(ptrs_.data(), n, batch[0].buf->state_size, policy_.data(), value_.data());
+        }
+        const auto t1 = std::chrono::steady_clock::now();
         for (int i = 0; i < n; ++i) {
-            NNResultBuf* buf = batch[i];
+            NNResultBuf* buf = batch[i].buf;
             std::lock_guard<std::mutex> lock(buf->mu);
             buf->policy.assign(policy_.begin() + (size_t)i * a, policy_.begin() + (size_t)(i + 1) * a);
             buf->value = value_[i];
@@ -111,15 +142,18 @@ void GpuEvaluator::run_batch(std::vector<NNResultBuf*>& batch) {
             // and destroy its buffer (and condition variable).
             buf->cv.notify_one();
         }
+        const auto t2 = std::chrono::steady_clock::now();
+        engine_ns_.fetch_add((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count());
+        scatter_ns_.fetch_add((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(t2 - t1).count());
         return;
     }
     std::vector<std::vector<float>> states;
     states.reserve(n);
-    for (auto* buf : batch) states.emplace_back(buf->state_data, buf->state_data + buf->state_size);
+    for (const auto& p : batch) states.emplace_back(p.buf->state_data, p.buf->state_data + p.buf->state_size);
     auto results = engine_->predict_batch(states);
     if ((int)results.size() != n) throw std::runtime_error("engine returned a short batch");
     for (int i = 0; i < n; ++i) {
-        NNResultBuf* buf = batch[i];
+        NNResultBuf* buf = batch[i].buf;
         std::lock_guard<std::mutex> lock(buf->mu);
         buf->policy = std::move(results[i].first);
         buf->value = results[i].second;
@@ -129,7 +163,7 @@ void GpuEvaluator::run_batch(std::vector<NNResultBuf*>& batch) {
 }
 
 void GpuEvaluator::server_loop() {
-    std::vector<NNResultBuf*> batch;
+    std::vector<Pending> batch;
     batch.reserve(max_batch_);
     while (true) {
         {
@@ -155,7 +189,8 @@ void GpuEvaluator::server_loop() {
             }
             // Wake every client of the batch with an empty policy: each one
             // turns that into an exception on its own thread.
-            for (auto* buf : batch) {
+            for (const auto& p : batch) {
+                NNResultBuf* buf = p.buf;
                 std::lock_guard<std::mutex> lock(buf->mu);
                 if (!buf->done) {
                     buf->policy.clear();

@@ -10,9 +10,13 @@
 //     thread, where the reference returned an empty policy that the search
 //     then indexed out of bounds (src/nn_evaluator.cpp:117-125,
 //     src/mcts.cpp:59-64);
-//   * with a CudaEngine, states are gathered straight from the clients'
-//     buffers into the engine's pinned input buffer (one host copy instead of
-//     the reference's two, src/nn_evaluator.cpp:108-112 plus the engine's);
+//   * with a CudaEngine, each client packs its own state's binary planes
+//     into the bit-packed wire format (1/32 of the fp32 bytes) on its own
+//     thread before queueing it, and the server only gathers those words
+//     into the engine's pinned buffer: the reference's server thread copies
+//     every 24.5 KB fp32 state twice (src/nn_evaluator.cpp:108-112 plus the
+//     engine's flatten), and packing on the server thread alone took 60% of
+//     its time at 19x19 with 1024 search threads;
 //   * a client is woken while its buffer's mutex is held: the reference
 //     notifies after unlocking (src/nn_evaluator.cpp:127-137), so a client
 //     that sees `done` can return and destroy its stack NNResultBuf while
@@ -56,10 +60,21 @@ public:
     uint64_t positions() const { return positions_.load(); }
     int largest_batch() const { return largest_.load(); }
     uint64_t failed_batches() const { return failed_.load(); }
+    // Server-thread time (ns) in the engine call (gather, H2D, forward, D2H)
+    // and in handing results back to the clients (copy + wake-up).
+    uint64_t engine_ns() const { return engine_ns_.load(); }
+    uint64_t scatter_ns() const { return scatter_ns_.load(); }
 
 private:
+    // A queued request: the client's buffer and, with a CudaEngine, its
+    // state packed to bits (null if it is not binary).
+    struct Pending {
+        NNResultBuf* buf;
+        const uint32_t* bits;
+    };
     void server_loop();
-    void run_batch(std::vector<NNResultBuf*>& batch);
+    void run_batch(std::vector<Pending>& batch);
+    void enqueue(const Pending* items, size_t n);
     Result take_result(NNResultBuf& buf);
 
     InferenceEngine* engine_;
@@ -68,14 +83,16 @@ private:
 
     std::mutex mu_;
     std::condition_variable cv_;
-    std::vector<NNResultBuf*> queue_;
+    std::vector<Pending> queue_;
     bool stop_ = false;
     std::string last_error_;  // guarded by mu_
 
     std::vector<const float*> ptrs_;
+    std::vector<const uint32_t*> bit_ptrs_;
     std::vector<float> policy_, value_;
 
     std::atomic<uint64_t> batches_{0}, positions_{0}, failed_{0};
+    std::atomic<uint64_t> engine_ns_{0}, scatter_ns_{0};
     std::atomic<int> largest_{0};
     std::thread server_;
 };

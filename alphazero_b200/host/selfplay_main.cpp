@@ -1,0 +1,137 @@
+// selfplay_cuda: end-to-end self-play throughput of this backend.
+//
+// The reference's own search (src/mcts.cpp, src/game.cpp, compiled unmodified
+// from the reference tree) plays games through a ShardedEvaluator: one
+// GpuEvaluator batching server and one CudaEngine per GPU, weights replicated,
+// each search thread bound to one GPU round-robin.  This is what the
+// reference's selfplay binary runs once the backend is wired in
+// (src/main_selfplay.cpp:66-84 with create_engine returning a CudaEngine),
+// minus the game-record file writes.
+//
+//   selfplay_cuda --model M.onnx [--gpus N] [--workers 64] [--search-threads 16]
+//                 [--sims 800] [--max-batch 512] [--warmup-seconds 10]
+//                 [--seconds 30] [--precision bf16|fp16|fp32]
+//                 [--servers-per-gpu K]
+//
+// With K > 1 each GPU gets K engines (each its own weights copy, stream and
+// buffers) and K batching servers, so one server's host work (gathering the
+// batch, waking its clients) overlaps another's GPU work.
+//
+// Prints one JSON line: MCTS visits/s (searches completed in the measured
+// window x simulations per search), NN positions/s and mean batch size.
+#include "cuda_engine.h"
+#include "gpu_evaluator.h"
+#include "selfplay_loop.h"
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <exception>
+#include <memory>
+#include <string>
+#include <thread>
+#include <vector>
+
+using namespace minigo;
+
+int main(int argc, char** argv) {
+    std::string model;
+    int gpus = 1, workers = 64, search_threads = 16, sims = 800, max_batch = 512, per_gpu = 1;
+    double warmup_s = 10.0, measure_s = 30.0;
+    CudaEngine::Precision prec = CudaEngine::kBf16;
+    for (int i = 1; i < argc; ++i) {
+        const std::string a = argv[i];
+        auto next = [&]() -> const char* {
+            if (i + 1 >= argc) {
+                std::fprintf(stderr, "missing value after %s\n", a.c_str());
+                std::exit(2);
+            }
+            return argv[++i];
+        };
+        if (a == "--model") model = next();
+        else if (a == "--gpus") gpus = std::atoi(next());
+        else if (a == "--workers") workers = std::atoi(next());
+        else if (a == "--search-threads") search_threads = std::atoi(next());
+        else if (a == "--sims") sims = std::atoi(next());
+        else if (a == "--max-batch") max_batch = std::atoi(next());
+        else if (a == "--servers-per-gpu") per_gpu = std::atoi(next());
+        else if (a == "--warmup-seconds") warmup_s = std::atof(next());
+        else if (a == "--seconds") measure_s = std::atof(next());
+        else if (a == "--precision") {
+            const std::string p = next();
+            prec = p == "fp16" ? CudaEngine::kFp16 : (p == "fp32" ? CudaEngine::kFp32 : CudaEngine::kBf16);
+        } else {
+            std::fprintf(stderr, "unknown argument %s\n", a.c_str());
+            return 2;
+        }
+    }
+    if (model.empty() || gpus < 1 || workers < 1 || search_threads < 1 || sims < 1 || max_batch < 1 ||
+        per_gpu < 1) {
+        std::fprintf(stderr, "usage: selfplay_cuda --model M.onnx [--gpus N] ...\n");
+        return 2;
+    }
+    try {
+        std::vector<std::unique_ptr<CudaEngine>> engines;
+        std::vector<InferenceEngine*> raw;
+        for (int k = 0; k < per_gpu; ++k)
+            for (int d = 0; d < gpus; ++d) {
+                engines.push_back(std::make_unique<CudaEngine>(d, prec, false, max_batch));
+                engines.back()->load_model(model);
+                raw.push_back(engines.back().get());
+            }
+        ShardedEvaluator evaluator(raw, max_batch);
+
+        Config config;
+        config.board_size = engines[0]->board_size;
+        config.input_channels = engines[0]->input_channels;
+        config.num_filters = engines[0]->num_filters;
+        config.num_res_blocks = engines[0]->num_res_blocks;
+        config.max_moves_per_game = config.board_size * config.board_size * 2;
+        config.num_search_threads = search_threads;
+        config.num_simulations = sims;
+        config.max_batch_size = max_batch;
+
+        auto nn = [&](mgb_selfplay::Counters& c) {
+            c.nn_positions = c.nn_batches = c.gpu_launches = c.engine_ns = c.scatter_ns = 0;
+            for (size_t s = 0; s < evaluator.shards(); ++s) {
+                c.nn_positions += evaluator.shard(s).positions();
+                c.nn_batches += evaluator.shard(s).batches();
+                c.engine_ns += evaluator.shard(s).engine_ns();
+                c.scatter_ns += evaluator.shard(s).scatter_ns();
+            }
+            for (const auto& e : engines) {
+                c.gpu_launches += e->kernel_launches();
+                c.pack_ns += e->pack_ns();
+            }
+        };
+        const mgb_selfplay::Window w =
+            mgb_selfplay::run(&evaluator, config, workers, warmup_s, measure_s, nn);
+
+        const double moves = (double)(w.end.moves - w.begin.moves);
+        const double pos = (double)(w.end.nn_positions - w.begin.nn_positions);
+        const double bat = (double)(w.end.nn_batches - w.begin.nn_batches);
+        uint64_t failed = 0;
+        for (size_t s = 0; s < evaluator.shards(); ++s) failed += evaluator.shard(s).failed_batches();
+        std::printf(
+            "{\"visits_per_s\": %.3f, \"nn_positions_per_s\": %.3f, \"moves_per_s\": %.4f, "
+            "\"mean_batch\": %.2f, \"seconds\": %.3f, \"moves\": %.0f, \"games_finished\": %llu, "
+            "\"gpus\": %d, \"servers_per_gpu\": %d, \"workers\": %d, \"search_threads\": %d, \"sims\": %d, "
+            "\"max_batch\": %d, \"board\": %d, \"filters\": %d, \"blocks\": %d, "
+            "\"host_threads\": %u, \"failed_batches\": %llu, \"gpu_launches\": %llu, "
+            "\"server_engine_frac\": %.3f, \"server_pack_frac\": %.3f, \"server_scatter_frac\": %.3f}\n",
+            moves * sims / w.seconds, pos / w.seconds, moves / w.seconds, bat > 0 ? pos / bat : 0.0,
+            w.seconds, moves, (unsigned long long)(w.end.games - w.begin.games), gpus, per_gpu, workers,
+            search_threads, sims, max_batch, config.board_size, config.num_filters,
+            config.num_res_blocks, std::thread::hardware_concurrency(),
+            (unsigned long long)failed,
+            (unsigned long long)(w.end.gpu_launches - w.begin.gpu_launches),
+            (double)(w.end.engine_ns - w.begin.engine_ns) * 1e-9 / w.seconds / evaluator.shards(),
+            (double)(w.end.pack_ns - w.begin.pack_ns) * 1e-9 / w.seconds / evaluator.shards(),
+            (double)(w.end.scatter_ns - w.begin.scatter_ns) * 1e-9 / w.seconds / evaluator.shards());
+        std::fflush(stdout);
+    } catch (const std::exception& e) {
+        std::fprintf(stderr, "selfplay_cuda: %s\n", e.what());
+        return 1;
+    }
+    return 0;
+}

@@ -2,7 +2,8 @@
 (InferenceEngine::predict_batch, include/inference_engine.h:25-32) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload b19c128x10_bs512|b19c256x20_bs1024|b9c128x10_bs256|b9c64x6_bs16]
+                    [--workload b19c128x10_bs512|b19c256x20_bs1024|b9c128x10_bs256|b9c64x6_bs16
+                                |selfplay_b19c128x10]
 
 A step is one forward pass of the network over one batch of seeded random-
 playout positions.  Under torchrun each rank drives its own GPU with its own
@@ -22,6 +23,19 @@ JSON line.  Numbers:
   cpu_baseline  the oracle (C restatement of src/eigen_engine.cpp) on the
              host cores over a bounded sample (rank 0, N = 1 only).
 --impl reference times that CPU implementation alone as the reference arm.
+
+selfplay_b19c128x10 is end-to-end self-play instead: the reference's own
+search (src/mcts.cpp, compiled unmodified) with 64 game workers x 16 search
+threads, 800 simulations per move, max batch 512, over one batching server
+and engine per GPU (alphazero_b200/lib/selfplay_cuda).  One process drives
+all N GPUs (under torchrun rank 0 runs it, the other ranks wait).  A step is
+one second of the measured window (at least 10), a warm-up step two seconds
+(at least 6).  value = MCTS visits/s = searches completed in the window x 800
+/ window seconds; nn_positions_per_s = positions the engines evaluated.  The
+reference arm runs the same search with the reference's NNEvaluator over the
+oracle engine on one core, as the reference's Eigen backend runs; no search
+completes in a bounded window there, so its value is leaf evaluations/s
+(one per simulation that reaches a non-terminal leaf).
 """
 from __future__ import annotations
 
@@ -47,6 +61,11 @@ WORKLOADS = {
     "b19c256x20_bs1024": (19, 256, 20, 1024, 250),
     "b9c128x10_bs256": (9, 128, 10, 256, 60),
     "b9c64x6_bs16": (9, 64, 6, 16, 60),
+}
+SELFPLAY_WORKLOADS = {
+    # name: (board, filters, blocks, game workers, search threads per search,
+    #        simulations per move, max batch per evaluator)
+    "selfplay_b19c128x10": (19, 128, 10, 64, 16, 800, 512),
 }
 DEFAULT_WORKLOAD = "b19c128x10_bs512"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
@@ -408,17 +427,132 @@ def run_b200(args, wl):
     print(json.dumps(line), flush=True)
 
 
+def selfplay_config(wl):
+    board, filters, blocks, workers, threads, sims, max_batch = SELFPLAY_WORKLOADS[wl]
+    return {"workload": f"self-play {board}x{board} b{blocks}c{filters}: {workers} game workers x "
+                        f"{threads} search threads, {sims} simulations per move, max batch {max_batch}",
+            "board": board, "filters": filters, "blocks": blocks, "workers": workers,
+            "search_threads": threads, "simulations": sims, "max_batch": max_batch,
+            "search": "reference src/mcts.cpp compiled unmodified",
+            "weights": "seeded random init (export_onnx --init distributions)",
+            "parallelism": "one batching server + engine per GPU, search threads round-robin, "
+                           "weights replicated, no collective"}
+
+
+def selfplay_window(args):
+    """(warm-up seconds, measured seconds) for --warmup / --steps."""
+    return max(6.0, 2.0 * args.warmup), max(10.0, float(args.steps))
+
+
+def run_selfplay_binary(exe, model, wl, args, gpus):
+    board, filters, blocks, workers, threads, sims, max_batch = SELFPLAY_WORKLOADS[wl]
+    warm, window = selfplay_window(args)
+    cmd = [exe, "--model", model, "--gpus", str(gpus), "--workers", str(workers),
+           "--search-threads", str(threads), "--sims", str(sims), "--max-batch", str(max_batch),
+           "--warmup-seconds", str(warm), "--seconds", str(window)]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=warm + window + 600)
+    if r.returncode != 0:
+        raise RuntimeError(f"{os.path.basename(exe)} failed ({r.returncode}): {r.stderr[-2000:]}")
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+def selfplay_model(wl):
+    from alphazero_b200 import weights
+
+    board, filters, blocks = SELFPLAY_WORKLOADS[wl][:3]
+    sd = weights.make_state_dict(board, filters, blocks, seed=0, variant="init")
+    tmp = tempfile.mkdtemp(prefix="mgb_selfplay_")
+    return weights.write_onnx(os.path.join(tmp, "model.onnx"), sd)
+
+
+def oracle_selfplay(wl, args):
+    """The reference arm / CPU baseline of the self-play workload."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "selfplay_oracle")
+    if not os.path.exists(exe):
+        return None, "oracle/_ref/selfplay_oracle was not built (no reference tree at build time)"
+    out = run_selfplay_binary(exe, selfplay_model(wl), wl, args, 0)
+    return out, None
+
+
+def run_selfplay(args, wl):
+    world, rank, _ = dist_setup()
+    ranks = Ranks("gloo", timeout_s=1800)
+    board, filters, blocks, workers, threads, sims, max_batch = SELFPLAY_WORKLOADS[wl]
+    line = None
+    if rank == 0:
+        metric = (f"MCTS visits/sec (self-play {board}x{board} b{blocks}c{filters}, {workers} workers x "
+                  f"{threads} search threads, {sims} sims)")
+        if args.impl == "reference":
+            out, why = oracle_selfplay(wl, args)
+            if out is None:
+                line = {"impl": "reference", "unavailable": why}
+            else:
+                v = out["nn_positions_per_s"]
+                line = {"impl": "reference", "metric": metric, "value": v, "unit": "visits/s",
+                        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                        "ms_per_step": 1000.0, "higher_is_better": True, "scaling": "strong",
+                        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                        "config": selfplay_config(wl), "selfplay": out,
+                        "cpu_baseline": {"value": v, "unit": "visits/s", "cores": 1, "kind": "port",
+                                         "sample": f"{out['seconds']:.0f} s window of the same "
+                                                   "self-play; NN on one core like the reference's "
+                                                   "Eigen backend; leaf evaluations/s"},
+                        "e2e": {"value": v, "unit": "visits/s", "h2d_bytes_per_step": 0,
+                                "d2h_bytes_per_step": 0}}
+        else:
+            from alphazero_b200 import build
+
+            if not os.path.exists(build.SELFPLAY_BIN):
+                raise SystemExit("selfplay_cuda was not built: the reference tree's src/mcts.cpp "
+                                 "is needed at build time")
+            gpus = max(args.gpus, world)
+            with ClockSampler(0) as clocks:
+                out = run_selfplay_binary(build.SELFPLAY_BIN, selfplay_model(wl), wl, args, gpus)
+            base = None
+            if gpus == 1 and not args.no_cpu_baseline:
+                base_out, _ = oracle_selfplay(wl, args)
+                if base_out is not None:
+                    base = {"value": base_out["nn_positions_per_s"], "unit": "visits/s", "cores": 1,
+                            "kind": "port",
+                            "sample": f"{base_out['seconds']:.0f} s window of the same self-play; "
+                                      "the reference's NNEvaluator over the oracle engine on one "
+                                      "core; leaf evaluations/s"}
+            words = (17 * board * board + 31) // 32
+            pps = out["nn_positions_per_s"]
+            line = {"metric": metric, "value": out["visits_per_s"], "unit": "visits/s",
+                    "n_gpus": gpus, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": 1000.0 * out["seconds"] / max(1, args.steps),
+                    "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                    "dtype": "bf16", "data": "synthetic", "config": selfplay_config(wl),
+                    "selfplay": out,
+                    "e2e": {"value": out["visits_per_s"], "unit": "visits/s",
+                            "h2d_bytes_per_step": int(pps * words * 4),
+                            "d2h_bytes_per_step": int(pps * (board * board + 2) * 4),
+                            "api": "reference MCTS -> ShardedEvaluator -> CudaEngine::predict_raw "
+                                   "(bit-packed planes); bytes per one-second step"},
+                    "gpu_launches": out["gpu_launches"],
+                    "clocks": clocks.summary()}
+            if base is not None:
+                line["cpu_baseline"] = base
+    ranks.close()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD,
+                    choices=sorted(WORKLOADS) + sorted(SELFPLAY_WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
-    if args.impl == "reference":
+    if args.workload in SELFPLAY_WORKLOADS:
+        run_selfplay(args, args.workload)
+    elif args.impl == "reference":
         run_reference(args, args.workload)
     else:
         run_b200(args, args.workload)

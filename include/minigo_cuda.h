@@ -128,6 +128,13 @@ int mg_forward_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_o
  * model is loaded or allocation fails. */
 float* mg_host_input(mg_engine* e);
 
+/* The same for the bit-packed wire format of mg_forward_packed: room for
+ * mg_max_batch() positions of mg_words_per_position() words.  A batch
+ * gathered here and passed to mg_forward_packed crosses to the device with
+ * no intermediate host copy.  Same validity as mg_host_input.  No reference
+ * counterpart (the reference ships fp32 planes). */
+uint32_t* mg_host_bits(mg_engine* e);
+
 /* Current max batch (mg_set_max_batch). */
 int mg_max_batch(const mg_engine* e);
 

@@ -56,3 +56,40 @@ def test_cuda_engine_and_sharded_evaluator(tmp_path):
     assert np.abs(vals - ov).max() < 2e-2
     assert np.abs(probs - op).max() < 2e-2
     assert "sharded ok" in r.stdout
+
+
+_REF_SEARCH = [os.path.join(build.REFERENCE_TREE, s) for s in build.REFERENCE_SOURCES]
+
+
+@pytest.mark.skipif(not all(os.path.exists(p) for p in _REF_SEARCH),
+                    reason="the reference tree (src/mcts.cpp, src/game.cpp) is not present")
+def test_selfplay_loop_with_fake_engines(tmp_path):
+    """The self-play measurement loop over the reference's own MCTS (compiled
+    from the reference tree) and a two-shard ShardedEvaluator of fake engines."""
+    exe = str(tmp_path / "test_selfplay_loop")
+    _compile("test_selfplay_loop.cpp", exe,
+             ["-DMGB_USE_REFERENCE_HEADERS", "-I" + os.path.join(build.REFERENCE_TREE, "include")]
+             + _REF_SEARCH)
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "selfplay loop ok" in r.stdout
+
+
+@pytest.mark.gpu
+def test_selfplay_harness_on_gpu(tmp_path):
+    """selfplay_cuda (built where the reference tree is present; it travels
+    with the package) plays real games on the GPU for a short window."""
+    import json
+
+    if not os.path.exists(build.SELFPLAY_BIN):
+        pytest.skip("selfplay_cuda was not built (no reference tree at build time)")
+    sd = weights.make_state_dict(9, 64, 2, seed=3, variant="init")
+    model = weights.write_onnx(str(tmp_path / "m.onnx"), sd)
+    r = subprocess.run([build.SELFPLAY_BIN, "--model", model, "--workers", "4", "--search-threads", "4",
+                        "--sims", "64", "--max-batch", "64", "--warmup-seconds", "1", "--seconds", "3"],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert out["moves"] > 0 and out["visits_per_s"] > 0
+    assert out["nn_positions_per_s"] > 0 and out["failed_batches"] == 0
+    assert out["gpu_launches"] > 0
