@@ -17,6 +17,7 @@ GpuEvaluator::GpuEvaluator(InferenceEngine* engine, int max_batch_size)
     if (engine_ == nullptr || max_batch_ < 1) throw std::invalid_argument("GpuEvaluator: bad arguments");
     queue_.reserve(max_batch_);
     server_ = std::thread(&GpuEvaluator::server_loop, this);
+    completer_ = std::thread(&GpuEvaluator::completion_loop, this);
 }
 
 GpuEvaluator::~GpuEvaluator() {
@@ -25,7 +26,8 @@ GpuEvaluator::~GpuEvaluator() {
         stop_ = true;
     }
     cv_.notify_all();
-    server_.join();
+    server_.join();  // drains the queue, then tells the completion thread
+    completer_.join();
 }
 
 BatchEvaluator::Result GpuEvaluator::take_result(NNResultBuf& buf) {
@@ -113,59 +115,84 @@ std::vector<BatchEvaluator::Result> GpuEvaluator::evaluate(
     return out;
 }
 
-void GpuEvaluator::run_batch(std::vector<Pending>& batch) {
+void GpuEvaluator::run_batch(Slot& slot) {
+    std::vector<Pending>& batch = slot.batch;
     const int n = (int)batch.size();
+    const auto t0 = std::chrono::steady_clock::now();
     if (cuda_ != nullptr) {
         const int a = cuda_->action_size();
-        bool packed = true;
-        for (const auto& p : batch) packed &= p.bits != nullptr && p.buf->state_size == batch[0].buf->state_size;
-        policy_.resize((size_t)n * a);
-        value_.resize(n);
-        const auto t0 = std::chrono::steady_clock::now();
-        if (packed && batch[0].buf->state_size == cuda_->input_channels * cuda_->board_size * cuda_->board_size) {
+        const int size = batch[0].buf->state_size;
+        bool packed = size == cuda_->input_channels * cuda_->board_size * cuda_->board_size;
+        for (const auto& p : batch) packed &= p.bits != nullptr && p.buf->state_size == size;
+        slot.policy.resize((size_t)n * a);
+        slot.value.resize(n);
+        if (packed) {
             bit_ptrs_.resize(n);
             for (int i = 0; i < n; ++i) bit_ptrs_[i] = batch[i].bits;
-            cuda_->predict_bits(bit_ptrs_.data(), n, policy_.data(), value_.data());
+            cuda_->predict_bits(bit_ptrs_.data(), n, slot.policy.data(), slot.value.data());
         } else {
             ptrs_.resize(n);
             for (int i = 0; i < n; ++i) ptrs_[i] = batch[i].buf->state_data;
-            cuda_->predict_raw(ptrs_.data(), n, batch[0].buf->state_size, policy_.data(), value_.data());
+            cuda_->predict_raw(ptrs_.data(), n, size, slot.policy.data(), slot.value.data());
         }
-        const auto t1 = std::chrono::steady_clock::now();
-        for (int i = 0; i < n; ++i) {
-            NNResultBuf* buf = batch[i].buf;
-            std::lock_guard<std::mutex> lock(buf->mu);
-            buf->policy.assign(policy_.begin() + (size_t)i * a, policy_.begin() + (size_t)(i + 1) * a);
-            buf->value = value_[i];
-            buf->done = true;
-            // Notify under the lock: once the client sees `done` it may return
-            // and destroy its buffer (and condition variable).
-            buf->cv.notify_one();
-        }
-        const auto t2 = std::chrono::steady_clock::now();
-        engine_ns_.fetch_add((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count());
-        scatter_ns_.fetch_add((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(t2 - t1).count());
-        return;
+    } else {
+        std::vector<std::vector<float>> states;
+        states.reserve(n);
+        for (const auto& p : batch) states.emplace_back(p.buf->state_data, p.buf->state_data + p.buf->state_size);
+        slot.results = engine_->predict_batch(states);
+        if ((int)slot.results.size() != n) throw std::runtime_error("engine returned a short batch");
     }
-    std::vector<std::vector<float>> states;
-    states.reserve(n);
-    for (const auto& p : batch) states.emplace_back(p.buf->state_data, p.buf->state_data + p.buf->state_size);
-    auto results = engine_->predict_batch(states);
-    if ((int)results.size() != n) throw std::runtime_error("engine returned a short batch");
+    engine_ns_.fetch_add((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                             std::chrono::steady_clock::now() - t0)
+                             .count());
+}
+
+void GpuEvaluator::hand_back(Slot& slot) {
+    const auto t0 = std::chrono::steady_clock::now();
+    const int n = (int)slot.batch.size();
+    const size_t a = cuda_ != nullptr ? (size_t)cuda_->action_size() : 0;
     for (int i = 0; i < n; ++i) {
-        NNResultBuf* buf = batch[i].buf;
+        NNResultBuf* buf = slot.batch[i].buf;
         std::lock_guard<std::mutex> lock(buf->mu);
-        buf->policy = std::move(results[i].first);
-        buf->value = results[i].second;
+        if (cuda_ != nullptr) {
+            buf->policy.assign(slot.policy.begin() + i * a, slot.policy.begin() + (i + 1) * a);
+            buf->value = slot.value[i];
+        } else {
+            buf->policy = std::move(slot.results[i].first);
+            buf->value = slot.results[i].second;
+        }
         buf->done = true;
+        // Notify under the lock: once the client sees `done` it may return
+        // and destroy its buffer (and condition variable).
         buf->cv.notify_one();
     }
+    slot.batch.clear();
+    slot.results.clear();
+    scatter_ns_.fetch_add((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                              std::chrono::steady_clock::now() - t0)
+                              .count());
+}
+
+void GpuEvaluator::fail_batch(std::vector<Pending>& batch) {
+    // Wake every client of the batch with an empty policy: each one turns
+    // that into an exception on its own thread.
+    for (const auto& p : batch) {
+        NNResultBuf* buf = p.buf;
+        std::lock_guard<std::mutex> lock(buf->mu);
+        if (!buf->done) {
+            buf->policy.clear();
+            buf->value = std::numeric_limits<float>::quiet_NaN();
+            buf->done = true;
+            buf->cv.notify_one();
+        }
+    }
+    batch.clear();
 }
 
 void GpuEvaluator::server_loop() {
     std::vector<Pending> batch;
     batch.reserve(max_batch_);
-    while (true) {
+    for (uint64_t k = 0;; ++k) {
         {
             std::unique_lock<std::mutex> lock(mu_);
             cv_.wait(lock, [this] { return !queue_.empty() || stop_; });
@@ -174,33 +201,62 @@ void GpuEvaluator::server_loop() {
             batch.assign(queue_.begin(), queue_.begin() + n);
             queue_.erase(queue_.begin(), queue_.begin() + n);
         }
+        const int si = (int)(k & 1);
+        Slot& slot = slots_[si];
+        {
+            // The completion thread may still be handing back the batch
+            // that used this slot two batches ago.
+            std::unique_lock<std::mutex> lock(cmu_);
+            ccv_.wait(lock, [&] { return !slot.busy; });
+        }
+        slot.batch.swap(batch);
         try {
-            run_batch(batch);
+            run_batch(slot);
+            const int n = (int)slot.batch.size();
             batches_.fetch_add(1);
-            positions_.fetch_add(batch.size());
+            positions_.fetch_add(n);
             int seen = largest_.load();
-            while ((int)batch.size() > seen && !largest_.compare_exchange_weak(seen, (int)batch.size())) {
+            while (n > seen && !largest_.compare_exchange_weak(seen, n)) {
             }
+            {
+                std::lock_guard<std::mutex> lock(cmu_);
+                slot.busy = true;
+                posted_.push_back(si);
+            }
+            ccv_.notify_all();
         } catch (const std::exception& ex) {
             failed_.fetch_add(1);
             {
                 std::lock_guard<std::mutex> lock(mu_);
                 last_error_ = ex.what();
             }
-            // Wake every client of the batch with an empty policy: each one
-            // turns that into an exception on its own thread.
-            for (const auto& p : batch) {
-                NNResultBuf* buf = p.buf;
-                std::lock_guard<std::mutex> lock(buf->mu);
-                if (!buf->done) {
-                    buf->policy.clear();
-                    buf->value = std::numeric_limits<float>::quiet_NaN();
-                    buf->done = true;
-                    buf->cv.notify_one();
-                }
-            }
+            fail_batch(slot.batch);
         }
         batch.clear();
+    }
+    {
+        std::lock_guard<std::mutex> lock(cmu_);
+        done_ = true;
+    }
+    ccv_.notify_all();
+}
+
+void GpuEvaluator::completion_loop() {
+    while (true) {
+        int si;
+        {
+            std::unique_lock<std::mutex> lock(cmu_);
+            ccv_.wait(lock, [this] { return !posted_.empty() || done_; });
+            if (posted_.empty()) break;  // done_ and nothing left
+            si = posted_.front();
+            posted_.erase(posted_.begin());
+        }
+        hand_back(slots_[si]);
+        {
+            std::lock_guard<std::mutex> lock(cmu_);
+            slots_[si].busy = false;
+        }
+        ccv_.notify_all();
     }
 }
 

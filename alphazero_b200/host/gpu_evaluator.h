@@ -17,6 +17,12 @@
 //     every 24.5 KB fp32 state twice (src/nn_evaluator.cpp:108-112 plus the
 //     engine's flatten), and packing on the server thread alone took 60% of
 //     its time at 19x19 with 1024 search threads;
+//   * handing results back is pipelined with the next engine call: the
+//     server thread forms batch k+1 and runs it on the engine while a
+//     completion thread copies batch k's results into the clients' buffers
+//     and wakes them (two result slots; waking a sleeping client is a
+//     futex call of a few microseconds, half the server's time at 19x19
+//     batch 512 when it was done inline);
 //   * a client is woken while its buffer's mutex is held: the reference
 //     notifies after unlocking (src/nn_evaluator.cpp:127-137), so a client
 //     that sees `done` can return and destroy its stack NNResultBuf while
@@ -60,8 +66,9 @@ public:
     uint64_t positions() const { return positions_.load(); }
     int largest_batch() const { return largest_.load(); }
     uint64_t failed_batches() const { return failed_.load(); }
-    // Server-thread time (ns) in the engine call (gather, H2D, forward, D2H)
-    // and in handing results back to the clients (copy + wake-up).
+    // Time (ns) in the engine call (server thread: gather, H2D, forward,
+    // D2H) and in handing results back to the clients (completion thread:
+    // copy + wake-up).
     uint64_t engine_ns() const { return engine_ns_.load(); }
     uint64_t scatter_ns() const { return scatter_ns_.load(); }
 
@@ -72,8 +79,18 @@ private:
         NNResultBuf* buf;
         const uint32_t* bits;
     };
+    // One batch between the server and the completion thread.
+    struct Slot {
+        std::vector<Pending> batch;
+        std::vector<float> policy, value;  // CudaEngine results, flat
+        std::vector<Result> results;       // other engines' results
+        bool busy = false;                 // posted, not yet handed back
+    };
     void server_loop();
-    void run_batch(std::vector<Pending>& batch);
+    void completion_loop();
+    void run_batch(Slot& slot);
+    void hand_back(Slot& slot);
+    void fail_batch(std::vector<Pending>& batch);
     void enqueue(const Pending* items, size_t n);
     Result take_result(NNResultBuf& buf);
 
@@ -89,12 +106,17 @@ private:
 
     std::vector<const float*> ptrs_;
     std::vector<const uint32_t*> bit_ptrs_;
-    std::vector<float> policy_, value_;
+
+    Slot slots_[2];
+    std::mutex cmu_;  // guards slots_[*].busy, posted_, done_
+    std::condition_variable ccv_;
+    std::vector<int> posted_;  // slots waiting for the completion thread
+    bool done_ = false;        // the server has exited
 
     std::atomic<uint64_t> batches_{0}, positions_{0}, failed_{0};
     std::atomic<uint64_t> engine_ns_{0}, scatter_ns_{0};
     std::atomic<int> largest_{0};
-    std::thread server_;
+    std::thread server_, completer_;
 };
 
 class ShardedEvaluator : public BatchEvaluator {
