@@ -149,8 +149,8 @@ int mg_forward_device(mg_engine* e, const float* d_states, int n, float* d_polic
  * library, so it suits callers that may not call cudaMalloc/cudaFree once
  * running (both synchronise the device; cudaFree waits for all of it) or
  * that work inside a fixed GPU memory budget.  No counterpart in the
- * reference.  Limits: n is capped by the arena (19x19 bf16: 71 positions
- * with 128 filters, 38 with 256; the error message states the cap); the first call on
+ * reference.  Limits: n is capped by the arena (19x19 bf16: 70 positions
+ * with 128 filters, 37 with 256; the error message states the cap); the first call on
  * a device looks up the arena's address and should come before any stream
  * capture; all calls on a device share the arena, so calls whose work
  * overlaps on the GPU race and must be serialised.  Blocks until the results
