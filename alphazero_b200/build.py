@@ -5,7 +5,8 @@
   libminigo_host.so  CPU-only helpers (include/minigo_host.h): position
                      generator and ONNX reader; g++.
   libminigo_evaluator.so  CudaEngine / GpuEvaluator / ShardedEvaluator
-                     (the reference's C++ interfaces over the C ABI).
+                     (the reference's C++ interfaces over the C ABI) and
+                     FastSearch (the reference's MCTS at a lower host cost).
   selfplay_cuda      end-to-end self-play harness: the reference's own
                      search (src/mcts.cpp, src/game.cpp) compiled unmodified
                      from the reference tree with this backend's evaluator;
@@ -63,11 +64,16 @@ HOST_HEADERS = [
 EVAL_SOURCES = [
     os.path.join(HOST, "cuda_engine.cpp"),
     os.path.join(HOST, "gpu_evaluator.cpp"),
+    os.path.join(HOST, "fast_search.cpp"),
+    os.path.join(HOST, "go_positions.cpp"),
 ]
 EVAL_HEADERS = [
     os.path.join(HOST, "cuda_engine.h"),
     os.path.join(HOST, "gpu_evaluator.h"),
     os.path.join(HOST, "minigo_api.h"),
+    os.path.join(HOST, "packed_evaluator.h"),
+    os.path.join(HOST, "fast_search.h"),
+    os.path.join(HOST, "go_positions.h"),
     os.path.join(INCLUDE, "minigo_cuda.h"),
 ]
 
@@ -75,8 +81,12 @@ SELFPLAY_SOURCES = [
     os.path.join(HOST, "selfplay_main.cpp"),
     os.path.join(HOST, "cuda_engine.cpp"),
     os.path.join(HOST, "gpu_evaluator.cpp"),
+    os.path.join(HOST, "fast_search.cpp"),
+    os.path.join(HOST, "go_positions.cpp"),
 ]
-SELFPLAY_HEADERS = EVAL_HEADERS + [os.path.join(HOST, "selfplay_loop.h")]
+SELFPLAY_HEADERS = EVAL_HEADERS + [os.path.join(HOST, h) for h in (
+    "selfplay_loop.h", "selfplay_window.h", "fast_selfplay.h", "fast_search.h", "go_positions.h",
+    "packed_evaluator.h")]
 # The reference tree the self-play harness compiles src/mcts.cpp and
 # src/game.cpp from (read in place, never copied).
 REFERENCE_TREE = os.environ.get("MGB_REFERENCE_TREE", "/root/reference")

@@ -144,6 +144,35 @@ void GoPosition::encode(float* out) const {
     }
 }
 
+void GoPosition::encode_bits(uint32_t* words) const {
+    const int nn = n_ * n_;
+    const int nw = packed_words();
+    std::memset(words, 0, sizeof(uint32_t) * (size_t)nw);
+    auto set = [&](int j) { words[j >> 5] |= 1u << (j & 31); };
+    const int8_t us = (int8_t)to_move_, them = (int8_t)(3 - to_move_);
+    for (int i = 0; i < hist_len_; ++i) {
+        const int8_t* snap = hist_[(hist_top_ - i + kHistory) % kHistory];
+        const int mine = i * nn, theirs = (kHistory + i) * nn;
+        for (int q = 0; q < nn; ++q) {
+            if (snap[q] == us) set(mine + q);
+            else if (snap[q] == them) set(theirs + q);
+        }
+    }
+    if (to_move_ == 1) {
+        // plane 16: bits [16 * nn, 17 * nn) all set
+        int j = 2 * kHistory * nn;
+        const int end = j + nn;
+        for (; j < end && (j & 31); ++j) set(j);
+        for (; j + 32 <= end; j += 32) words[j >> 5] = 0xffffffffu;
+        for (; j < end; ++j) set(j);
+    }
+}
+
+void GoPosition::legal_mask(uint8_t* out) const {
+    const int nn = n_ * n_;
+    for (int a = 0; a <= nn; ++a) out[a] = legal(a) ? 1 : 0;
+}
+
 void GoPosition::decide_winner() {
     const int nn = n_ * n_;
     float area[3] = {0.f, 0.f, 0.f};

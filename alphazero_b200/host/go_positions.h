@@ -33,6 +33,13 @@ public:
     bool legal(int action) const;  // action in [0, n*n]; n*n = pass
     void play(int action);         // caller guarantees legal(action)
     void encode(float* out) const; // kInputPlanes * n * n floats, plane-major
+    // The same planes in the bit-packed wire format of mg_forward_packed:
+    // element j = plane * n * n + point at bit j % 32 of word j / 32;
+    // packed_words() words, the unused tail bits zero.
+    void encode_bits(uint32_t* words) const;
+    int packed_words() const { return (kInputPlanes * n_ * n_ + 31) / 32; }
+    // out[a] = 1 if legal(a) else 0, for a in [0, n * n] (pass last).
+    void legal_mask(uint8_t* out) const;
 
     int size() const { return n_; }
     bool over() const { return over_; }

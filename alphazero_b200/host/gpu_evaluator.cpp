@@ -75,6 +75,29 @@ BatchEvaluator::Result GpuEvaluator::evaluate_with_buf(NNResultBuf& buf,
     return take_result(buf);
 }
 
+void GpuEvaluator::evaluate_packed(const uint32_t* words, int n_words, float* policy, float* value) {
+    if (cuda_ == nullptr) throw std::logic_error("evaluate_packed needs a CudaEngine");
+    const int size = cuda_->input_channels * cuda_->board_size * cuda_->board_size;
+    if (n_words != (size + 31) / 32)
+        throw std::invalid_argument("packed state has " + std::to_string(n_words) + " words, expected " +
+                                    std::to_string((size + 31) / 32));
+    // One buffer per client thread, as the reference's search keeps one per
+    // search thread (src/mcts.cpp:133).
+    thread_local NNResultBuf buf;
+    buf.done = false;
+    buf.state_data = nullptr;
+    buf.state_size = size;
+    Pending p{&buf, words};
+    enqueue(&p, 1);
+    {
+        std::unique_lock<std::mutex> lock(buf.mu);
+        buf.cv.wait(lock, [&] { return buf.done; });
+    }
+    if (buf.policy.empty()) (void)take_result(buf);  // throws with the server's error
+    std::copy(buf.policy.begin(), buf.policy.end(), policy);
+    *value = buf.value;
+}
+
 BatchEvaluator::Result GpuEvaluator::evaluate_single(const std::vector<float>& state) {
     NNResultBuf buf;
     return evaluate_with_buf(buf, state);
@@ -131,8 +154,21 @@ void GpuEvaluator::run_batch(Slot& slot) {
             for (int i = 0; i < n; ++i) bit_ptrs_[i] = batch[i].bits;
             cuda_->predict_bits(bit_ptrs_.data(), n, slot.policy.data(), slot.value.data());
         } else {
+            // Mixed batch: fp32 planes for all; packed-only requests
+            // (evaluate_packed) are unpacked first.
             ptrs_.resize(n);
-            for (int i = 0; i < n; ++i) ptrs_[i] = batch[i].buf->state_data;
+            int unpack = 0;
+            for (const auto& p : batch) unpack += p.buf->state_data == nullptr;
+            unpacked_.resize((size_t)unpack * size);
+            for (int i = 0, u = 0; i < n; ++i) {
+                if (batch[i].buf->state_data != nullptr) {
+                    ptrs_[i] = batch[i].buf->state_data;
+                    continue;
+                }
+                float* dst = unpacked_.data() + (size_t)u++ * size;
+                for (int j = 0; j < size; ++j) dst[j] = (float)((batch[i].bits[j >> 5] >> (j & 31)) & 1u);
+                ptrs_[i] = dst;
+            }
             cuda_->predict_raw(ptrs_.data(), n, size, slot.policy.data(), slot.value.data());
         }
     } else {
@@ -305,6 +341,10 @@ int ShardedEvaluator::shard_of_this_thread() {
 BatchEvaluator::Result ShardedEvaluator::evaluate_with_buf(NNResultBuf& buf,
                                                           const std::vector<float>& state) {
     return shards_[shard_of_this_thread()]->evaluate_with_buf(buf, state);
+}
+
+void ShardedEvaluator::evaluate_packed(const uint32_t* words, int n_words, float* policy, float* value) {
+    shards_[shard_of_this_thread()]->evaluate_packed(words, n_words, policy, value);
 }
 
 BatchEvaluator::Result ShardedEvaluator::evaluate_single(const std::vector<float>& state) {

@@ -36,6 +36,7 @@
 #pragma once
 
 #include "minigo_api.h"
+#include "packed_evaluator.h"
 
 #include <atomic>
 #include <condition_variable>
@@ -50,7 +51,7 @@ namespace minigo {
 
 class CudaEngine;
 
-class GpuEvaluator : public BatchEvaluator {
+class GpuEvaluator : public BatchEvaluator, public mgb::PackedEvaluator {
 public:
     GpuEvaluator(InferenceEngine* engine, int max_batch_size);
     ~GpuEvaluator() override;
@@ -60,6 +61,9 @@ public:
     std::vector<Result> evaluate(const std::vector<std::vector<float>>& states) override;
     Result evaluate_with_buf(NNResultBuf& buf, const std::vector<float>& state) override;
     Result evaluate_single(const std::vector<float>& state) override;
+    // A position already in the bit-packed wire format (CudaEngine only):
+    // queued like evaluate_with_buf, with no fp32 planes at all.
+    void evaluate_packed(const uint32_t* words, int n_words, float* policy, float* value) override;
 
     // Counters (for batching statistics and tests).
     uint64_t batches() const { return batches_.load(); }
@@ -106,6 +110,7 @@ private:
 
     std::vector<const float*> ptrs_;
     std::vector<const uint32_t*> bit_ptrs_;
+    std::vector<float> unpacked_;  // fp32 planes of packed-only requests in a mixed batch
 
     Slot slots_[2];
     std::mutex cmu_;  // guards slots_[*].busy, posted_, done_
@@ -119,7 +124,7 @@ private:
     std::thread server_, completer_;
 };
 
-class ShardedEvaluator : public BatchEvaluator {
+class ShardedEvaluator : public BatchEvaluator, public mgb::PackedEvaluator {
 public:
     // One GpuEvaluator per engine (the engines stay owned by the caller).
     ShardedEvaluator(const std::vector<InferenceEngine*>& engines, int max_batch_size);
@@ -137,6 +142,7 @@ public:
     // Routed to the calling thread's shard.
     Result evaluate_with_buf(NNResultBuf& buf, const std::vector<float>& state) override;
     Result evaluate_single(const std::vector<float>& state) override;
+    void evaluate_packed(const uint32_t* words, int n_words, float* policy, float* value) override;
 
     size_t shards() const { return shards_.size(); }
     GpuEvaluator& shard(size_t i) { return *shards_[i]; }

@@ -11,8 +11,11 @@
 //   selfplay_cuda --model M.onnx [--gpus N] [--workers 64] [--search-threads 16]
 //                 [--sims 800] [--max-batch 512] [--warmup-seconds 10]
 //                 [--seconds 30] [--precision bf16|fp16|fp32]
-//                 [--servers-per-gpu K]
+//                 [--servers-per-gpu K] [--search reference|fast]
 //
+// --search fast replaces the reference's search with FastSearch
+// (fast_search.h: the same algorithm at a lower host cost per visit, boards
+// encoded straight to the bit-packed wire format).
 // With K > 1 each GPU gets K engines (each its own weights copy, stream and
 // buffers) and K batching servers, so one server's host work (gathering the
 // batch, waking its clients) overlaps another's GPU work.
@@ -20,6 +23,7 @@
 // Prints one JSON line: MCTS visits/s (searches completed in the measured
 // window x simulations per search), NN positions/s and mean batch size.
 #include "cuda_engine.h"
+#include "fast_selfplay.h"
 #include "gpu_evaluator.h"
 #include "selfplay_loop.h"
 
@@ -39,6 +43,7 @@ int main(int argc, char** argv) {
     int gpus = 1, workers = 64, search_threads = 16, sims = 800, max_batch = 512, per_gpu = 1;
     double warmup_s = 10.0, measure_s = 30.0;
     CudaEngine::Precision prec = CudaEngine::kBf16;
+    bool fast = false;
     for (int i = 1; i < argc; ++i) {
         const std::string a = argv[i];
         auto next = [&]() -> const char* {
@@ -55,6 +60,14 @@ int main(int argc, char** argv) {
         else if (a == "--sims") sims = std::atoi(next());
         else if (a == "--max-batch") max_batch = std::atoi(next());
         else if (a == "--servers-per-gpu") per_gpu = std::atoi(next());
+        else if (a == "--search") {
+            const std::string v = next();
+            if (v != "fast" && v != "reference") {
+                std::fprintf(stderr, "--search takes reference or fast\n");
+                return 2;
+            }
+            fast = v == "fast";
+        }
         else if (a == "--warmup-seconds") warmup_s = std::atof(next());
         else if (a == "--seconds") measure_s = std::atof(next());
         else if (a == "--precision") {
@@ -104,8 +117,22 @@ int main(int argc, char** argv) {
                 c.pack_ns += e->pack_ns();
             }
         };
-        const mgb_selfplay::Window w =
-            mgb_selfplay::run(&evaluator, config, workers, warmup_s, measure_s, nn);
+        mgb_selfplay::Window w;
+        if (fast) {
+            mgb_selfplay::FastGameParams fp;
+            fp.board = config.board_size;
+            fp.komi = config.komi;
+            fp.max_moves = config.max_moves_per_game;
+            fp.temperature_threshold = config.temperature_threshold;
+            fp.search.simulations = sims;
+            fp.search.c_puct = config.c_puct;
+            fp.search.dirichlet_alpha = config.dirichlet_alpha;
+            fp.search.dirichlet_epsilon = config.dirichlet_epsilon;
+            fp.search.threads = search_threads;
+            w = mgb_selfplay::run_fast(&evaluator, fp, workers, warmup_s, measure_s, nn);
+        } else {
+            w = mgb_selfplay::run(&evaluator, config, workers, warmup_s, measure_s, nn);
+        }
 
         const double moves = (double)(w.end.moves - w.begin.moves);
         const double pos = (double)(w.end.nn_positions - w.begin.nn_positions);
@@ -115,12 +142,13 @@ int main(int argc, char** argv) {
         std::printf(
             "{\"visits_per_s\": %.3f, \"nn_positions_per_s\": %.3f, \"moves_per_s\": %.4f, "
             "\"mean_batch\": %.2f, \"seconds\": %.3f, \"moves\": %.0f, \"games_finished\": %llu, "
-            "\"gpus\": %d, \"servers_per_gpu\": %d, \"workers\": %d, \"search_threads\": %d, \"sims\": %d, "
+            "\"search\": \"%s\", \"gpus\": %d, \"servers_per_gpu\": %d, \"workers\": %d, \"search_threads\": %d, \"sims\": %d, "
             "\"max_batch\": %d, \"board\": %d, \"filters\": %d, \"blocks\": %d, "
             "\"host_threads\": %u, \"failed_batches\": %llu, \"gpu_launches\": %llu, "
             "\"server_engine_frac\": %.3f, \"server_pack_frac\": %.3f, \"server_scatter_frac\": %.3f}\n",
             moves * sims / w.seconds, pos / w.seconds, moves / w.seconds, bat > 0 ? pos / bat : 0.0,
-            w.seconds, moves, (unsigned long long)(w.end.games - w.begin.games), gpus, per_gpu, workers,
+            w.seconds, moves, (unsigned long long)(w.end.games - w.begin.games), fast ? "fast" : "reference",
+            gpus, per_gpu, workers,
             search_threads, sims, max_batch, config.board_size, config.num_filters,
             config.num_res_blocks, std::thread::hardware_concurrency(),
             (unsigned long long)failed,

@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                     [--workload b19c128x10_bs512|b19c256x20_bs1024|b9c128x10_bs256|b9c64x6_bs16
-                                |selfplay_b19c128x10]
+                                |selfplay_b19c128x10|selfplay_b19c128x10_fast]
 
 A step is one forward pass of the network over one batch of seeded random-
 playout positions.  Under torchrun each rank drives its own GPU with its own
@@ -27,7 +27,9 @@ JSON line.  Numbers:
 selfplay_b19c128x10 is end-to-end self-play instead: the reference's own
 search (src/mcts.cpp, compiled unmodified) with 64 game workers x 16 search
 threads, 800 simulations per move, max batch 512, over one batching server
-and engine per GPU (alphazero_b200/lib/selfplay_cuda).  One process drives
+and engine per GPU (alphazero_b200/lib/selfplay_cuda); selfplay_b19c128x10_fast
+is the same with FastSearch (alphazero_b200/host/fast_search.h, the
+reference's algorithm at a lower host cost per visit).  One process drives
 all N GPUs (under torchrun rank 0 runs it, the other ranks wait).  A step is
 one second of the measured window (at least 10), a warm-up step two seconds
 (at least 6).  value = MCTS visits/s = searches completed in the window x 800
@@ -66,7 +68,12 @@ SELFPLAY_WORKLOADS = {
     # name: (board, filters, blocks, game workers, search threads per search,
     #        simulations per move, max batch per evaluator)
     "selfplay_b19c128x10": (19, 128, 10, 64, 16, 800, 512),
+    "selfplay_b19c128x10_fast": (19, 128, 10, 64, 16, 800, 512),
 }
+
+
+def selfplay_search(wl):
+    return "fast" if wl.endswith("_fast") else "reference"
 DEFAULT_WORKLOAD = "b19c128x10_bs512"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
@@ -433,7 +440,8 @@ def selfplay_config(wl):
                         f"{threads} search threads, {sims} simulations per move, max batch {max_batch}",
             "board": board, "filters": filters, "blocks": blocks, "workers": workers,
             "search_threads": threads, "simulations": sims, "max_batch": max_batch,
-            "search": "reference src/mcts.cpp compiled unmodified",
+            "search": ("FastSearch (the reference's MCTS algorithm, own implementation)"
+                       if selfplay_search(wl) == "fast" else "reference src/mcts.cpp compiled unmodified"),
             "weights": "seeded random init (export_onnx --init distributions)",
             "parallelism": "one batching server + engine per GPU, search threads round-robin, "
                            "weights replicated, no collective"}
@@ -444,12 +452,14 @@ def selfplay_window(args):
     return max(6.0, 2.0 * args.warmup), max(10.0, float(args.steps))
 
 
-def run_selfplay_binary(exe, model, wl, args, gpus):
+def run_selfplay_binary(exe, model, wl, args, gpus, search=None):
     board, filters, blocks, workers, threads, sims, max_batch = SELFPLAY_WORKLOADS[wl]
     warm, window = selfplay_window(args)
     cmd = [exe, "--model", model, "--gpus", str(gpus), "--workers", str(workers),
            "--search-threads", str(threads), "--sims", str(sims), "--max-batch", str(max_batch),
            "--warmup-seconds", str(warm), "--seconds", str(window)]
+    if search is not None:
+        cmd += ["--search", search]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=warm + window + 600)
     if r.returncode != 0:
         raise RuntimeError(f"{os.path.basename(exe)} failed ({r.returncode}): {r.stderr[-2000:]}")
@@ -481,7 +491,8 @@ def run_selfplay(args, wl):
     line = None
     if rank == 0:
         metric = (f"MCTS visits/sec (self-play {board}x{board} b{blocks}c{filters}, {workers} workers x "
-                  f"{threads} search threads, {sims} sims)")
+                  f"{threads} search threads, {sims} sims"
+                  + (", FastSearch)" if selfplay_search(wl) == "fast" else ")"))
         if args.impl == "reference":
             out, why = oracle_selfplay(wl, args)
             if out is None:
@@ -507,7 +518,8 @@ def run_selfplay(args, wl):
                                  "is needed at build time")
             gpus = max(args.gpus, world)
             with ClockSampler(0) as clocks:
-                out = run_selfplay_binary(build.SELFPLAY_BIN, selfplay_model(wl), wl, args, gpus)
+                out = run_selfplay_binary(build.SELFPLAY_BIN, selfplay_model(wl), wl, args, gpus,
+                                          search=selfplay_search(wl))
             base = None
             if gpus == 1 and not args.no_cpu_baseline:
                 base_out, _ = oracle_selfplay(wl, args)

@@ -92,6 +92,30 @@ int main(int argc, char** argv) {
     CHECK(sh.shard(0).positions() > 0 && sh.shard(1).positions() > 0);
     auto all = sh.evaluate(states);
     for (int i = 0; i < n; ++i) CHECK(maxdiff(all[i].first, batch[i].first) < 1e-5f);
+
+    // Bit-packed requests (evaluate_packed, the FastSearch path), alone and
+    // mixed into batches with fp32-plane requests, give the same results.
+    std::vector<std::vector<uint32_t>> words(n, std::vector<uint32_t>((per + 31) / 32));
+    for (int i = 0; i < n; ++i) CHECK(CudaEngine::pack_planes(states[i].data(), per, words[i].data()));
+    std::atomic<int> bad_packed{0};
+    th.clear();
+    for (int t = 0; t < T; ++t)
+        th.emplace_back([&, t] {
+            NNResultBuf buf;
+            std::vector<float> p(362);
+            float v = 0.0f;
+            for (int i = t; i < n; i += T) {
+                if ((i + t) % 2) {
+                    sh.evaluate_packed(words[i].data(), (int)words[i].size(), p.data(), &v);
+                    if (maxdiff(p, batch[i].first) > 1e-5f || std::fabs(v - batch[i].second) > 1e-5f) bad_packed++;
+                } else {
+                    auto r = sh.evaluate_with_buf(buf, states[i]);
+                    if (maxdiff(r.first, batch[i].first) > 1e-5f) bad_packed++;
+                }
+            }
+        });
+    for (auto& x : th) x.join();
+    CHECK(bad_packed == 0);
     std::printf("sharded ok: %llu + %llu positions\n", (unsigned long long)sh.shard(0).positions(),
                 (unsigned long long)sh.shard(1).positions());
     return 0;

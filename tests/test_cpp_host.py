@@ -93,3 +93,48 @@ def test_selfplay_harness_on_gpu(tmp_path):
     assert out["moves"] > 0 and out["visits_per_s"] > 0
     assert out["nn_positions_per_s"] > 0 and out["failed_batches"] == 0
     assert out["gpu_launches"] > 0
+
+
+@pytest.mark.skipif(not all(os.path.exists(p) for p in _REF_SEARCH),
+                    reason="the reference tree (src/mcts.cpp, src/game.cpp) is not present")
+@pytest.mark.parametrize("sanitize", [False, True])
+def test_fast_search_against_the_reference_mcts(tmp_path, sanitize):
+    """FastSearch / GoPosition against the reference's own MCTS and GoGame:
+    identical rules move by move, identical root visits for a single-threaded
+    search without noise, the thread pool (also under ThreadSanitizer) and
+    the failure path."""
+    exe = str(tmp_path / "test_fast_search")
+    cmd = ["g++", "-std=c++17", "-O1" if sanitize else "-O2", "-g", "-pthread",
+           "-I" + os.path.join(build.REFERENCE_TREE, "include"), "-I" + HOST,
+           os.path.join(CPP, "test_fast_search.cpp"), os.path.join(HOST, "fast_search.cpp"),
+           os.path.join(HOST, "go_positions.cpp")] + _REF_SEARCH + ["-o", exe]
+    if sanitize:
+        cmd.append("-fsanitize=thread")
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    env = dict(os.environ, TSAN_OPTIONS="halt_on_error=1")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "fast search tests passed" in r.stdout
+    if sanitize:
+        assert "ThreadSanitizer" not in r.stderr
+
+
+@pytest.mark.gpu
+def test_fast_selfplay_harness_on_gpu(tmp_path):
+    """selfplay_cuda --search fast: FastSearch through ShardedEvaluator's
+    packed path on the GPU for a short window."""
+    import json
+
+    if not os.path.exists(build.SELFPLAY_BIN):
+        pytest.skip("selfplay_cuda was not built (no reference tree at build time)")
+    sd = weights.make_state_dict(9, 64, 2, seed=3, variant="init")
+    model = weights.write_onnx(str(tmp_path / "m.onnx"), sd)
+    r = subprocess.run([build.SELFPLAY_BIN, "--model", model, "--search", "fast", "--workers", "4",
+                        "--search-threads", "4", "--sims", "64", "--max-batch", "64",
+                        "--warmup-seconds", "1", "--seconds", "3"],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert out["search"] == "fast" and out["moves"] > 0 and out["visits_per_s"] > 0
+    assert out["failed_batches"] == 0 and out["gpu_launches"] > 0
