@@ -66,6 +66,7 @@ EVAL_SOURCES = [
     os.path.join(HOST, "gpu_evaluator.cpp"),
     os.path.join(HOST, "fast_search.cpp"),
     os.path.join(HOST, "go_positions.cpp"),
+    os.path.join(HOST, "selfplay_records.cpp"),
 ]
 EVAL_HEADERS = [
     os.path.join(HOST, "cuda_engine.h"),
@@ -74,6 +75,7 @@ EVAL_HEADERS = [
     os.path.join(HOST, "packed_evaluator.h"),
     os.path.join(HOST, "fast_search.h"),
     os.path.join(HOST, "go_positions.h"),
+    os.path.join(HOST, "selfplay_records.h"),
     os.path.join(INCLUDE, "minigo_cuda.h"),
 ]
 
@@ -83,10 +85,11 @@ SELFPLAY_SOURCES = [
     os.path.join(HOST, "gpu_evaluator.cpp"),
     os.path.join(HOST, "fast_search.cpp"),
     os.path.join(HOST, "go_positions.cpp"),
+    os.path.join(HOST, "selfplay_records.cpp"),
 ]
 SELFPLAY_HEADERS = EVAL_HEADERS + [os.path.join(HOST, h) for h in (
     "selfplay_loop.h", "selfplay_window.h", "fast_selfplay.h", "fast_search.h", "go_positions.h",
-    "packed_evaluator.h")]
+    "packed_evaluator.h", "selfplay_records.h")]
 # The reference tree the self-play harness compiles src/mcts.cpp and
 # src/game.cpp from (read in place, never copied).
 REFERENCE_TREE = os.environ.get("MGB_REFERENCE_TREE", "/root/reference")

@@ -16,6 +16,12 @@
 // --search fast replaces the reference's search with FastSearch
 // (fast_search.h: the same algorithm at a lower host cost per visit, boards
 // encoded straight to the bit-packed wire format).
+//
+//   selfplay_cuda --model M.onnx --search fast --games N [--records DIR] ...
+//
+// plays N whole games instead of a timed window, like the reference's
+// selfplay binary (src/main_selfplay.cpp:86-122), and writes each game's
+// 8-fold augmented training records to DIR/game_<i>.bin in its format.
 // With K > 1 each GPU gets K engines (each its own weights copy, stream and
 // buffers) and K batching servers, so one server's host work (gathering the
 // batch, waking its clients) overlaps another's GPU work.
@@ -26,7 +32,10 @@
 #include "fast_selfplay.h"
 #include "gpu_evaluator.h"
 #include "selfplay_loop.h"
+#include "selfplay_records.h"
 
+#include <atomic>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -44,6 +53,8 @@ int main(int argc, char** argv) {
     double warmup_s = 10.0, measure_s = 30.0;
     CudaEngine::Precision prec = CudaEngine::kBf16;
     bool fast = false;
+    int games = 0;
+    std::string records_dir;
     for (int i = 1; i < argc; ++i) {
         const std::string a = argv[i];
         auto next = [&]() -> const char* {
@@ -60,6 +71,8 @@ int main(int argc, char** argv) {
         else if (a == "--sims") sims = std::atoi(next());
         else if (a == "--max-batch") max_batch = std::atoi(next());
         else if (a == "--servers-per-gpu") per_gpu = std::atoi(next());
+        else if (a == "--games") games = std::atoi(next());
+        else if (a == "--records") records_dir = next();
         else if (a == "--search") {
             const std::string v = next();
             if (v != "fast" && v != "reference") {
@@ -117,6 +130,44 @@ int main(int argc, char** argv) {
                 c.pack_ns += e->pack_ns();
             }
         };
+        if (games > 0) {
+            if (!fast) {
+                std::fprintf(stderr, "--games needs --search fast\n");
+                return 2;
+            }
+            mgb::SearchParams sp;
+            sp.simulations = sims;
+            sp.c_puct = config.c_puct;
+            sp.dirichlet_alpha = config.dirichlet_alpha;
+            sp.dirichlet_epsilon = config.dirichlet_epsilon;
+            sp.threads = search_threads;
+            std::atomic<int> next_game{0};
+            std::atomic<uint64_t> moves{0}, records{0};
+            const auto t0 = std::chrono::steady_clock::now();
+            std::vector<std::thread> pool;
+            for (int i = 0; i < workers; ++i)
+                pool.emplace_back([&, i] {
+                    mgb::FastSearch search(&evaluator, config.board_size, sp, 1000 + (uint64_t)i);
+                    for (int g; (g = next_game.fetch_add(1)) < games;) {
+                        auto recs = mgb::self_play_game(search, config.board_size, config.komi,
+                                                        config.max_moves_per_game,
+                                                        config.temperature_threshold);
+                        moves += recs.size() / 8;
+                        records += recs.size();
+                        if (!records_dir.empty())
+                            mgb::write_records(records_dir + "/game_" + std::to_string(g) + ".bin", recs);
+                    }
+                });
+            for (auto& t : pool) t.join();
+            const double secs =
+                std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            std::printf("{\"games\": %d, \"seconds\": %.3f, \"moves\": %llu, \"records\": %llu, "
+                        "\"visits_per_s\": %.3f, \"seconds_per_game\": %.3f}\n",
+                        games, secs, (unsigned long long)moves.load(), (unsigned long long)records.load(),
+                        (double)moves.load() * sims / secs, secs / games);
+            std::fflush(stdout);
+            return 0;
+        }
         mgb_selfplay::Window w;
         if (fast) {
             mgb_selfplay::FastGameParams fp;

@@ -138,3 +138,61 @@ def test_fast_selfplay_harness_on_gpu(tmp_path):
     out = json.loads(r.stdout.strip().splitlines()[-1])
     assert out["search"] == "fast" and out["moves"] > 0 and out["visits_per_s"] > 0
     assert out["failed_batches"] == 0 and out["gpu_launches"] > 0
+
+    # whole games with record files in the reference selfplay's format
+    rec_dir = tmp_path / "records"
+    rec_dir.mkdir()
+    r = subprocess.run([build.SELFPLAY_BIN, "--model", model, "--search", "fast", "--games", "2",
+                        "--records", str(rec_dir), "--workers", "2", "--search-threads", "4",
+                        "--sims", "32", "--max-batch", "64"],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert out["games"] == 2 and out["records"] == 8 * out["moves"] > 0
+    total = 0
+    for f in sorted(rec_dir.glob("game_*.bin")):
+        data = f.read_bytes()
+        n = int(np.frombuffer(data[:4], np.int32)[0])
+        rec = 4 + 17 * 81 * 4 + 4 + 82 * 4 + 4 + 4
+        assert len(data) == 4 + n * rec
+        total += n
+    assert total == out["records"]
+
+
+@pytest.mark.skipif(not all(os.path.exists(p) for p in _REF_SEARCH)
+                    or not os.path.exists(os.path.join(build.REFERENCE_TREE, "scripts", "train.py")),
+                    reason="the reference tree (src/mcts.cpp, scripts/train.py) is not present")
+def test_selfplay_records_against_the_reference(tmp_path):
+    """Training records: the 8-fold augmentation reproduces the reference's
+    own self-play records bit for bit, and a FastSearch game's record file is
+    read back by the reference trainer's reader (scripts/train.py:33-55)."""
+    import importlib.util
+    import sys
+
+    exe = str(tmp_path / "test_selfplay_records")
+    cmd = ["g++", "-std=c++17", "-O2", "-g", "-pthread",
+           "-I" + os.path.join(build.REFERENCE_TREE, "include"), "-I" + HOST,
+           os.path.join(CPP, "test_selfplay_records.cpp"), os.path.join(HOST, "selfplay_records.cpp"),
+           os.path.join(HOST, "fast_search.cpp"), os.path.join(HOST, "go_positions.cpp")] + _REF_SEARCH + ["-o", exe]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    path = str(tmp_path / "game_0.bin")
+    r = subprocess.run([exe, path], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "records tests passed" in r.stdout
+    count = int(r.stdout.split("records ")[1].split()[0])
+
+    scripts = os.path.join(build.REFERENCE_TREE, "scripts")
+    sys.path.insert(0, scripts)
+    try:
+        spec = importlib.util.spec_from_file_location("reference_train", os.path.join(scripts, "train.py"))
+        train = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(train)
+    finally:
+        sys.path.remove(scripts)
+    recs = train.read_selfplay_data(path)
+    assert len(recs) == count and count % 8 == 0
+    for state, policy, value in recs:
+        assert state.shape == (17 * 25,) and policy.shape == (26,)
+        assert set(np.unique(state)) <= {0.0, 1.0}
+        assert abs(float(policy.sum()) - 1.0) < 1e-5 and value in (-1.0, 0.0, 1.0)
