@@ -153,7 +153,7 @@ def test_fast_selfplay_harness_on_gpu(tmp_path):
     for f in sorted(rec_dir.glob("game_*.bin")):
         data = f.read_bytes()
         n = int(np.frombuffer(data[:4], np.int32)[0])
-        rec = 4 + 17 * 81 * 4 + 4 + 82 * 4 + 4 + 4
+        rec = 4 + 17 * 81 * 4 + 4 + 82 * 4 + 4  # sizes, state, policy, value
         assert len(data) == 4 + n * rec
         total += n
     assert total == out["records"]
