@@ -398,16 +398,21 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
         }
         tc_fence_before();
         if (progress != nullptr) {
-            // This warp's stores of the tile are done; the last of the
-            // epilogue warps publishes the CTA's count of finished tiles.
-            fence_proxy_async_global();
-            __threadfence();
+            // This warp's stores of the tile are done (the warp barrier
+            // orders every lane's stores before lane 0's release).  The
+            // epilogue warps count themselves in at CTA scope; the last one,
+            // whose acquire sees the others' stores, alone pays for the
+            // GPU-scope fences and publishes the CTA's count of finished
+            // tiles (a full fence in every warp stalled the epilogue).
             __syncwarp();
             if (lane == 0) {
                 const unsigned before = atom_add_acq_rel_cta(smem_u32(&tcount[acc]), 1u);
                 if (before == (unsigned)(kEpiWarps * use + kEpiWarps - 1) &&
-                    (int)blockIdx.x != a.withhold_cta)
+                    (int)blockIdx.x != a.withhold_cta) {
+                    fence_proxy_async_global();
+                    __threadfence();
                     red_max_release_gpu(&progress[blockIdx.x], (unsigned)(l * nt + q + 1));
+                }
             }
         }
         __syncwarp();
