@@ -966,6 +966,19 @@ uint32_t* mg_host_bits(mg_engine* e) {
     return out;
 }
 
+void* mg_host_alloc(size_t bytes) {
+    void* p = nullptr;
+    if (bytes == 0 || cudaMallocHost(&p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return p;
+}
+
+void mg_host_free(void* p) {
+    if (p != nullptr) cudaFreeHost(p);
+}
+
 int mg_max_batch(const mg_engine* e) { return e ? e->max_batch : 0; }
 
 int mg_launch_conv(mg_engine* e, int n, int layer, int reps) {

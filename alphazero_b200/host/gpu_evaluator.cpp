@@ -2,6 +2,8 @@
 
 #include "cuda_engine.h"
 
+#include "../../include/minigo_cuda.h"
+
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -20,6 +22,22 @@ GpuEvaluator::GpuEvaluator(InferenceEngine* engine, int max_batch_size)
     completer_ = std::thread(&GpuEvaluator::completion_loop, this);
 }
 
+void GpuEvaluator::reserve(Slot& slot, size_t n, size_t actions) {
+    if (n <= slot.capacity) return;
+    mg_host_free(slot.policy);
+    mg_host_free(slot.value);
+    slot.policy = static_cast<float*>(mg_host_alloc(n * actions * sizeof(float)));
+    slot.value = static_cast<float*>(mg_host_alloc(n * sizeof(float)));
+    if (slot.policy == nullptr || slot.value == nullptr) {
+        mg_host_free(slot.policy);
+        mg_host_free(slot.value);
+        slot.policy = slot.value = nullptr;
+        slot.capacity = 0;
+        throw std::runtime_error("page-locked result buffers could not be allocated");
+    }
+    slot.capacity = n;
+}
+
 GpuEvaluator::~GpuEvaluator() {
     {
         std::lock_guard<std::mutex> lock(mu_);
@@ -28,6 +46,10 @@ GpuEvaluator::~GpuEvaluator() {
     cv_.notify_all();
     server_.join();  // drains the queue, then tells the completion thread
     completer_.join();
+    for (Slot& s : slots_) {
+        mg_host_free(s.policy);
+        mg_host_free(s.value);
+    }
 }
 
 BatchEvaluator::Result GpuEvaluator::take_result(NNResultBuf& buf) {
@@ -147,12 +169,11 @@ void GpuEvaluator::run_batch(Slot& slot) {
         const int size = batch[0].buf->state_size;
         bool packed = size == cuda_->input_channels * cuda_->board_size * cuda_->board_size;
         for (const auto& p : batch) packed &= p.bits != nullptr && p.buf->state_size == size;
-        slot.policy.resize((size_t)n * a);
-        slot.value.resize(n);
+        reserve(slot, (size_t)std::max(n, max_batch_), (size_t)a);
         if (packed) {
             bit_ptrs_.resize(n);
             for (int i = 0; i < n; ++i) bit_ptrs_[i] = batch[i].bits;
-            cuda_->predict_bits(bit_ptrs_.data(), n, slot.policy.data(), slot.value.data());
+            cuda_->predict_bits(bit_ptrs_.data(), n, slot.policy, slot.value);
         } else {
             // Mixed batch: fp32 planes for all; packed-only requests
             // (evaluate_packed) are unpacked first.
@@ -169,7 +190,7 @@ void GpuEvaluator::run_batch(Slot& slot) {
                 for (int j = 0; j < size; ++j) dst[j] = (float)((batch[i].bits[j >> 5] >> (j & 31)) & 1u);
                 ptrs_[i] = dst;
             }
-            cuda_->predict_raw(ptrs_.data(), n, size, slot.policy.data(), slot.value.data());
+            cuda_->predict_raw(ptrs_.data(), n, size, slot.policy, slot.value);
         }
     } else {
         std::vector<std::vector<float>> states;
@@ -191,7 +212,7 @@ void GpuEvaluator::hand_back(Slot& slot) {
         NNResultBuf* buf = slot.batch[i].buf;
         std::lock_guard<std::mutex> lock(buf->mu);
         if (cuda_ != nullptr) {
-            buf->policy.assign(slot.policy.begin() + i * a, slot.policy.begin() + (i + 1) * a);
+            buf->policy.assign(slot.policy + i * a, slot.policy + (i + 1) * a);
             buf->value = slot.value[i];
         } else {
             buf->policy = std::move(slot.results[i].first);

@@ -86,10 +86,15 @@ private:
     // One batch between the server and the completion thread.
     struct Slot {
         std::vector<Pending> batch;
-        std::vector<float> policy, value;  // CudaEngine results, flat
+        // CudaEngine results, flat, in page-locked memory (mg_host_alloc)
+        // so that the engine's result copies are direct DMA; grown on demand.
+        float* policy = nullptr;
+        float* value = nullptr;
+        size_t capacity = 0;               // positions policy / value hold
         std::vector<Result> results;       // other engines' results
         bool busy = false;                 // posted, not yet handed back
     };
+    static void reserve(Slot& slot, size_t n, size_t actions);
     void server_loop();
     void completion_loop();
     void run_batch(Slot& slot);

@@ -135,6 +135,14 @@ float* mg_host_input(mg_engine* e);
  * counterpart (the reference ships fp32 planes). */
 uint32_t* mg_host_bits(mg_engine* e);
 
+/* Page-locked host memory of `bytes` bytes, for callers that keep their own
+ * input or output buffers (a batching server's result slots): copies to and
+ * from it are direct DMA instead of a staged copy through pageable memory.
+ * NULL if the allocation fails.  Free with mg_host_free.  No reference
+ * counterpart. */
+void* mg_host_alloc(size_t bytes);
+void mg_host_free(void* p);
+
 /* Current max batch (mg_set_max_batch). */
 int mg_max_batch(const mg_engine* e);
 
