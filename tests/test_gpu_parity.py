@@ -82,6 +82,22 @@ def test_full_size_batches(gpu_engine_factory, board, filters, blocks, n, max_mo
     assert np.array_equal(l2, l[perm]) and np.array_equal(v2, v[perm])
 
 
+def test_b20c256_fp32_verification_pass_on_64_positions(gpu_engine_factory):
+    """The 19x19 20-block 256-filter network's fp32 verification pass: 64
+    seeded random-playout positions, every row against the oracle, fp32 mode
+    at 1e-4 and the bf16 default at 2e-2 on the same batch."""
+    sd = weights.make_state_dict(19, 256, 20, seed=13, variant="perturbed")
+    x = host_lib.random_positions(19, 64, 77, 250)
+    _, ov, ol = oracle.EigenOracle(sd).predict_batch(x, oracle.CANONICAL,
+                                                     threads=min(32, os.cpu_count() or 1))
+    for precision in ("fp32", "bf16"):
+        e = gpu_engine_factory(sd, precision, max_batch=64)
+        p, v, l = e.forward(x)
+        assert np.abs(p.sum(1) - 1).max() < 1e-5
+        assert np.abs(l - ol).max() < TOL[precision], (precision, float(np.abs(l - ol).max()))
+        assert np.abs(v - ov).max() < TOL[precision], (precision, float(np.abs(v - ov).max()))
+
+
 def test_ragged_and_chunked_batches(gpu_engine_factory):
     z, sd = load_golden("b19c128x10_pert")
     e = gpu_engine_factory(sd, "bf16", max_batch=64)
