@@ -161,6 +161,23 @@ template <>
 __device__ __forceinline__ float from16<true>(uint16_t h) {
     return __half2float(__ushort_as_half(h));
 }
+// Two values rounded in one conversion; the first in the low half.
+template <bool FP16>
+__device__ __forceinline__ uint32_t to16x2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t to16x2<false>(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t to16x2<true>(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t lo_bits2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
 __device__ __forceinline__ float lo_value(uint16_t l) { return __half2float(__ushort_as_half(l)); }
 __device__ __forceinline__ uint16_t lo_bits(float r) { return __half_as_ushort(__float2half_rn(r)); }
 
@@ -340,12 +357,14 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
                 const int nrow = min(kChunk, G.m_total - px0);
                 uint32_t lw[8];
 #pragma unroll
-                for (int j = 0; j < kChunk; ++j) {
-                    const uint16_t h = to16<FP16>(f[j]);
-                    if (j < nrow) oh[j * kCo] = h;
+                for (int j = 0; j < kChunk; j += 2) {
+                    // two pixels per conversion: hi pair, then lo pair
+                    const uint32_t hp = to16x2<FP16>(f[j], f[j + 1]);
+                    const uint16_t h0 = (uint16_t)(hp & 0xffffu), h1 = (uint16_t)(hp >> 16);
+                    if (j < nrow) oh[j * kCo] = h0;
+                    if (j + 1 < nrow) oh[(j + 1) * kCo] = h1;
                     // rows past the end (f = 0) fill the last block
-                    const uint32_t lb = lo_bits(f[j] - from16<FP16>(h));
-                    lw[j >> 1] = (j & 1) ? (lw[j >> 1] | (lb << 16)) : lb;
+                    lw[j >> 1] = lo_bits2(f[j] - from16<FP16>(h0), f[j + 1] - from16<FP16>(h1));
                 }
                 if (has_lo) {
                     uint4* ol = reinterpret_cast<uint4*>(out_lo + lo_block(px0, co));
