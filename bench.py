@@ -466,12 +466,12 @@ def run_selfplay_binary(exe, model, wl, args, gpus, search=None):
     return json.loads(r.stdout.strip().splitlines()[-1])
 
 
-def selfplay_model(wl):
+def selfplay_model(wl, tmp):
+    """Writes the workload's seeded network as ONNX into directory tmp."""
     from alphazero_b200 import weights
 
     board, filters, blocks = SELFPLAY_WORKLOADS[wl][:3]
     sd = weights.make_state_dict(board, filters, blocks, seed=0, variant="init")
-    tmp = tempfile.mkdtemp(prefix="mgb_selfplay_")
     return weights.write_onnx(os.path.join(tmp, "model.onnx"), sd)
 
 
@@ -480,7 +480,8 @@ def oracle_selfplay(wl, args):
     exe = os.path.join(ROOT, "oracle", "_ref", "selfplay_oracle")
     if not os.path.exists(exe):
         return None, "oracle/_ref/selfplay_oracle was not built (no reference tree at build time)"
-    out = run_selfplay_binary(exe, selfplay_model(wl), wl, args, 0)
+    with tempfile.TemporaryDirectory(prefix="mgb_selfplay_") as tmp:
+        out = run_selfplay_binary(exe, selfplay_model(wl, tmp), wl, args, 0)
     return out, None
 
 
@@ -518,8 +519,9 @@ def run_selfplay(args, wl):
                                  "is needed at build time")
             gpus = max(args.gpus, world)
             with ClockSampler(0) as clocks:
-                out = run_selfplay_binary(build.SELFPLAY_BIN, selfplay_model(wl), wl, args, gpus,
-                                          search=selfplay_search(wl))
+                with tempfile.TemporaryDirectory(prefix="mgb_selfplay_") as tmp:
+                    out = run_selfplay_binary(build.SELFPLAY_BIN, selfplay_model(wl, tmp), wl, args,
+                                              gpus, search=selfplay_search(wl))
             base = None
             if gpus == 1 and not args.no_cpu_baseline:
                 base_out, _ = oracle_selfplay(wl, args)
