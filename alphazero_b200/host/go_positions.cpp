@@ -1,9 +1,55 @@
 #include "go_positions.h"
 
+#include <array>
 #include <cstring>
 #include <random>
+#if defined(__SSE2__)
+#include <emmintrin.h>
+#endif
 
 namespace mgb {
+
+namespace {
+// Orthogonal neighbours of every point, per board size (built once).
+struct NeighbourTable {
+    int8_t count[kMaxBoard * kMaxBoard];
+    int16_t at[kMaxBoard * kMaxBoard][4];
+};
+
+const NeighbourTable& neighbour_table(int n) {
+    static const std::array<NeighbourTable, kMaxBoard + 1> tables = [] {
+        std::array<NeighbourTable, kMaxBoard + 1> t{};
+        for (int b = 1; b <= kMaxBoard; ++b)
+            for (int p = 0; p < b * b; ++p) {
+                const int r = p / b, c = p % b;
+                int k = 0;
+                if (r > 0) t[b].at[p][k++] = (int16_t)(p - b);
+                if (r < b - 1) t[b].at[p][k++] = (int16_t)(p + b);
+                if (c > 0) t[b].at[p][k++] = (int16_t)(p - 1);
+                if (c < b - 1) t[b].at[p][k++] = (int16_t)(p + 1);
+                t[b].count[p] = (int8_t)k;
+            }
+        return t;
+    }();
+    return tables[n];
+}
+
+// ORs the low `nbits` bits of src (64-bit words, bit i of the sequence at
+// bit i % 64 of word i / 64) into words[] starting at bit `dest`.
+void or_bits(uint32_t* words, int nw, int dest, const uint64_t* src, int nbits) {
+    for (int k = 0; k * 64 < nbits; ++k) {
+        uint64_t v = src[k];
+        const int left = nbits - k * 64;
+        if (left < 64) v &= (uint64_t(1) << left) - 1;
+        if (v == 0) continue;
+        const int bit = dest + k * 64, off = bit >> 5, sh = bit & 31;
+        const uint64_t lo = v << sh;
+        words[off] |= (uint32_t)lo;
+        if (off + 1 < nw) words[off + 1] |= (uint32_t)(lo >> 32);
+        if (sh != 0 && off + 2 < nw) words[off + 2] |= (uint32_t)(v >> (64 - sh));
+    }
+}
+}  // namespace
 
 GoPosition::GoPosition(int board_size, float komi) : n_(board_size), komi_(komi) {
     reset();
@@ -25,11 +71,9 @@ void GoPosition::reset() {
 }
 
 int GoPosition::neighbours(int p, int* out) const {
-    int r = p / n_, c = p % n_, k = 0;
-    if (r > 0) out[k++] = p - n_;
-    if (r < n_ - 1) out[k++] = p + n_;
-    if (c > 0) out[k++] = p - 1;
-    if (c < n_ - 1) out[k++] = p + 1;
+    const NeighbourTable& t = neighbour_table(n_);
+    const int k = t.count[p];
+    for (int i = 0; i < k; ++i) out[i] = t.at[p][i];
     return k;
 }
 
@@ -150,13 +194,29 @@ void GoPosition::encode_bits(uint32_t* words) const {
     std::memset(words, 0, sizeof(uint32_t) * (size_t)nw);
     auto set = [&](int j) { words[j >> 5] |= 1u << (j & 31); };
     const int8_t us = (int8_t)to_move_, them = (int8_t)(3 - to_move_);
+    constexpr int kW64 = (kMaxBoard * kMaxBoard + 63) / 64;
     for (int i = 0; i < hist_len_; ++i) {
         const int8_t* snap = hist_[(hist_top_ - i + kHistory) % kHistory];
-        const int mine = i * nn, theirs = (kHistory + i) * nn;
-        for (int q = 0; q < nn; ++q) {
-            if (snap[q] == us) set(mine + q);
-            else if (snap[q] == them) set(theirs + q);
+        // the snapshot's two planes as bit strings, then placed at their
+        // plane offsets (which are not word-aligned)
+        uint64_t mine[kW64] = {}, theirs[kW64] = {};
+        int q = 0;
+#if defined(__SSE2__)
+        // 16 points per compare; q is a multiple of 16, so a group's 16 bits
+        // never straddle two 64-bit words
+        const __m128i vus = _mm_set1_epi8(us), vthem = _mm_set1_epi8(them);
+        for (; q + 16 <= nn; q += 16) {
+            const __m128i x = _mm_loadu_si128(reinterpret_cast<const __m128i*>(snap + q));
+            mine[q >> 6] |= (uint64_t)(uint32_t)_mm_movemask_epi8(_mm_cmpeq_epi8(x, vus)) << (q & 63);
+            theirs[q >> 6] |= (uint64_t)(uint32_t)_mm_movemask_epi8(_mm_cmpeq_epi8(x, vthem)) << (q & 63);
         }
+#endif
+        for (; q < nn; ++q) {
+            mine[q >> 6] |= (uint64_t)(snap[q] == us) << (q & 63);
+            theirs[q >> 6] |= (uint64_t)(snap[q] == them) << (q & 63);
+        }
+        or_bits(words, nw, i * nn, mine, nn);
+        or_bits(words, nw, (kHistory + i) * nn, theirs, nn);
     }
     if (to_move_ == 1) {
         // plane 16: bits [16 * nn, 17 * nn) all set
@@ -170,7 +230,23 @@ void GoPosition::encode_bits(uint32_t* words) const {
 
 void GoPosition::legal_mask(uint8_t* out) const {
     const int nn = n_ * n_;
-    for (int a = 0; a <= nn; ++a) out[a] = legal(a) ? 1 : 0;
+    if (over_) {
+        std::memset(out, 0, (size_t)nn + 1);
+        return;
+    }
+    // legal()'s fast path inline: an empty point with an empty neighbour is
+    // legal; only points whose neighbours are all occupied take the full test.
+    const NeighbourTable& t = neighbour_table(n_);
+    for (int a = 0; a < nn; ++a) {
+        if (cells_[a] != 0) {
+            out[a] = 0;
+            continue;
+        }
+        bool open = false;
+        for (int i = 0; i < t.count[a]; ++i) open |= cells_[t.at[a][i]] == 0;
+        out[a] = (open || legal(a)) ? 1 : 0;
+    }
+    out[nn] = 1;
 }
 
 void GoPosition::decide_winner() {
