@@ -62,3 +62,20 @@ def test_single_process_needs_no_process_group():
         assert bench.aggregate_rate(1, 512, 10, 2.0) == 2560.0
     finally:
         os.environ.update(env)
+
+
+def test_reference_arm_prints_one_json_line():
+    """bench.py --impl reference (the CPU arm the driver runs next to the
+    GPU arm) prints one JSON line with the GPU arm's metric and unit."""
+    import json
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference",
+                        "--workload", "b9c64x6_bs16", "--steps", "2", "--warmup", "3"],
+                       capture_output=True, text=True, timeout=600, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unit"] == "positions/s" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["e2e"]["value"] == line["value"]
