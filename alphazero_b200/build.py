@@ -91,9 +91,11 @@ SELFPLAY_HEADERS = EVAL_HEADERS + [os.path.join(HOST, h) for h in (
     "selfplay_loop.h", "selfplay_window.h", "fast_selfplay.h", "fast_search.h", "go_positions.h",
     "packed_evaluator.h", "selfplay_records.h")]
 # The reference tree the self-play harness compiles src/mcts.cpp and
-# src/game.cpp from (read in place, never copied).
+# src/game.cpp from (read in place, never copied).  The one setting for its
+# location: the MGB_REFERENCE_TREE environment variable, with this default;
+# the oracle's build and the fixture generator read it from here.
 REFERENCE_TREE = os.environ.get("MGB_REFERENCE_TREE", "/root/reference")
-REFERENCE_SOURCES = ["src/mcts.cpp", "src/game.cpp"]
+REFERENCE_SOURCES = ["src/mcts.cpp", "src/game.cpp", "src/onnx_loader.cpp"]
 
 CUDA_LIB = os.path.join(LIB, "libminigo_cuda.so")
 HOST_LIB = os.path.join(LIB, "libminigo_host.so")

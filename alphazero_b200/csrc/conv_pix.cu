@@ -861,20 +861,19 @@ cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16
 }
 
 // Whether launch_trunk_pix runs its layers as one persistent launch (at
-// least kTrunkMinTiles tiles per CTA) or as one launch per layer.
-bool trunk_in_one_launch(int m_total, int max_npx, int grid_limit) {
-    constexpr int kTrunkMinTiles = 3;
+// least min_tiles tiles per CTA) or as one launch per layer.
+bool trunk_in_one_launch(int m_total, int max_npx, int grid_limit, int min_tiles) {
     const int units = (m_total + 15) / 16;
     const int grid = units < grid_limit ? (units < 1 ? 1 : units) : grid_limit;
     const int span = (((m_total + grid - 1) / grid) + 15) / 16 * 16;
-    return (span + max_npx - 1) / max_npx >= kTrunkMinTiles;
+    return (span + max_npx - 1) / max_npx >= min_tiles;
 }
 
 }  // namespace
 
-int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit) {
+int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit, int min_tiles) {
     if (n <= 0) return 0;
-    if (!trunk_in_one_launch(m_total, max_npx, grid_limit)) return n;
+    if (!trunk_in_one_launch(m_total, max_npx, grid_limit, min_tiles)) return n;
     return (n + kMaxLayers - 1) / kMaxLayers;
 }
 
@@ -901,13 +900,13 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
 
 cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool fp16,
                              int grid_limit, unsigned* progress, cudaStream_t stream,
-                             int withhold_cta) {
+                             int withhold_cta, int min_tiles) {
     // With few tiles per CTA a tile of the next layer depends on most of the
     // CTA's range and its neighbours' of the layer before, so one launch per
     // layer (programmatic dependent launches) is faster than the cross-CTA
     // handoff (measured: 19x19 batch 64 and 9x9 batch 256, one or two tiles
     // per CTA).
-    if (n > 0 && !trunk_in_one_launch(layers[0].m_total, max_npx, grid_limit)) {
+    if (n > 0 && !trunk_in_one_launch(layers[0].m_total, max_npx, grid_limit, min_tiles)) {
         for (int l = 0; l < n; ++l) {
             cudaError_t e = launch_layers(layers + l, 1, max_npx, fp16, grid_limit, nullptr, stream);
             if (e != cudaSuccess) return e;

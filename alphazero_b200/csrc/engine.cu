@@ -82,6 +82,7 @@ struct mg_engine {
     int pix_mode = 1;      // 1: pixels-on-N kernel for 128-channel layers
     int pix_npx = 0;       // pixels per tile override (0 = heuristic)
     int pix_trunk = 1;     // 1: all 128-channel trunk layers as one persistent launch
+    int pix_trunk_min_tiles = 3;  // ... when every CTA gets at least this many tiles
     int withhold_cta = -1;  // test hook (MG_TEST_WITHHOLD_PROGRESS): see launch_trunk_pix
     bool use_graphs = true;
     cudaStream_t stream = nullptr;
@@ -454,54 +455,67 @@ struct mg_engine {
         }
     }
 
+    // The buffers a forward pass runs on: the engine's own (allocated for
+    // max_batch positions) or a caller-provided set of the same roles.
+    struct LayerBuffers {
+        const void* stage;  // staged input rows
+        float* x32;         // fp32 residual stream (the lo plane on the 16-bit paths)
+        void* x16;          // 16-bit residual operand (hi plane)
+        void* t;            // block-internal activation
+        float* feat;        // head features
+        int* err;           // device status word
+    };
+    LayerBuffers own_buffers() const { return {d_stage, d_x, d_x16, d_t, d_feat, d_err}; }
+
     ConvLayer layer_desc(int li, int bucket) const {
+        return layer_desc(li, bucket * g.is, fused_heads(bucket), own_buffers());
+    }
+
+    // Layer li over m_total framed rows on buffer set b.
+    ConvLayer layer_desc(int li, int m_total, bool fused, const LayerBuffers& b) const {
         ConvLayer L{};
-        L.m_total = bucket * g.is;
+        L.m_total = m_total;
         L.cin = wcin[li];
         L.cout = cpad;
         L.g = g;
         L.bias = d_bias[li];
-        L.err = d_err;
+        L.err = b.err;
         const bool f32 = precision == MG_PREC_FP32;
         L.weight = f32 ? (const void*)d_w32[li] : (const void*)d_w16[li];
         if (!f32) {
-            wire_hilo_layer(L, li, d_stage, d_x16, reinterpret_cast<uint16_t*>(d_x), d_t);
+            wire_hilo_layer(L, li, b.stage, b.x16, reinterpret_cast<uint16_t*>(b.x32), b.t);
         } else if (li == 0) {  // input conv: staged planes -> x
-            L.in = d_stage;
-            L.out32 = d_x;
-            L.out16 = f32 ? nullptr : d_x16;
+            L.in = b.stage;
+            L.out32 = b.x32;
         } else if (li % 2 == 1) {  // conv1 of a block: x -> t
-            L.in = f32 ? (const void*)d_x : (const void*)d_x16;
-            if (f32) L.out32 = reinterpret_cast<float*>(d_t);
-            else L.out16 = d_t;
+            L.in = b.x32;
+            L.out32 = reinterpret_cast<float*>(b.t);
         } else {  // conv2: t (+ x) -> x, in place over the residual rows
-            L.in = d_t;
-            L.res32 = d_x;
-            L.out32 = d_x;
-            L.out16 = f32 ? nullptr : d_x16;
+            L.in = b.t;
+            L.res32 = b.x32;
+            L.out32 = b.x32;
         }
-        if (li == n_convs - 1 && fused_heads(bucket)) {
+        if (li == n_convs - 1 && fused) {
             // The trunk output is consumed only by the heads.
             L.out32 = nullptr;
             L.out16 = nullptr;
             L.out_lo = nullptr;
             L.head_w = d_head_w;
             L.head_b = d_head_b;
-            L.feat = d_feat;
+            L.feat = b.feat;
         }
         return L;
     }
 
-    void launch_conv(int li, int bucket) {
-        ConvLayer L = layer_desc(li, bucket);
+    // One convolution layer as its own launch on `st`.
+    void launch_layer(const ConvLayer& L, int li, cudaStream_t st) const {
         if (precision == MG_PREC_FP32) {
-            ck(launch_conv_simt(L, stream), "conv3x3_simt launch");
+            ck(launch_conv_simt(L, st), "conv3x3_simt launch");
             return;
         }
         const bool fp16 = precision == MG_PREC_FP16;
         if (use_pix()) {
-            ck(launch_conv_pix(L, choose_npx(L.m_total), fp16, num_sms, stream),
-               "conv3x3_pix launch");
+            ck(launch_conv_pix(L, choose_npx(L.m_total), fp16, num_sms, st), "conv3x3_pix launch");
             return;
         }
         // the head-projection layer's tile spans every channel
@@ -509,7 +523,17 @@ struct mg_engine {
         CUtensorMap ta, tb;
         const char* why = "";
         if (!make_conv_tensor_maps(L, bn, fp16, &ta, &tb, &why)) throw std::runtime_error(why);
-        ck(launch_conv_tc(L, ta, tb, bn, fp16, num_sms, stream), "conv3x3_tc launch");
+        ck(launch_conv_tc(L, ta, tb, bn, fp16, num_sms, st), "conv3x3_tc launch");
+    }
+
+    void launch_conv(int li, int bucket) { launch_layer(layer_desc(li, bucket), li, stream); }
+
+    // The 16-bit modes' limit on the network width (one tensor-core tile
+    // spans every output channel of the head-projection layer).
+    void check_width() const {
+        if (precision != MG_PREC_FP32 && cpad > 256)
+            throw std::runtime_error(
+                "the bf16/fp16 modes support networks of up to 256 filters; use fp32");
     }
 
     // All trunk convolutions of a forward pass (the persistent trunk kernel
@@ -520,7 +544,7 @@ struct mg_engine {
             for (int li = 0; li < n_convs; ++li) layers[li] = layer_desc(li, bucket);
             ck(launch_trunk_pix(layers.data(), n_convs, choose_npx(bucket * g.is),
                                 precision == MG_PREC_FP16, num_sms, d_progress, stream,
-                                withhold_cta),
+                                withhold_cta, pix_trunk_min_tiles),
                "conv3x3_pix trunk launch");
         } else {
             for (int li = 0; li < n_convs; ++li) launch_conv(li, bucket);
@@ -529,14 +553,13 @@ struct mg_engine {
 
     int trunk_launches(int bucket) const {
         if (use_pix() && pix_trunk)
-            return trunk_pix_launches(bucket * g.is, n_convs, choose_npx(bucket * g.is), num_sms);
+            return trunk_pix_launches(bucket * g.is, n_convs, choose_npx(bucket * g.is), num_sms,
+                                      pix_trunk_min_tiles);
         return n_convs;
     }
 
     void enqueue_trunk_heads(int bucket) {
-        if (precision != MG_PREC_FP32 && cpad > 256)
-            throw std::runtime_error(
-                "the bf16/fp16 modes support networks of up to 256 filters; use fp32");
+        check_width();
         enqueue_trunk(bucket);
         if (!fused_heads(bucket))
             ck(launch_head_projection(d_x, bucket, cpad, g, d_head_w, d_head_b, d_feat, stream),
@@ -681,6 +704,8 @@ mg_engine* mg_create(int device, int flags) {
     if (const char* s = std::getenv("MG_PIX")) e->pix_mode = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_NPX")) e->pix_npx = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_TRUNK")) e->pix_trunk = std::atoi(s);
+    if (const char* s = std::getenv("MG_PIX_TRUNK_MIN_TILES"))
+        e->pix_trunk_min_tiles = std::max(1, std::atoi(s));
     if (const char* s = std::getenv("MG_TEST_WITHHOLD_PROGRESS")) e->withhold_cta = std::atoi(s);
     return e.release();
 }
@@ -1120,6 +1145,7 @@ extern "C" int mg_forward_device_noalloc(mg_engine* e, const float* d_states, in
         const bool f32 = e->precision == MG_PREC_FP32;
         if (f32 ? e->d_w32.size() != (size_t)e->n_convs : e->w16_prec != e->precision)
             throw std::logic_error("weights for the current precision are not on the device");
+        e->check_width();  // before anything is enqueued
         // Largest batch that fits the arena, for the error message.
         int cap = 0;
         while (noalloc_layout(e, cap + 1, nullptr, nullptr) <= kNoAllocArenaBytes) ++cap;
@@ -1139,56 +1165,9 @@ extern "C" int mg_forward_device_noalloc(mg_engine* e, const float* d_states, in
                               (e->flags & MG_FLAG_EIGEN_COMPAT) != 0, e->act_type(), b.stage, st),
            "stage launch");
         const bool fused = e->fused_heads(n);
-        for (int li = 0; li < e->n_convs; ++li) {
-            // The same wiring as the engine's own forward, on arena buffers.
-            ConvLayer L{};
-            L.m_total = n * e->g.is;
-            L.cin = e->wcin[li];
-            L.cout = e->cpad;
-            L.g = e->g;
-            L.bias = e->d_bias[li];
-            L.err = b.err;
-            L.weight = f32 ? (const void*)e->d_w32[li] : (const void*)e->d_w16[li];
-            if (!f32) {
-                e->wire_hilo_layer(L, li, b.stage, b.x16, reinterpret_cast<uint16_t*>(b.x32), b.t);
-            } else if (li == 0) {
-                L.in = b.stage;
-                L.out32 = b.x32;
-                L.out16 = f32 ? nullptr : b.x16;
-            } else if (li % 2 == 1) {
-                L.in = f32 ? (const void*)b.x32 : (const void*)b.x16;
-                if (f32) L.out32 = reinterpret_cast<float*>(b.t);
-                else L.out16 = b.t;
-            } else {
-                L.in = b.t;
-                L.res32 = b.x32;
-                L.out32 = b.x32;
-                L.out16 = f32 ? nullptr : b.x16;
-            }
-            if (li == e->n_convs - 1 && fused) {
-                L.out32 = nullptr;
-                L.out16 = nullptr;
-                L.out_lo = nullptr;
-                L.head_w = e->d_head_w;
-                L.head_b = e->d_head_b;
-                L.feat = b.feat;
-            }
-            if (f32) {
-                ck(launch_conv_simt(L, st), "conv3x3_simt launch");
-            } else if (e->use_pix()) {
-                ck(launch_conv_pix(L, e->choose_npx(L.m_total), e->precision == MG_PREC_FP16,
-                                   e->num_sms, st),
-                   "conv3x3_pix launch");
-            } else {
-                const bool fp16 = e->precision == MG_PREC_FP16;
-                const int bn = li == e->n_convs - 1 ? e->cpad : e->choose_bn(L.m_total);
-                CUtensorMap ta, tb;
-                const char* why = "";
-                if (!make_conv_tensor_maps(L, bn, fp16, &ta, &tb, &why))
-                    throw std::runtime_error(why);
-                ck(launch_conv_tc(L, ta, tb, bn, fp16, e->num_sms, st), "conv3x3_tc launch");
-            }
-        }
+        const mg_engine::LayerBuffers lb{b.stage, b.x32, b.x16, b.t, b.feat, b.err};
+        for (int li = 0; li < e->n_convs; ++li)
+            e->launch_layer(e->layer_desc(li, n * e->g.is, fused, lb), li, st);
         if (!fused)
             ck(launch_head_projection(b.x32, n, e->cpad, e->g, e->d_head_w, e->d_head_b, b.feat, st),
                "head projection launch");

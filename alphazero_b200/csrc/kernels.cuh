@@ -109,15 +109,16 @@ cudaError_t configure_conv_pix();
 // next layer as soon as the tiles of the previous layer that it reads are
 // stored.  Layers 1..n-1 must have cin 128 and their weights back to back
 // from layers[1].weight; progress points at grid_limit counters of scratch.
-// When CTAs get fewer than 3 tiles the layers go out as one launch each.
+// When CTAs get fewer than min_tiles tiles the layers go out as one launch
+// each.
 // withhold_cta >= 0 is a test hook for the failure path: that CTA never
 // publishes its progress, so the CTAs waiting on it (itself included) give up
 // after the bounded wait and report kErrWaitDep in the status word.
 cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool fp16,
                              int grid_limit, unsigned* progress, cudaStream_t stream,
-                             int withhold_cta = -1);
+                             int withhold_cta = -1, int min_tiles = 3);
 // Number of kernel launches launch_trunk_pix makes for n layers of m_total rows.
-int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit);
+int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit, int min_tiles = 3);
 
 // fp32 SIMT path used by the fp32 verification mode.
 cudaError_t launch_conv_simt(const ConvLayer& layer, cudaStream_t stream);

@@ -9,6 +9,9 @@
 #endif
 #include <cstring>
 #include <stdexcept>
+#if defined(MGB_USE_REFERENCE_HEADERS)
+#include "onnx_loader.h"
+#endif
 
 namespace minigo {
 
@@ -35,7 +38,32 @@ void CudaEngine::count_launches(int n) {
 }
 
 void CudaEngine::load_model(const std::string& model_path) {
+#if defined(MGB_USE_REFERENCE_HEADERS)
+    // Built inside the reference tree: the model goes through the
+    // reference's own loader, onnx_parser::parse_onnx_file
+    // (src/onnx_loader.cpp:183), as its Eigen / OpenCL / Metal engines load it
+    // (it throws "Cannot open model file: ..."), and the parsed initializers
+    // go to the device through mg_load_weights.  Non-FLOAT tensors
+    // (num_batches_tracked) are passed without values, as mg_load_onnx does.
+    const std::vector<onnx_parser::OnnxTensor> parsed = onnx_parser::parse_onnx_file(model_path);
+    std::vector<std::vector<float>> values(parsed.size());
+    std::vector<mg_tensor> tensors(parsed.size());
+    for (size_t i = 0; i < parsed.size(); ++i) {
+        const onnx_parser::OnnxTensor& t = parsed[i];
+        if (t.data_type == 0 || t.data_type == 1) values[i] = t.get_floats();
+        if (!values[i].empty() && (int64_t)values[i].size() != t.total_elements())
+            throw std::runtime_error("tensor " + t.name + " holds " + std::to_string(values[i].size()) +
+                                     " values for " + std::to_string(t.total_elements()) + " elements");
+        tensors[i].name = t.name.c_str();
+        tensors[i].dims = t.dims.data();
+        tensors[i].ndims = (int)t.dims.size();
+        tensors[i].data = values[i].empty() ? nullptr : values[i].data();
+    }
+    if (mg_load_weights(h_, tensors.data(), (int)tensors.size()) != MG_OK)
+        throw std::runtime_error(mg_last_error(h_));
+#else
     if (mg_load_onnx(h_, model_path.c_str()) != MG_OK) throw std::runtime_error(mg_last_error(h_));
+#endif
     check(mg_get_info(h_, &board_size, &input_channels, &num_filters, &num_res_blocks, &action_size_),
           "mg_get_info");
 }

@@ -1,8 +1,8 @@
 // The reference's engine and evaluator interfaces, as the CUDA backend's C++
 // host code sees them.
 //
-// Built inside the reference tree (-DMGB_USE_REFERENCE_HEADERS, see
-// INTEGRATION.md) the reference's own headers are used.  Built standalone
+// Built inside the reference tree (-DMGB_USE_REFERENCE_HEADERS) the
+// reference's own headers are used.  Built standalone
 // (this repository's tests) the same declarations are restated here; they
 // must stay layout- and signature-identical to
 //   include/inference_engine.h:14-41   InferenceEngine

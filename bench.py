@@ -21,7 +21,18 @@ JSON line.  Numbers:
              algorithmic FLOPs per launch / average launch time, against the
              measured dense bf16 peak;
   cpu_baseline  the oracle (C restatement of src/eigen_engine.cpp) on the
-             host cores over a bounded sample (rank 0, N = 1 only).
+             host cores over a bounded sample (rank 0, N = 1 only), and
+             torch_cpu: a torch restatement of the reference network
+             (scripts/model.py) on all host cores over a bounded sample;
+  configs    (N = 1, default workload only) the same value / e2e / roofline
+             for the other predict_batch configurations: 19x19 b20c256
+             batch 1024 (the configuration the 60% tensor-peak target is
+             quoted on), 9x9 b10c128 batch 256 and 9x9 b6c64 batch 16;
+  selfplay   (every N, default workload only) end-to-end self-play MCTS
+             visits/s over all N GPUs after the per-rank engines are closed:
+             rank 0 runs alphazero_b200/lib/selfplay_cuda with FastSearch and
+             with the reference's own search (the selfplay_b19c128x10*
+             workloads below) for a bounded window each.
 --impl reference times that CPU implementation alone as the reference arm.
 
 selfplay_b19c128x10 is end-to-end self-play instead: the reference's own
@@ -173,9 +184,47 @@ class ClockSampler:
                 "samples": len(self.rows)}
 
 
+def torch_cpu_baseline(sd, x, target_s=6.0):
+    """A torch restatement of the reference network (scripts/model.py,
+    oracle/torch_net.py) on all host cores over a bounded sample of the
+    workload, at up to the workload's batch per call."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import torch
+    from torch_net import TorchNet
+
+    threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        net = TorchNet(sd)
+        probe = min(len(x), 8)
+        net.forward(x[:probe])  # first call: thread pool and allocator warm-up
+        t0 = time.perf_counter()
+        net.forward(x[:probe])
+        per_pos = (time.perf_counter() - t0) / probe
+        sample = max(probe, min(len(x), int(target_s / max(per_pos, 1e-9))))
+        t0 = time.perf_counter()
+        net.forward(x[:sample])
+        dt = time.perf_counter() - t0
+    finally:
+        torch.set_num_threads(prev)
+    cpu = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            cpu = next((l.split(":", 1)[1].strip() for l in f if l.startswith("model name")), "")
+    except OSError:
+        pass
+    return {"value": sample / dt, "unit": "positions/s", "cores": threads, "kind": "port",
+            "cpu": cpu, "torch": torch.__version__,
+            "sample": f"{sample} positions of the same workload in one batch; torch fp32 "
+                      f"restatement of scripts/model.py (eval mode) on {threads} threads "
+                      f"({dt:.1f} s)"}
+
+
 def cpu_baseline(sd, x, target_s=12.0):
     """The oracle on all host cores over a bounded sample of the workload
-    (about target_s seconds of wall time)."""
+    (about target_s seconds of wall time), with the torch-CPU figure beside
+    it."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
@@ -189,9 +238,15 @@ def cpu_baseline(sd, x, target_s=12.0):
     t0 = time.perf_counter()
     orc.predict_batch(x[:sample], oracle.CANONICAL, threads=threads)
     dt = time.perf_counter() - t0
-    return {"value": sample / dt, "unit": "positions/s", "cores": threads, "kind": "port",
-            "sample": f"{sample} positions of the same workload; oracle C restatement of "
-                      f"src/eigen_engine.cpp on {threads} threads ({dt:.1f} s)"}
+    out = {"value": sample / dt, "unit": "positions/s", "cores": threads, "kind": "port",
+           "sample": f"{sample} positions of the same workload; oracle C restatement of "
+                     f"src/eigen_engine.cpp on {threads} threads ({dt:.1f} s)",
+           "one_core_equivalent": sample / dt / threads}
+    try:
+        out["torch_cpu"] = torch_cpu_baseline(sd, x)
+    except Exception as ex:  # reported, never fatal to the GPU line
+        out["torch_cpu"] = {"unavailable": f"{type(ex).__name__}: {ex}"}
+    return out
 
 
 def dist_setup():
@@ -254,10 +309,12 @@ def run_reference(args, wl):
     board, filters, blocks, batch, max_moves = WORKLOADS[wl]
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
-    from alphazero_b200 import host_lib, weights
+    from alphazero_b200 import weights  # seeded numpy weights (no native code)
 
     sd = weights.make_state_dict(board, filters, blocks, seed=0, variant="init")
-    x = host_lib.random_positions(board, batch, 1000, max_moves)
+    # the reference's own src/game.cpp generates the positions (bit-identical
+    # to the product's generator; the reference arm maps no product library)
+    x = oracle.ref_random_positions(board, batch, 1000, max_moves)
     threads = os.cpu_count() or 1
     orc = oracle.EigenOracle(sd)
     t0 = time.perf_counter()
@@ -302,23 +359,35 @@ def workload_config(wl):
             "parallelism": "replicas; positions sharded per GPU, no collective"}
 
 
-def run_b200(args, wl):
+def trunk_kernel_label(filters, n_convs, trunk_launches):
+    """Which kernel runs the trunk on this path, and in how many launches."""
+    if filters == 128 and trunk_launches < n_convs:
+        return (f"trunk: all {n_convs} 3x3 conv layers, conv3x3_pix_kernel, "
+                f"{trunk_launches} persistent launch{'es' if trunk_launches > 1 else ''}")
+    kern = "conv3x3_pix_kernel" if filters == 128 else "conv3x3_tc_kernel"
+    return f"trunk: all {n_convs} 3x3 conv layers, {kern}, one launch per layer"
+
+
+def measure_predict(wl, args, ranks, world, rank, local, planes_e2e=True):
+    """positions/s (device-resident and end to end) and the trunk roofline
+    of workload wl on this rank's GPU; every rank takes the same collective
+    steps.  Returns the fields of a bench line (rank 0's view)."""
     import torch
 
-    world, rank, local = dist_setup()
-    torch.cuda.set_device(local)
-    ranks = Ranks("nccl", device=torch.device("cuda", local))
     board, filters, blocks, batch, max_moves = WORKLOADS[wl]
     hw = board * board
     actions = hw + 1
+    n_convs = 1 + 2 * blocks
     from alphazero_b200 import host_lib, weights
-    from alphazero_b200.engine import CudaEngine
+    from alphazero_b200.engine import CudaEngine, pack_states
 
     sd = weights.make_state_dict(board, filters, blocks, seed=0, variant="init")
     tmp = tempfile.mkdtemp(prefix="mgb_bench_")
     model = weights.write_onnx(os.path.join(tmp, "model.onnx"), sd)
     eng = CudaEngine(local, precision="bf16", max_batch=batch)
     eng.load_model(model)
+    os.remove(model)
+    os.rmdir(tmp)
     x = host_lib.random_positions(board, batch, 1000 + rank, max_moves)
 
     stream = torch.cuda.ExternalStream(eng.stream_handle())
@@ -331,8 +400,6 @@ def run_b200(args, wl):
     def barrier():
         ranks.barrier()
         torch.cuda.synchronize()
-
-    max_over_ranks = ranks.max
 
     # ---- value: device-resident inputs, L2 flushed before each step ----
     with torch.cuda.stream(stream):
@@ -353,14 +420,13 @@ def run_b200(args, wl):
         eng.synchronize()
     barrier()
     dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    dev_ms = max_over_ranks(dev_ms)
+    dev_ms = ranks.max(dev_ms)
     value = aggregate_rate(world, batch, args.steps, dev_ms / 1e3)
-    launches = eng.launches_per_forward(batch) * args.steps
+    per_forward = eng.launches_per_forward(batch)
+    launches = per_forward * args.steps
 
     # ---- e2e: host API, pinned inputs and outputs, H2D + forward + D2H per
     # step, in the bit-packed wire format (and, for comparison, fp32 planes)
-    from alphazero_b200.engine import pack_states
-
     words = eng.words_per_position()
     bits = torch.from_numpy(pack_states(x).view(np.int32)).pin_memory().numpy().view(np.uint32)
     outs = (torch.empty((batch, actions)).pin_memory().numpy(), torch.empty((batch,)).pin_memory().numpy())
@@ -374,14 +440,16 @@ def run_b200(args, wl):
             step()
         dt = time.perf_counter() - t0
         barrier()
-        return aggregate_rate(world, batch, args.steps, max_over_ranks(dt))
+        return aggregate_rate(world, batch, args.steps, ranks.max(dt))
 
     e2e = e2e_loop(lambda: eng.forward_packed(bits, batch, out=outs))
-    xin = torch.from_numpy(x).pin_memory().numpy()
-    e2e_planes = e2e_loop(lambda: eng.forward(xin, want_logits=False))
+    e2e_planes = None
+    if planes_e2e:
+        xin = torch.from_numpy(x).pin_memory().numpy()
+        e2e_planes = e2e_loop(lambda: eng.forward(xin, want_logits=False))
 
-    # ---- roofline: the dominant kernel, the trunk (every 3x3 conv layer;
-    # one persistent launch on the 128-channel path), timed alone ----
+    # ---- roofline: the dominant kernel, the trunk (every 3x3 conv layer),
+    # timed alone on the engine's stream ----
     reps = 10
     eng.forward_device(d_x.data_ptr(), batch, d_p.data_ptr(), d_v.data_ptr(), None)
     eng.launch_trunk(batch, 2)
@@ -390,37 +458,26 @@ def run_b200(args, wl):
     eng.launch_trunk(batch, reps)
     c1.record(stream)
     eng.synchronize()
-    trunk_ms = c0.elapsed_time(c1) / reps
+    trunk_ms = ranks.max(c0.elapsed_time(c1) / reps)
+    eng.close()
+    del d_x, d_p, d_v, flush
+    torch.cuda.empty_cache()
+
     trunk_flops = float(batch) * trunk_flops_per_position(board, filters, blocks)
     peaks, peak_src = load_peaks()
     achieved = trunk_flops / (trunk_ms / 1e3) / 1e12
-    traffic = profiled_traffic(wl)
-
-    base = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        base = cpu_baseline(sd, x)
-
-    ranks.close()
-    if rank != 0:
-        return
-    line = {
-        "metric": metric_name(wl), "value": value, "unit": "positions/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic", "config": workload_config(wl),
+    trunk_launches = per_forward - 3  # staging, FC, softmax/tanh finish
+    out = {
+        "value": value, "ms_per_step": dev_ms / args.steps,
         "e2e": {"value": e2e, "unit": "positions/s",
-                "h2d_bytes_per_step": batch * words * 4,
-                "d2h_bytes_per_step": batch * (actions + 1) * 4,
+                "h2d_bytes_per_step": world * batch * words * 4,
+                "d2h_bytes_per_step": world * batch * (actions + 1) * 4,
                 "api": "mg_forward_packed (bit-packed planes, pinned host buffers)"},
-        "e2e_fp32_planes": {"value": e2e_planes, "unit": "positions/s",
-                            "h2d_bytes_per_step": batch * 17 * hw * 4,
-                            "d2h_bytes_per_step": batch * (actions + 1) * 4,
-                            "api": "mg_forward (fp32 planes, pinned input)"},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                     "traffic": traffic,
-                     "kernel": "trunk: all 3x3 conv layers (conv3x3_pix_kernel, persistent)",
+                     "traffic": profiled_traffic(wl),
+                     "kernel": trunk_kernel_label(filters, n_convs, trunk_launches),
                      "flops_per_launch": trunk_flops, "launch_ms": trunk_ms,
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops, burst)",
                      "peak_sustained": peaks["bf16_tflops_sustained"],
@@ -429,8 +486,77 @@ def run_b200(args, wl):
         "tflops_whole_forward": value * flops_per_position(board, filters, blocks) / 1e12,
         "clocks": clocks.summary(),
     }
+    if e2e_planes is not None:
+        out["e2e_fp32_planes"] = {"value": e2e_planes, "unit": "positions/s",
+                                  "h2d_bytes_per_step": world * batch * 17 * hw * 4,
+                                  "d2h_bytes_per_step": world * batch * (actions + 1) * 4,
+                                  "api": "mg_forward (fp32 planes, pinned input)"}
+    return out, sd, x
+
+
+# The other predict_batch configurations reported beside the default one.
+EXTRA_CONFIGS = ("b19c256x20_bs1024", "b9c128x10_bs256", "b9c64x6_bs16")
+
+
+def selfplay_records(world, args):
+    """Self-play visits/s over all `world` GPUs, FastSearch and the
+    reference's own search, each for a bounded window (rank 0 only)."""
+    from alphazero_b200 import build
+
+    if not os.path.exists(build.SELFPLAY_BIN):
+        return {"unavailable": "selfplay_cuda was not built (the reference tree's src/mcts.cpp is "
+                               "needed at build time)"}
+    recs = {}
+    with tempfile.TemporaryDirectory(prefix="mgb_selfplay_") as tmp:
+        model = selfplay_model("selfplay_b19c128x10", tmp)
+        for search, wl in (("fast", "selfplay_b19c128x10_fast"), ("reference", "selfplay_b19c128x10")):
+            with ClockSampler(0) as clocks:
+                out = run_selfplay_binary(build.SELFPLAY_BIN, model, wl, args, world, search=search,
+                                          window=(args.selfplay_warmup, args.selfplay_seconds))
+            out["clocks_gpu0"] = clocks.summary()
+            out["metric"] = "MCTS visits/s"
+            out["config"] = selfplay_config(wl)
+            recs[search] = out
+    return recs
+
+
+def run_b200(args, wl):
+    import torch
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    ranks = Ranks("nccl", device=torch.device("cuda", local))
+    board, filters, blocks, batch, max_moves = WORKLOADS[wl]
+
+    m, sd, x = measure_predict(wl, args, ranks, world, rank, local)
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base = cpu_baseline(sd, x)
+    configs = None
+    if world == 1 and wl == DEFAULT_WORKLOAD and not args.no_extras:
+        configs = {}
+        for cw in EXTRA_CONFIGS:
+            cm, _, _ = measure_predict(cw, args, ranks, world, rank, local, planes_e2e=False)
+            cm.update(metric=metric_name(cw), unit="positions/s", config=workload_config(cw))
+            configs[cw] = cm
+    ranks.close()
+    if rank != 0:
+        return
+    line = {
+        "metric": metric_name(wl), "value": m["value"], "unit": "positions/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": m["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": workload_config(wl),
+    }
+    line.update({k: v for k, v in m.items() if k not in ("value", "ms_per_step")})
     if base is not None:
         line["cpu_baseline"] = base
+    if configs is not None:
+        line["configs"] = configs
+    if wl == DEFAULT_WORKLOAD and not args.no_extras:
+        # The metric's second half: MCTS visits/s over all N GPUs (the
+        # per-rank engines are closed; the other ranks have exited).
+        line["selfplay"] = selfplay_records(world, args)
     print(json.dumps(line), flush=True)
 
 
@@ -452,9 +578,9 @@ def selfplay_window(args):
     return max(6.0, 2.0 * args.warmup), max(10.0, float(args.steps))
 
 
-def run_selfplay_binary(exe, model, wl, args, gpus, search=None):
+def run_selfplay_binary(exe, model, wl, args, gpus, search=None, window=None):
     board, filters, blocks, workers, threads, sims, max_batch = SELFPLAY_WORKLOADS[wl]
-    warm, window = selfplay_window(args)
+    warm, window = selfplay_window(args) if window is None else window
     cmd = [exe, "--model", model, "--gpus", str(gpus), "--workers", str(workers),
            "--search-threads", str(threads), "--sims", str(sims), "--max-batch", str(max_batch),
            "--warmup-seconds", str(warm), "--seconds", str(window)]
@@ -562,6 +688,12 @@ def main():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD,
                     choices=sorted(WORKLOADS) + sorted(SELFPLAY_WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="default workload: skip the other configurations and self-play")
+    ap.add_argument("--selfplay-warmup", type=float, default=4.0,
+                    help="self-play record: warm-up seconds per search")
+    ap.add_argument("--selfplay-seconds", type=float, default=8.0,
+                    help="self-play record: measured seconds per search")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
     if args.workload in SELFPLAY_WORKLOADS:

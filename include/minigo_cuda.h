@@ -161,8 +161,10 @@ int mg_forward_device(mg_engine* e, const float* d_states, int n, float* d_polic
  * with 128 filters, 37 with 256; the error message states the cap); the first call on
  * a device looks up the arena's address and should come before any stream
  * capture; all calls on a device share the arena, so calls whose work
- * overlaps on the GPU race and must be serialised.  Blocks until the results
- * are in the output buffers; d_logits may be NULL. */
+ * overlaps on the GPU race and must be serialised.  Each call synchronises
+ * the engine's stream before it returns (it reads the arena's status word
+ * back to the host), so the results are in the output buffers on return;
+ * d_logits may be NULL. */
 int mg_forward_device_noalloc(mg_engine* e, const float* d_states, int n, float* d_policy,
                               float* d_value, float* d_logits);
 

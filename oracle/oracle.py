@@ -21,8 +21,24 @@ REF_SO = os.path.join(HERE, "_ref", "libref_harness.so")
 CANONICAL, LITERAL = 0, 1
 
 
-def build(ref_dir: str = "/root/reference") -> None:
-    """Runs oracle/Makefile (the _ref part only when ref_dir exists)."""
+def reference_tree() -> str:
+    """The reference tree's location: alphazero_b200.build.REFERENCE_TREE
+    (the MGB_REFERENCE_TREE environment variable or its default)."""
+    import sys
+
+    root = os.path.dirname(HERE)
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    from alphazero_b200 import build as native
+
+    return native.REFERENCE_TREE
+
+
+def build(ref_dir: str | None = None) -> None:
+    """Runs oracle/Makefile (the _ref part only when the reference tree
+    exists)."""
+    if ref_dir is None:
+        ref_dir = reference_tree()
     r = subprocess.run(["make", "-C", HERE, f"REF={ref_dir}"], capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + r.stdout + r.stderr)

@@ -1,7 +1,8 @@
 """Generates the golden fixtures in tests/golden/*.npz from the reference.
 
 Run from the repo root in a container that has the reference tree:
-    python tests/golden/make_golden.py [/root/reference]
+    python tests/golden/make_golden.py [REFERENCE_TREE]
+(default: alphazero_b200.build.REFERENCE_TREE, i.e. $MGB_REFERENCE_TREE).
 
 For each case it
   * builds the seeded state dict (alphazero_b200.weights.make_state_dict) and
@@ -84,4 +85,6 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    from alphazero_b200 import build as native
+
+    main(sys.argv[1] if len(sys.argv) > 1 else native.REFERENCE_TREE)

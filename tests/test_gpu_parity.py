@@ -56,30 +56,85 @@ def _oracle_rows(sd, x, rows):
     return orc.predict_batch(x[rows], oracle.CANONICAL, threads=min(32, os.cpu_count() or 1))
 
 
-@pytest.mark.parametrize("board,filters,blocks,n,max_moves", [
-    (9, 128, 10, 256, 60),     # 9x9 b10c128, batch 256
-    (19, 128, 10, 512, 250),   # 19x19 b10c128, batch 512
-    (19, 256, 20, 1024, 250),  # 19x19 b20c256, batch 1024
-])
-def test_full_size_batches(gpu_engine_factory, board, filters, blocks, n, max_moves):
-    sd = weights.make_state_dict(board, filters, blocks, seed=11, variant="perturbed")
-    e = gpu_engine_factory(sd, "bf16")
-    x = host_lib.random_positions(board, n, 2024, max_moves)
+# Full-size batches of the predict_batch configurations, (board, filters,
+# blocks, batch, max random moves, rows checked against the oracle).  Every
+# row is checked except on the 20-block 256-filter net, where 256 of the 1024
+# rows are (the oracle takes about 8x longer per position there).
+FULL_CONFIGS = {
+    "b9c64x6_bs16": (9, 64, 6, 16, 60, None),
+    "b9c128x10_bs256": (9, 128, 10, 256, 60, None),
+    "b19c128x10_bs512": (19, 128, 10, 512, 250, None),
+    "b19c256x20_bs1024": (19, 256, 20, 1024, 250, 256),
+}
+# Weight sets: exactly the network bench.py times (seed 0, export_onnx --init
+# distributions) on its rank-0 positions (seed 1000), and a perturbed-BN set
+# whose logits are O(1), on other positions.
+WEIGHT_SETS = {"bench": (0, "init", 1000), "perturbed": (11, "perturbed", 2024)}
+_ORACLE_CACHE = {}
+
+
+def _full_case(cfg, wset):
+    board, filters, blocks, n, max_moves, nrows = FULL_CONFIGS[cfg]
+    wseed, variant, pseed = WEIGHT_SETS[wset]
+    key = (cfg, wset)
+    if key not in _ORACLE_CACHE:
+        sd = weights.make_state_dict(board, filters, blocks, seed=wseed, variant=variant)
+        x = host_lib.random_positions(board, n, pseed, max_moves)
+        rows = np.arange(n) if nrows is None else np.sort(
+            np.random.default_rng(0).choice(n, nrows, replace=False))
+        if nrows is not None:
+            rows[0], rows[-1] = 0, n - 1
+        _, ov, ol = _oracle_rows(sd, x, rows)
+        _ORACLE_CACHE[key] = (sd, x, rows, ov, ol)
+    return _ORACLE_CACHE[key]
+
+
+def _report(entry):
+    """Appends one parity record to $MGB_PARITY_REPORT (JSON lines) if set."""
+    import json
+
+    path = os.environ.get("MGB_PARITY_REPORT")
+    print("parity", entry)
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(entry) + "\n")
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp16"])
+@pytest.mark.parametrize("wset", sorted(WEIGHT_SETS))
+@pytest.mark.parametrize("cfg", list(FULL_CONFIGS))
+def test_full_size_batches(gpu_engine_factory, cfg, wset, precision):
+    sd, x, rows, ov, ol = _full_case(cfg, wset)
+    n = len(x)
+    e = gpu_engine_factory(sd, precision, max_batch=n)
     p, v, l = e.forward(x)
     # size-independent properties over the whole batch
     assert np.isfinite(l).all() and np.isfinite(v).all()
     assert np.abs(p.sum(1) - 1).max() < 1e-5
     assert (np.abs(v) <= 1).all()
-    # a sample of rows against the oracle
-    rows = np.random.default_rng(0).choice(n, 12, replace=False)
-    rows[:2] = [0, n - 1]
-    _, ov, ol = _oracle_rows(sd, x, rows)
-    assert np.abs(l[rows] - ol).max() < TOL["bf16"]
-    assert np.abs(v[rows] - ov).max() < TOL["bf16"]
+    # the checked rows against the oracle (fp32 C restatement of the reference engine)
+    dl = np.abs(l[rows] - ol)
+    dv = np.abs(v[rows] - ov)
+    top1 = float((l[rows].argmax(1) == ol.argmax(1)).mean())
+    # top-1 agreement among rows whose oracle top-2 logits are at least
+    # 2x the tolerance apart (closer pairs may swap within tolerance)
+    srt = np.sort(ol, axis=1)
+    clear = (srt[:, -1] - srt[:, -2]) > 2 * TOL[precision]
+    top1_clear = float((l[rows][clear].argmax(1) == ol[clear].argmax(1)).mean()) if clear.any() else None
+    _report({"config": cfg, "weights": wset, "precision": precision, "rows": int(len(rows)),
+             "batch": n, "max_dlogit": float(dl.max()), "max_dvalue": float(dv.max()),
+             "logit_std": float(ol.std()), "max_dlogit_over_std": float(dl.max() / ol.std()),
+             "top1_agreement": top1, "top1_agreement_clear": top1_clear,
+             "clear_rows": int(clear.sum())})
+    assert dl.max() < TOL[precision], float(dl.max())
+    assert dv.max() < TOL[precision], float(dv.max())
+    if top1_clear is not None:
+        assert top1_clear == 1.0
     # positions are independent: permuting the batch permutes the results
-    perm = np.random.default_rng(1).permutation(n)
-    p2, v2, l2 = e.forward(x[perm])
-    assert np.array_equal(l2, l[perm]) and np.array_equal(v2, v[perm])
+    if cfg == "b19c128x10_bs512" and precision == "bf16":
+        perm = np.random.default_rng(1).permutation(n)
+        p2, v2, l2 = e.forward(x[perm])
+        assert np.array_equal(l2, l[perm]) and np.array_equal(v2, v[perm])
 
 
 def test_b20c256_fp32_verification_pass_on_64_positions(gpu_engine_factory):
