@@ -8,10 +8,20 @@
                      (the reference's C++ interfaces over the C ABI) and
                      FastSearch (the reference's MCTS at a lower host cost).
   selfplay_cuda      end-to-end self-play harness: the reference's own
-                     search (src/mcts.cpp, src/game.cpp) compiled unmodified
+                     search (src/mcts.cpp, src/game.cpp, with its model
+                     loader src/onnx_loader.cpp) compiled unmodified
                      from the reference tree with this backend's evaluator;
                      built only where that tree is present (the binary then
                      travels with the package).
+
+  ref_benchmark_cuda, ref_selfplay_cuda
+                     the reference's own `benchmark` and `selfplay` binaries
+                     (src/main_benchmark.cpp, src/main_selfplay.cpp) built by
+                     the reference's CMake with -DMINIGO_BACKEND=cuda: a copy
+                     of the reference tree in a temporary directory with
+                     integration/cuda_backend.patch applied (the factory and
+                     CMake changes a maintainer makes); built only where that
+                     tree and cmake are present.
 
 Run as ``python -m alphazero_b200.build``.  Rebuilds a library only when one
 of its sources is newer than it.
@@ -170,11 +180,66 @@ def build_selfplay(force: bool = False) -> str | None:
     return SELFPLAY_BIN
 
 
+PATCH = os.path.join(PKG, "integration", "cuda_backend.patch")
+REF_BENCHMARK_BIN = os.path.join(LIB, "ref_benchmark_cuda")
+REF_SELFPLAY_BIN = os.path.join(LIB, "ref_selfplay_cuda")
+# What the reference's minigo_core target compiles with the cuda backend.
+REFERENCE_BUILD_FILES = ["CMakeLists.txt", "src/inference_engine.cpp", "src/game.cpp",
+                         "src/onnx_loader.cpp", "src/nn_evaluator.cpp", "src/mcts.cpp",
+                         "src/main_benchmark.cpp", "src/main_selfplay.cpp"]
+
+
+def build_reference_binaries(force: bool = False) -> list[str]:
+    """The reference's `benchmark` and `selfplay` targets built by its own
+    CMake with -DMINIGO_BACKEND=cuda, from a temporary copy of the reference
+    tree with integration/cuda_backend.patch applied.  The reference tree is
+    only read.  Returns the binaries (none where the tree or cmake is absent;
+    an earlier build is kept)."""
+    have = [p for p in (REF_BENCHMARK_BIN, REF_SELFPLAY_BIN) if os.path.exists(p)]
+    ref = [os.path.join(REFERENCE_TREE, f) for f in REFERENCE_BUILD_FILES]
+    cmake = shutil.which("cmake")
+    if cmake is None or shutil.which("patch") is None or not all(os.path.exists(r) for r in ref):
+        return have
+    cuda = build_cuda(force)
+    deps = ref + [PATCH, cuda] + [os.path.join(HOST, f) for f in (
+        "cuda_engine.cpp", "cuda_engine.h", "gpu_evaluator.cpp", "gpu_evaluator.h", "minigo_api.h",
+        "packed_evaluator.h")] + [os.path.join(INCLUDE, "minigo_cuda.h")]
+    if not force and not _stale(REF_BENCHMARK_BIN, deps) and not _stale(REF_SELFPLAY_BIN, deps):
+        return have
+    import tempfile
+
+    with tempfile.TemporaryDirectory(prefix="mgb_reference_build_") as tmp:
+        tree = os.path.join(tmp, "src")
+        shutil.copytree(REFERENCE_TREE, tree, symlinks=True,
+                        ignore=shutil.ignore_patterns(".git", "build", "third_party", "*.onnx",
+                                                      "selfplay_data"))
+        for root, dirs, files in os.walk(tree):  # the copy must be writable
+            for n in dirs + files:
+                p = os.path.join(root, n)
+                if not os.path.islink(p):
+                    os.chmod(p, os.stat(p).st_mode | 0o200)
+        _run(["patch", "-p1", "-s", "-d", tree, "-i", PATCH])
+        bld = os.path.join(tmp, "build")
+        # RelWithDebInfo with portable flags: the reference's Release flags
+        # are -march=native, which would tie the binaries to this host's CPU.
+        _run([cmake, "-S", tree, "-B", bld, "-DMINIGO_BACKEND=cuda", "-DMGB_ROOT=" + ROOT,
+              "-DCMAKE_BUILD_TYPE=RelWithDebInfo",
+              "-DCMAKE_CXX_FLAGS_RELWITHDEBINFO=-O3 -march=x86-64-v3 -DNDEBUG",
+              "-DCMAKE_BUILD_RPATH=$ORIGIN"])
+        _run([cmake, "--build", bld, "--target", "benchmark", "selfplay", "-j",
+              str(os.cpu_count() or 4)])
+        for name, dst in (("benchmark", REF_BENCHMARK_BIN), ("selfplay", REF_SELFPLAY_BIN)):
+            shutil.copy2(os.path.join(bld, name), dst + ".tmp")
+            os.replace(dst + ".tmp", dst)
+    return [REF_BENCHMARK_BIN, REF_SELFPLAY_BIN]
+
+
 def build_all(force: bool = False) -> list[str]:
     out = [build_host(force), build_cuda(force), build_evaluator(force)]
     sp = build_selfplay(force)
     if sp is not None:
         out.append(sp)
+    out += build_reference_binaries(force)
     return out
 
 

@@ -131,6 +131,8 @@ struct mg_engine {
     int* h_err = nullptr;       // pinned status word
     uint32_t* d_bits = nullptr;  // bit-packed inputs [max_batch][words]
     uint32_t* h_bits = nullptr;  // pinned staging for pageable packed inputs
+    uint32_t* d_hist = nullptr;  // history wire format inputs [max_batch][history_words()]
+    uint32_t* h_hist = nullptr;  // pinned staging for pageable history inputs
 
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (bucket, precision)
     int last_bucket = 0;
@@ -153,8 +155,12 @@ struct mg_engine {
         if (h_err) cudaFreeHost(h_err);
         if (d_bits) cudaFree(d_bits);
         if (h_bits) cudaFreeHost(h_bits);
+        if (d_hist) cudaFree(d_hist);
+        if (h_hist) cudaFreeHost(h_hist);
         d_bits = nullptr;
         h_bits = nullptr;
+        d_hist = nullptr;
+        h_hist = nullptr;
         d_stage = d_x16 = d_t = nullptr;
         d_x = d_feat = d_fc = nullptr;
         d_states = d_probs = d_logits = d_value = nullptr;
@@ -189,6 +195,8 @@ struct mg_engine {
 
     int elem_bytes() const { return precision == MG_PREC_FP32 ? 4 : 2; }
     int words_per_pos() const { return (planes * hw + 31) / 32; }
+    // 32-bit words per position of the history wire format.
+    int history_words() const { return 1 + kHistoryBoards * ((hw + 15) / 16); }
     ActType act_type() const {
         return precision == MG_PREC_FP32 ? ActType::FP32
                                          : (precision == MG_PREC_FP16 ? ActType::FP16 : ActType::BF16);
@@ -387,6 +395,10 @@ struct mg_engine {
         ck(cudaMemset(d_bits, 0, (size_t)max_batch * words_per_pos() * 4), "cudaMemset(bits)");
         ck(cudaMallocHost(reinterpret_cast<void**>(&h_bits), (size_t)max_batch * words_per_pos() * 4),
            "cudaMallocHost(bits)");
+        d_hist = dalloc<uint32_t>((size_t)max_batch * history_words(), "cudaMalloc(history)");
+        ck(cudaMemset(d_hist, 0, (size_t)max_batch * history_words() * 4), "cudaMemset(history)");
+        ck(cudaMallocHost(reinterpret_cast<void**>(&h_hist), (size_t)max_batch * history_words() * 4),
+           "cudaMallocHost(history)");
         alloc_batch = max_batch;
         alloc_elem = elem;
     }
@@ -613,6 +625,17 @@ struct mg_engine {
         ck(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "cudaMemsetAsync(err)");
         ck(launch_stage_bits(d_src, words_per_pos(), n, bucket, planes, g, kStagedChannels,
                              (flags & MG_FLAG_EIGEN_COMPAT) != 0, act_type(), d_stage, stream),
+           "stage launch");
+        run_graph(bucket);
+        last_bucket = bucket;
+    }
+
+    // As forward_core for inputs in the history wire format (device pointer).
+    void forward_core_history(const uint32_t* d_src, int n) {
+        const int bucket = bucket_for(n);
+        ck(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "cudaMemsetAsync(err)");
+        ck(launch_stage_history(d_src, history_words(), n, bucket, g, kStagedChannels,
+                                (flags & MG_FLAG_EIGEN_COMPAT) != 0, act_type(), d_stage, stream),
            "stage launch");
         run_graph(bucket);
         last_bucket = bucket;
@@ -895,36 +918,47 @@ int mg_pack_states(const float* states, int n, int state_size, uint32_t* out) {
     return MG_OK;
 }
 
-int mg_forward_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_out,
-                      float* value_out, float* logits_out) {
+}  // extern "C"
+
+namespace {
+
+// Host-buffer forward of n positions of `words` 32-bit words each (one of
+// the packed wire formats): chunks of up to max_batch positions are copied
+// into the engine's device buffer e->*d_buf (straight from the caller's
+// buffer when it is page-locked, else through the pinned e->*h_buf), staged
+// by (e->*core)(device pointer, count), and the results copied back.
+int forward_words(mg_engine* e, const uint32_t* src_all, int n, float* policy_out,
+                  float* value_out, float* logits_out, int (mg_engine::*words_fn)() const,
+                  uint32_t* mg_engine::*d_buf, uint32_t* mg_engine::*h_buf,
+                  void (mg_engine::*core)(const uint32_t*, int)) {
     if (e == nullptr) return MG_E_ARG;
     if (n < 0) return fail(e, MG_E_ARG, "negative batch size");
     if (n == 0) return MG_OK;
-    if (bits == nullptr || policy_out == nullptr || value_out == nullptr)
+    if (src_all == nullptr || policy_out == nullptr || value_out == nullptr)
         return fail(e, MG_E_ARG, "null buffer");
     int dev_err = 0;
     int rc = guarded(e, [&] {
         e->check_ready();
         e->prepare_weights();
         e->ensure_buffers();
-        const size_t words = (size_t)e->words_per_pos();
+        const size_t words = (size_t)(e->*words_fn)();
         const int A = e->actions;
-        const bool pinned = is_pinned(bits);
+        const bool pinned = is_pinned(src_all);
         for (int base = 0; base < n; base += e->max_batch) {
             const int m = std::min(e->max_batch, n - base);
-            const uint32_t* src = bits + (size_t)base * words;
+            const uint32_t* src = src_all + (size_t)base * words;
             if (pinned) {
-                ck(cudaMemcpyAsync(e->d_bits, src, (size_t)m * words * 4, cudaMemcpyHostToDevice,
+                ck(cudaMemcpyAsync(e->*d_buf, src, (size_t)m * words * 4, cudaMemcpyHostToDevice,
                                    e->stream),
-                   "cudaMemcpyAsync(H2D bits)");
+                   "cudaMemcpyAsync(H2D inputs)");
             } else {
                 ck(cudaStreamSynchronize(e->stream), "cudaStreamSynchronize");
-                std::memcpy(e->h_bits, src, (size_t)m * words * 4);
-                ck(cudaMemcpyAsync(e->d_bits, e->h_bits, (size_t)m * words * 4,
+                std::memcpy(e->*h_buf, src, (size_t)m * words * 4);
+                ck(cudaMemcpyAsync(e->*d_buf, e->*h_buf, (size_t)m * words * 4,
                                    cudaMemcpyHostToDevice, e->stream),
-                   "cudaMemcpyAsync(H2D bits)");
+                   "cudaMemcpyAsync(H2D inputs)");
             }
-            e->forward_core_bits(e->d_bits, m);
+            (e->*core)(e->*d_buf, m);
             ck(cudaMemcpyAsync(policy_out + (size_t)base * A, e->d_probs, (size_t)m * A * sizeof(float),
                                cudaMemcpyDeviceToHost, e->stream),
                "cudaMemcpyAsync(D2H policy)");
@@ -949,6 +983,30 @@ int mg_forward_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_o
         return fail(e, MG_E_DEVICE, "a kernel gave up waiting (device status " +
                                         std::to_string(dev_err) + ")");
     return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mg_forward_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_out,
+                      float* value_out, float* logits_out) {
+    return forward_words(e, bits, n, policy_out, value_out, logits_out, &mg_engine::words_per_pos,
+                         &mg_engine::d_bits, &mg_engine::h_bits, &mg_engine::forward_core_bits);
+}
+
+int mg_history_words(const mg_engine* e) {
+    if (e == nullptr || !e->loaded) return 0;
+    return e->history_words();
+}
+
+int mg_forward_history(mg_engine* e, const uint32_t* history, int n, float* policy_out,
+                       float* value_out, float* logits_out) {
+    if (e != nullptr && e->loaded && e->planes != 2 * kHistoryBoards + 1)
+        return fail(e, MG_E_ARG, "the history wire format needs a network of 17 input planes");
+    return forward_words(e, history, n, policy_out, value_out, logits_out,
+                         &mg_engine::history_words, &mg_engine::d_hist, &mg_engine::h_hist,
+                         &mg_engine::forward_core_history);
 }
 
 int mg_synchronize(mg_engine* e) {

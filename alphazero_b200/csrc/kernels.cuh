@@ -140,6 +140,19 @@ cudaError_t launch_stage_bits(const uint32_t* bits, int words_per_pos, int n_val
                               int planes, const FrameGeom& g, int cpad, bool eigen_order, ActType t,
                               void* out, cudaStream_t stream);
 
+// As launch_stage_input for the history wire format (mg_forward_history in
+// include/minigo_cuda.h): position n's words_per_pos words are a header
+// (bits 0-1 the player to move, 1 black / 2 white; bits 4-7 the number h of
+// valid boards; bits 8-10 the ring slot of the current board) and
+// kHistoryBoards slots of ceil(B*B / 16) words, point p at bits 2*(p % 16)
+// of word p / 16 (0 empty, 1 black, 2 white); the board i moves back is slot
+// (top - i) mod kHistoryBoards, for i < h.  The 17 planes GoGame::encode
+// writes (src/game.cpp:229-256) are expanded on the device.
+constexpr int kHistoryBoards = 8;
+cudaError_t launch_stage_history(const uint32_t* hist, int words_per_pos, int n_valid, int n_pos,
+                                 const FrameGeom& g, int cpad, bool eigen_order, ActType t, void* out,
+                                 cudaStream_t stream);
+
 // Head projection as a separate pass (fp32 SIMT path, or when the
 // tensor-core tile does not span all channels): the 1x1 policy / value
 // convolutions over an fp32 trunk [positions * IS][c] -> feat (see

@@ -150,6 +150,72 @@ __global__ void stage_bits_kernel(const uint32_t* __restrict__ bits, int words_p
     }
 }
 
+// Value of input plane `plane` at board point `pt` of a position in the
+// history wire format (kernels.cuh: launch_stage_history), computed as
+// GoGame::encode writes it (src/game.cpp:229-256): planes 0-7 hold the
+// stones of the player to move on the boards 0-7 moves back, planes 8-15
+// the opponent's, plane 16 is all ones when black is to move.
+__device__ __forceinline__ float history_plane_value(const uint32_t* w, int slot_words, uint32_t hdr,
+                                                     int plane, int pt) {
+    const uint32_t to_move = hdr & 3u;
+    if (plane == 2 * kHistoryBoards) return to_move == 1u ? 1.0f : 0.0f;
+    const int i = plane < kHistoryBoards ? plane : plane - kHistoryBoards;
+    if (i >= (int)((hdr >> 4) & 15u)) return 0.0f;  // fewer boards played than i
+    const int slot = ((int)((hdr >> 8) & 7u) - i) & (kHistoryBoards - 1);
+    const uint32_t s = (w[1 + slot * slot_words + (pt >> 4)] >> (2 * (pt & 15))) & 3u;
+    const uint32_t want = plane < kHistoryBoards ? to_move : 3u - to_move;
+    return (s != 0u && s == want) ? 1.0f : 0.0f;
+}
+
+// As stage_input_kernel for the history wire format: position n's
+// words_per_pos words are a header and the ring of its last 8 boards at 2
+// bits per point; the planes are expanded here.
+template <ActType T>
+__global__ void stage_history_kernel(const uint32_t* __restrict__ hist, int words_per_pos,
+                                     int slot_words, int n_valid, int rows, int planes, StageGeom sg,
+                                     int cpad, int eigen_order, void* __restrict__ out) {
+    int m, c8;
+    if (!stage_thread<T>(sg, rows, planes, cpad, out, m, c8)) return;
+    const FrameGeom& g = sg.g;
+    const int n = stage_div(m, sg.is_magic);
+    const int q = m - n * g.is;
+    const int y = stage_div(q, sg.rs_magic);
+    const int x = q - y * g.rs;
+    const bool live = (n < n_valid) && (y < g.board) && (x < g.board);
+    const int hw = g.board * g.board;
+    const int p = y * g.board + x;
+    const uint32_t* w = hist + (size_t)n * words_per_pos;
+    const uint32_t hdr = live ? w[0] : 0u;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int c = c8 + j;
+        float val = 0.0f;
+        if (live && c < planes) {
+            int plane = c, pt = p;
+            if (eigen_order) {  // element (c, p) of the column-major reading
+                const int e = c + p * planes;
+                plane = e / hw;
+                pt = e - plane * hw;
+            }
+            val = history_plane_value(w, slot_words, hdr, plane, pt);
+        }
+        v[j] = val;
+    }
+    if (T == ActType::FP32) {
+        float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)m * cpad + c8);
+        o[0] = make_float4(v[0], v[1], v[2], v[3]);
+        o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint4 wv;
+        wv.x = pack2(v[0], v[1], T);
+        wv.y = pack2(v[2], v[3], T);
+        wv.z = pack2(v[4], v[5], T);
+        wv.w = pack2(v[6], v[7], T);
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + (size_t)m * cpad + c8) = wv;
+    }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -388,6 +454,37 @@ cudaError_t launch_stage_bits(const uint32_t* bits, int words_per_pos, int n_val
         case ActType::FP32:
             stage_bits_kernel<ActType::FP32><<<(unsigned)blocks, threads, 0, stream>>>(
                 bits, words_per_pos, n_valid, rows, planes, sg, cpad, eo, out);
+            break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_stage_history(const uint32_t* hist, int words_per_pos, int n_valid, int n_pos,
+                                 const FrameGeom& g, int cpad, bool eigen_order, ActType t, void* out,
+                                 cudaStream_t stream) {
+    const int planes = 2 * kHistoryBoards + 1;
+    const int slot_words = (g.board * g.board + 15) / 16;
+    if (words_per_pos < 1 + kHistoryBoards * slot_words || cpad < planes) return cudaErrorInvalidValue;
+    const long threads_total = (long)n_pos * g.is * (cpad / 8);
+    const int threads = 256;
+    const long blocks = (threads_total + threads - 1) / threads;
+    if (blocks == 0) return cudaSuccess;
+    const int rows = n_pos * g.is;
+    if (!stage_geom_ok(g, cpad, rows)) return cudaErrorInvalidValue;
+    const StageGeom sg = stage_geom(g, cpad);
+    const int eo = eigen_order ? 1 : 0;
+    switch (t) {
+        case ActType::BF16:
+            stage_history_kernel<ActType::BF16><<<(unsigned)blocks, threads, 0, stream>>>(
+                hist, words_per_pos, slot_words, n_valid, rows, planes, sg, cpad, eo, out);
+            break;
+        case ActType::FP16:
+            stage_history_kernel<ActType::FP16><<<(unsigned)blocks, threads, 0, stream>>>(
+                hist, words_per_pos, slot_words, n_valid, rows, planes, sg, cpad, eo, out);
+            break;
+        case ActType::FP32:
+            stage_history_kernel<ActType::FP32><<<(unsigned)blocks, threads, 0, stream>>>(
+                hist, words_per_pos, slot_words, n_valid, rows, planes, sg, cpad, eo, out);
             break;
     }
     return cudaGetLastError();

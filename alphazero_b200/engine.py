@@ -53,6 +53,8 @@ def lib() -> ctypes.CDLL:
         L.mg_forward_device.argtypes = [vp, fp, ci, fp, fp, fp]
         L.mg_forward_device_noalloc.argtypes = [vp, fp, ci, fp, fp, fp]
         L.mg_forward_packed.argtypes = [vp, fp, ci, fp, fp, fp]
+        L.mg_forward_history.argtypes = [vp, fp, ci, fp, fp, fp]
+        L.mg_history_words.argtypes = [vp]
         L.mg_words_per_position.argtypes = [vp]
         L.mg_pack_states.argtypes = [fp, ci, ci, fp]
         L.mg_synchronize.argtypes = [vp]
@@ -63,7 +65,8 @@ def lib() -> ctypes.CDLL:
         L.mg_launches_per_forward.argtypes = [vp, ci]
         for f in ("mg_load_onnx", "mg_load_weights", "mg_get_info", "mg_set_precision",
                   "mg_set_max_batch", "mg_forward", "mg_forward_device", "mg_forward_device_noalloc",
-                  "mg_forward_packed", "mg_words_per_position", "mg_pack_states", "mg_synchronize",
+                  "mg_forward_packed", "mg_forward_history", "mg_history_words",
+                  "mg_words_per_position", "mg_pack_states", "mg_synchronize",
                   "mg_launch_conv", "mg_launch_trunk", "mg_launches_per_forward"):
             getattr(L, f).restype = ci
         _LIB = L
@@ -184,6 +187,25 @@ class CudaEngine:
 
     def words_per_position(self) -> int:
         return self._L.mg_words_per_position(self._h)
+
+    def forward_history(self, hist, n: int, want_logits: bool = False, out=None):
+        """History wire format (include/minigo_cuda.h, mg_forward_history):
+        hist holds n x history_words() uint32 words, the last 8 boards of
+        each position at 2 bits per point; the planes are expanded on the
+        device.  Returns (probs, values, logits) like forward_packed."""
+        h = np.ascontiguousarray(hist, dtype=np.uint32)
+        A = self.action_size
+        probs, vals = out if out is not None else (np.empty((n, A), np.float32),
+                                                    np.empty((n,), np.float32))
+        logits = np.empty((n, A), np.float32) if want_logits else None
+        if n:
+            self._check(self._L.mg_forward_history(self._h, h.ctypes.data, n, probs.ctypes.data,
+                                                   vals.ctypes.data,
+                                                   logits.ctypes.data if want_logits else None))
+        return probs, vals, logits
+
+    def history_words(self) -> int:
+        return self._L.mg_history_words(self._h)
 
     def predict(self, state):
         """(softmaxed policy, value in [-1, 1]) for one flat state."""

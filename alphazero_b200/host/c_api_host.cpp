@@ -26,6 +26,17 @@ int mg_random_positions(int board, int n, uint32_t seed, int max_moves, float* o
     return 0;
 }
 
+int mg_random_histories(int board, int n, uint32_t seed, int max_moves, uint32_t* out) {
+    if (board < 2 || board > mgb::kMaxBoard || n < 0 || max_moves < 0 || (n > 0 && out == nullptr))
+        return -1;
+    mgb::random_histories(board, n, seed, max_moves, out);
+    return 0;
+}
+
+int mg_history_words_for(int board) {
+    return (board < 2 || board > mgb::kMaxBoard) ? 0 : mgb::history_words(board);
+}
+
 mg_onnx_file* mg_onnx_open(const char* path) {
     g_onnx_error.clear();
     if (path == nullptr) {

@@ -59,6 +59,8 @@ void GoPosition::reset() {
     std::memset(cells_, 0, sizeof(cells_));
     std::memset(prev_, 0, sizeof(prev_));
     std::memset(hist_, 0, sizeof(hist_));
+    std::memset(hist2_, 0, sizeof(hist2_));
+    std::memset(cur2_, 0, sizeof(cur2_));
     has_prev_ = false;
     to_move_ = 1;
     passes_ = 0;
@@ -147,6 +149,7 @@ void GoPosition::play(int action) {
     } else {
         passes_ = 0;
         cells_[action] = (int8_t)to_move_;
+        set2(action, to_move_);
         const int8_t them = (int8_t)(3 - to_move_);
         int nb[4];
         int k = neighbours(action, nb);
@@ -155,7 +158,10 @@ void GoPosition::play(int action) {
         for (int i = 0; i < k; ++i) {
             if (cells_[nb[i]] != them) continue;
             if (chain_liberties(cells_, nb[i], chain, &len) == 0)
-                for (int j = 0; j < len; ++j) cells_[chain[j]] = 0;
+                for (int j = 0; j < len; ++j) {
+                    cells_[chain[j]] = 0;
+                    set2(chain[j], 0);
+                }
         }
     }
     ++moves_;
@@ -166,7 +172,15 @@ void GoPosition::play(int action) {
 void GoPosition::push_history() {
     hist_top_ = (hist_top_ + 1) % kHistory;
     std::memcpy(hist_[hist_top_], cells_, sizeof(cells_));
+    std::memcpy(hist2_[hist_top_], cur2_, sizeof(uint32_t) * (size_t)history_slot_words(n_));
     if (hist_len_ < kHistory) ++hist_len_;
+}
+
+void GoPosition::encode_history(uint32_t* words) const {
+    const int sw = history_slot_words(n_);
+    words[0] = (uint32_t)to_move_ | ((uint32_t)hist_len_ << 4) | ((uint32_t)hist_top_ << 8);
+    for (int k = 0; k < kHistory; ++k)
+        std::memcpy(words + 1 + k * sw, hist2_[k], sizeof(uint32_t) * (size_t)sw);
 }
 
 void GoPosition::encode(float* out) const {
@@ -286,7 +300,11 @@ uint32_t draw_below(uint32_t r, uint32_t range) {
     return (uint32_t)(((uint64_t)r * (uint64_t)range) >> 32);
 }
 
-void random_positions(int board, int n, uint32_t seed, int max_moves, float* out) {
+namespace {
+// The seeded random-playout procedure of random_positions; emit(i, g)
+// receives position i.
+template <typename Emit>
+void random_playouts(int board, int n, uint32_t seed, int max_moves, Emit&& emit) {
     std::mt19937 rng(seed);
     const int nn = board * board;
     std::vector<int> legal_list;
@@ -301,8 +319,21 @@ void random_positions(int board, int n, uint32_t seed, int max_moves, float* out
             legal_list.push_back(nn);
             g.play(legal_list[draw_below(rng(), (uint32_t)legal_list.size())]);
         }
-        g.encode(out + (size_t)i * kInputPlanes * nn);
+        emit(i, g);
     }
+}
+}  // namespace
+
+void random_positions(int board, int n, uint32_t seed, int max_moves, float* out) {
+    const size_t per = (size_t)kInputPlanes * board * board;
+    random_playouts(board, n, seed, max_moves,
+                    [&](int i, const GoPosition& g) { g.encode(out + (size_t)i * per); });
+}
+
+void random_histories(int board, int n, uint32_t seed, int max_moves, uint32_t* out) {
+    const size_t per = (size_t)history_words(board);
+    random_playouts(board, n, seed, max_moves,
+                    [&](int i, const GoPosition& g) { g.encode_history(out + (size_t)i * per); });
 }
 
 }  // namespace mgb

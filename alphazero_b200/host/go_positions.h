@@ -25,6 +25,18 @@ constexpr int kMaxBoard = 19;
 constexpr int kHistory = 8;
 constexpr int kInputPlanes = 2 * kHistory + 1;  // 17
 
+// History wire format of mg_forward_history (include/minigo_cuda.h): the
+// board-history ring GoGame::encode reads (src/game.cpp:229-256), shipped as
+// it is kept instead of as planes.  Word 0 holds the player to move (bits
+// 0-1: 1 black, 2 white), the number h of valid boards (bits 4-7) and the
+// ring slot of the current board (bits 8-10); slot top - i (mod kHistory)
+// is the board i moves back, for i < h.  Then kHistory slots of
+// history_slot_words(n) words, point p of a slot at bits 2 * (p % 16) and
+// up of word p / 16 (0 empty, 1 black, 2 white).
+constexpr int kMaxSlotWords = (kMaxBoard * kMaxBoard + 15) / 16;
+inline int history_slot_words(int n) { return (n * n + 15) / 16; }
+inline int history_words(int n) { return 1 + kHistory * history_slot_words(n); }
+
 class GoPosition {
 public:
     explicit GoPosition(int board_size = 19, float komi = 7.5f);
@@ -40,6 +52,10 @@ public:
     int packed_words() const { return (kInputPlanes * n_ * n_ + 31) / 32; }
     // out[a] = 1 if legal(a) else 0, for a in [0, n * n] (pass last).
     void legal_mask(uint8_t* out) const;
+    // The position in the history wire format (history_words(size())
+    // words): a copy of the packed ring, which play() keeps up to date one
+    // board per move; the planes are expanded on the device.
+    void encode_history(uint32_t* words) const;
 
     int size() const { return n_; }
     bool over() const { return over_; }
@@ -64,6 +80,16 @@ private:
     int8_t hist_[kHistory][kMaxBoard * kMaxBoard];
     int hist_len_;
     int hist_top_;
+    // The same ring at 2 bits per point (the history wire format's slots),
+    // and the current board in that packing, updated stone by stone.
+    uint32_t hist2_[kHistory][kMaxSlotWords];
+    uint32_t cur2_[kMaxSlotWords];
+
+    void set2(int p, int colour) {
+        uint32_t& w = cur2_[p >> 4];
+        const int sh = 2 * (p & 15);
+        w = (w & ~(3u << sh)) | ((uint32_t)colour << sh);
+    }
 
     int neighbours(int p, int* out) const;
     // Flood-fills the chain through p on `b`; returns its liberty count and
@@ -85,5 +111,8 @@ uint32_t draw_below(uint32_t r, uint32_t range);
 // points in increasing index order followed by pass; rng is one
 // std::mt19937 seeded with `seed` shared by all n positions.
 void random_positions(int board, int n, uint32_t seed, int max_moves, float* out);
+// The same positions in the history wire format, history_words(board) words
+// each.
+void random_histories(int board, int n, uint32_t seed, int max_moves, uint32_t* out);
 
 }  // namespace mgb

@@ -22,6 +22,11 @@ def lib() -> ctypes.CDLL:
         L.mg_random_positions.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_uint32, ctypes.c_int,
                                           ctypes.c_void_p]
         L.mg_random_positions.restype = ctypes.c_int
+        L.mg_random_histories.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_uint32, ctypes.c_int,
+                                          ctypes.c_void_p]
+        L.mg_random_histories.restype = ctypes.c_int
+        L.mg_history_words_for.argtypes = [ctypes.c_int]
+        L.mg_history_words_for.restype = ctypes.c_int
         L.mg_onnx_open.argtypes = [ctypes.c_char_p]
         L.mg_onnx_open.restype = ctypes.c_void_p
         L.mg_onnx_error.restype = ctypes.c_char_p
@@ -46,6 +51,19 @@ def random_positions(board: int, n: int, seed: int, max_moves: int) -> np.ndarra
     rc = lib().mg_random_positions(board, n, seed & 0xFFFFFFFF, max_moves, out.ctypes.data)
     if rc != 0:
         raise ValueError("mg_random_positions rejected its arguments")
+    return out
+
+
+def random_histories(board: int, n: int, seed: int, max_moves: int) -> np.ndarray:
+    """The positions of random_positions(board, n, seed, max_moves) in the
+    history wire format of mg_forward_history: [n, history_words(board)]
+    uint32 (a header word and the ring of the last 8 boards, 2 bits per
+    point)."""
+    L = lib()
+    out = np.empty((n, L.mg_history_words_for(board)), dtype=np.uint32)
+    rc = L.mg_random_histories(board, n, seed & 0xFFFFFFFF, max_moves, out.ctypes.data)
+    if rc != 0:
+        raise ValueError("mg_random_histories rejected its arguments")
     return out
 
 

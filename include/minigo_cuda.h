@@ -121,6 +121,26 @@ int mg_pack_states(const float* states, int n, int state_size, uint32_t* out);
 int mg_forward_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_out,
                       float* value_out, float* logits_out);
 
+/* History wire format: a position travels as the board-history ring that
+ * GoGame::encode reads (src/game.cpp:213-256), and the 17 input planes are
+ * expanded on the device.  mg_history_words(e) = 1 + 8 * ceil(board^2 / 16)
+ * little-endian 32-bit words per position (185 words, 740 bytes, on 19x19):
+ *   word 0: bits 0-1 the player to move (1 black, 2 white), bits 4-7 the
+ *           number h of valid boards (0..8), bits 8-10 the ring slot `top`
+ *           of the current board;
+ *   then 8 slots of ceil(board^2 / 16) words; point p of a slot is at bits
+ *           2 * (p % 16) .. +1 of word p / 16 (0 empty, 1 black, 2 white).
+ * The board i moves back (i < h) is slot (top - i) mod 8.  Plane i (< 8)
+ * marks the player to move's stones on it, plane 8 + i the opponent's;
+ * plane 16 is all ones when black is to move.  A host that keeps its ring
+ * in this packing ships it with one copy, with no per-evaluation encode.
+ * Replaces the host-side GoGame::encode of src/mcts.cpp:206-209; results are
+ * identical to mg_forward on the planes that encode writes.  Needs a
+ * network with 17 input planes (MG_E_ARG otherwise). */
+int mg_history_words(const mg_engine* e);
+int mg_forward_history(mg_engine* e, const uint32_t* history, int n, float* policy_out,
+                       float* value_out, float* logits_out);
+
 /* The engine's pinned (page-locked) host input buffer, room for
  * mg_max_batch() positions.  Filling it and passing it to mg_forward avoids
  * any intermediate host copy.  Valid until mg_set_max_batch,

@@ -21,6 +21,12 @@ extern "C" {
  * Returns 0, or -1 for bad arguments (board outside 2..19, n < 0). */
 int mg_random_positions(int board, int n, uint32_t seed, int max_moves, float* out);
 
+/* The same positions in the history wire format of mg_forward_history
+ * (include/minigo_cuda.h): mg_history_words_for(board) 32-bit words each.
+ * No reference counterpart (the reference encodes planes on the host). */
+int mg_random_histories(int board, int n, uint32_t seed, int max_moves, uint32_t* out);
+int mg_history_words_for(int board);
+
 /* ONNX initializer reader (replaces onnx_parser::parse_onnx_file,
  * src/onnx_loader.cpp:183-195). */
 typedef struct mg_onnx_file mg_onnx_file;
