@@ -93,7 +93,7 @@ struct PixLayer {
     int wmap;                // weight tensor map (0 or 1)
     int wrow;                // first row of this layer's weights in that map
     int head;                // fused head projection (last trunk layer)
-    int pad[1];
+    int omap;                // tensor map of out16 (0 or 1) for the epilogue's TMA stores
 };
 static_assert(sizeof(PixLayer) == 64, "PixLayer layout");
 
@@ -241,6 +241,7 @@ template <bool FP16, bool HEAD>
 __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, int l, int nt, int& t,
                                                uint64_t* tfull, uint64_t* tempty, uint32_t* tcount,
                                                uint32_t tmem_base, float* hslot, const float* shead,
+                                               uint16_t* ostage, int& sc, const CUtensorMap* omap,
                                                int warp, int lane) {
     const int quarter = warp & 3;  // channels [32*quarter, +32)
     const int ew = warp - 2;       // 0..kEpiWarps-1
@@ -252,6 +253,12 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
     float* const feat = a.feat;
     const float* const head_b = a.head_b;
     float* slot = hslot + ew * kSlot;  // head layer: this warp's fp32 sums [16][32]
+    // This warp's two staging buffers for the hi plane, [16 pixels][32
+    // channels] each: lane = channel writes them, and one TMA store per chunk
+    // moves the 16 x 64-byte block to global memory, so the output bypasses
+    // the load/store unit.  Buffer sc & 1 is written only once the store
+    // issued from it two chunks earlier has read it.
+    uint16_t* const ost = ostage + ew * (2 * kSlot);
     const int bar_a = 2 + 2 * par, bar_b = 3 + 2 * par;  // head layer only
     bool ok = true;
     // The layer's parameters in registers (read once, not after every
@@ -353,19 +360,28 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
                 f[j] = ((board_mask >> j) & 1) ? fmaxf(x, 0.f) : 0.f;
             }
             if (!HEAD) {
-                uint16_t* oh = out16 + (size_t)px0 * kCo + co;
-                const int nrow = min(kChunk, G.m_total - px0);
+                uint16_t* const sb = ost + (sc & 1) * kSlot;
+                if (lane == 0) bulk_wait_read_n<1>();  // the store from sb two chunks ago has read it
+                __syncwarp();
                 uint32_t lw[8];
 #pragma unroll
                 for (int j = 0; j < kChunk; j += 2) {
                     // two pixels per conversion: hi pair, then lo pair
                     const uint32_t hp = to16x2<FP16>(f[j], f[j + 1]);
                     const uint16_t h0 = (uint16_t)(hp & 0xffffu), h1 = (uint16_t)(hp >> 16);
-                    if (j < nrow) oh[j * kCo] = h0;
-                    if (j + 1 < nrow) oh[(j + 1) * kCo] = h1;
+                    sb[j * 32 + lane] = h0;
+                    sb[(j + 1) * 32 + lane] = h1;
                     // rows past the end (f = 0) fill the last block
                     lw[j >> 1] = lo_bits2(f[j] - from16<FP16>(h0), f[j + 1] - from16<FP16>(h1));
                 }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    // rows past the tensor's end are not written
+                    tma_store_2d(omap, smem_u32(sb), quarter * 32, px0);
+                    bulk_commit();
+                }
+                ++sc;
                 if (has_lo) {
                     uint4* ol = reinterpret_cast<uint4*>(out_lo + lo_block(px0, co));
                     ol[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
@@ -415,7 +431,15 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
                 }
             }
         }
+        // The accumulator has been read: hand it back to the MMA warp first.
         tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+        if (!HEAD && lane == 0) {
+            // this warp's TMA stores of the tile have landed in global memory
+            bulk_wait_all();
+            fence_proxy_async_global();
+        }
         if (progress != nullptr) {
             // This warp's stores of the tile are done (the warp barrier
             // orders every lane's stores before lane 0's release).  The
@@ -435,7 +459,6 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
     }
     return ok;
 }
@@ -447,9 +470,10 @@ template <bool FP16>
 __device__ __noinline__ bool epilogue_head_layer(const PixArgs& a, const Geo G, int l, int nt,
                                                  int& t, uint64_t* tfull, uint64_t* tempty,
                                                  uint32_t* tcount, uint32_t tmem_base, float* hslot,
-                                                 const float* shead, int warp, int lane) {
+                                                 const float* shead, uint16_t* ostage, int& sc,
+                                                 const CUtensorMap* omap, int warp, int lane) {
     return epilogue_layer<FP16, true>(a, G, l, nt, t, tfull, tempty, tcount, tmem_base, hslot,
-                                      shead, warp, lane);
+                                      shead, ostage, sc, omap, warp, lane);
 }
 
 template <bool FP16>
@@ -458,7 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap tmW1,
                        const __grid_constant__ CUtensorMap tmX0,
                        const __grid_constant__ CUtensorMap tmX1,
-                       const __grid_constant__ CUtensorMap tmX2, const __grid_constant__ PixArgs a) {
+                       const __grid_constant__ CUtensorMap tmX2,
+                       const __grid_constant__ CUtensorMap tmO0,
+                       const __grid_constant__ CUtensorMap tmO1, const __grid_constant__ PixArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -466,7 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* wring = smem;                                   // kStages x 16 KB
     uint8_t* slab0 = wring + kStages * kWBytes;              // kSlabs slabs
     float* hslot = reinterpret_cast<float*>(slab0 + kSlabs * slab_bytes);  // [kEpiWarps][16][32]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(hslot + kEpiWarps * kSlot);
+    uint16_t* ostage = reinterpret_cast<uint16_t*>(hslot + kEpiWarps * kSlot);  // [kEpiWarps][2][16][32]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ostage + kEpiWarps * 2 * kSlot);
     uint64_t* wfull = bars;
     uint64_t* wempty = bars + kStages;
     uint64_t* sfull = bars + 2 * kStages;
@@ -664,14 +691,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         // chunk on its own, straight between registers and global memory.
         // Only the head-projection layer, which sums over all 128 channels,
         // couples the warps (through shared memory).
-        int t = 0;
+        int t = 0, sc = 0;
         bool ok = true;
-        for (int l = 0; l < a.n_layers && ok; ++l)
+        if (lane == 0) {
+            prefetch_tensormap(&tmO0);
+            prefetch_tensormap(&tmO1);
+        }
+        for (int l = 0; l < a.n_layers && ok; ++l) {
+            const CUtensorMap* omap = a.layer[l].omap ? &tmO1 : &tmO0;
             ok = a.layer[l].head != 0
                      ? epilogue_head_layer<FP16>(a, G, l, nt, t, tfull, tempty, tcount, tmem_base,
-                                                  hslot, shead, warp, lane)
+                                                  hslot, shead, ostage, sc, omap, warp, lane)
                      : epilogue_layer<FP16, false>(a, G, l, nt, t, tfull, tempty, tcount, tmem_base,
-                                                   hslot, shead, warp, lane);
+                                                   hslot, shead, ostage, sc, omap, warp, lane);
+        }
+        // every TMA store has landed before the CTA exits
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -689,7 +725,7 @@ int slab_rows_for(int npx, int rs) {
 
 size_t pix_smem_bytes(int npx, int rs) {
     const size_t slab = (size_t)slab_rows_for(npx, rs) * 128;
-    return (size_t)kStages * kWBytes + kSlabs * slab + (size_t)kEpiWarps * kSlot * 4 +
+    return (size_t)kStages * kWBytes + kSlabs * slab + (size_t)kEpiWarps * kSlot * (4 + 2 * 2) +
            (2 * kStages + 2 * kSlabs + 2 * kMaxBufs + 1) * 8 + 32 + 3 * kCo * 4 + 1024;
 }
 
@@ -769,10 +805,13 @@ cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16
     a.head_w = nullptr;
     a.head_b = nullptr;
     a.feat = nullptr;
-    // Up to three distinct input buffers, each with its own tensor map.
+    // Up to three distinct input buffers, each with its own tensor map, and
+    // up to two distinct 16-bit output buffers (the epilogue's TMA stores).
     const void* xin[3] = {nullptr, nullptr, nullptr};
     int xcin[3] = {0, 0, 0};
     int nx = 0;
+    const void* oout[2] = {nullptr, nullptr};
+    int no = 0;
     const size_t wstride = (size_t)kCo * 9 * 128;  // elements per cin-128 layer
     for (int l = 0; l < n; ++l) {
         const ConvLayer& L = layers[l];
@@ -797,6 +836,16 @@ cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16
             return cudaErrorInvalidValue;
         }
         P.xmap = xm;
+        P.omap = 0;
+        if (L.out16 != nullptr) {
+            int om = 0;
+            while (om < no && oout[om] != L.out16) ++om;
+            if (om == no) {
+                if (no == 2) return cudaErrorInvalidValue;
+                oout[no++] = L.out16;
+            }
+            P.omap = om;
+        }
         if (l == 0) {
             P.wmap = 0;
             P.wrow = 0;
@@ -833,6 +882,15 @@ cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16
                     (uint32_t)(a.slab_rows / 2), CU_TENSOR_MAP_SWIZZLE_128B))
             return cudaErrorInvalidValue;
     }
+    // Output maps: [rows][128] 16-bit, box of 32 channels x 16 rows (one
+    // epilogue warp's chunk), no swizzle; a map a launch does not use
+    // describes a valid dummy and is never written.
+    CUtensorMap tmO[2];
+    for (int i = 0; i < 2; ++i) {
+        const void* base = i < no ? oout[i] : (no > 0 ? oout[0] : xin[0]);
+        if (!encode(&tmO[i], t16, 2, base, (uint64_t)kCo, rows, 32, kChunk, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return cudaErrorInvalidValue;
+    }
     if (n > 1) {
         cudaError_t e = cudaMemsetAsync(progress, 0, (size_t)grid * sizeof(unsigned), stream);
         if (e != cudaSuccess) return e;
@@ -857,7 +915,7 @@ cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     auto fn = fp16 ? conv3x3_pix_kernel<true> : conv3x3_pix_kernel<false>;
-    return cudaLaunchKernelEx(&cfg, fn, tmW[0], tmW[1], tmX[0], tmX[1], tmX[2], a);
+    return cudaLaunchKernelEx(&cfg, fn, tmW[0], tmW[1], tmX[0], tmX[1], tmX[2], tmO[0], tmO[1], a);
 }
 
 // Whether launch_trunk_pix runs its layers as one persistent launch (at
