@@ -56,6 +56,7 @@ CUDA_SOURCES = [
 CUDA_HEADERS = [
     os.path.join(CSRC, "kernels.cuh"),
     os.path.join(CSRC, "ptx_sm100.cuh"),
+    os.path.join(CSRC, "trunk_schedule.cuh"),
     os.path.join(HOST, "net_weights.h"),
     os.path.join(HOST, "onnx_reader.h"),
     os.path.join(INCLUDE, "minigo_cuda.h"),

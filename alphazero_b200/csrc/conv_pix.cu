@@ -55,6 +55,7 @@
 // kernel's tail.
 #include "kernels.cuh"
 #include "ptx_sm100.cuh"
+#include "trunk_schedule.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -194,45 +195,6 @@ __device__ __forceinline__ size_t lo_block(int px0, int co) {
 // n / d for 0 <= n < 2^23 and d <= 1200 (the launcher checks both).
 __device__ __forceinline__ int div_magic(int n, uint64_t magic) {
     return (int)(((uint64_t)(uint32_t)n * magic) >> kMagicShift);
-}
-
-// Number of tiles of CTA c (those of the last CTA may be fewer).
-__device__ __forceinline__ int cta_tiles(const Geo& g, int c) {
-    const int start = c * g.span;
-    const int end = min(start + g.span, g.m_total);
-    return end > start ? (end - start + g.npx - 1) / g.npx : 0;
-}
-
-// Rows [m0, m0 + len) of CTA c's tile j.
-__device__ __forceinline__ void tile_rows(const Geo& g, int c, int j, int& m0, int& len) {
-    const int start = c * g.span;
-    const int end = min(start + g.span, g.m_total);
-    m0 = start + j * g.npx;
-    len = min(g.npx, end - m0);
-}
-
-// The tile CTA c takes q-th in each layer, and the position of tile j in
-// that order: even CTAs left to right, odd CTAs right to left.
-__device__ __forceinline__ int tile_at(int c, int q, int nt) { return (c & 1) ? nt - 1 - q : q; }
-__device__ __forceinline__ int order_of(int c, int j, int nt) { return (c & 1) ? nt - 1 - j : j; }
-
-// Before a tile of layer l (>= 1) reads rows [m0 - halo, m0 + len + halo)
-// of layer l-1's output: waits until every CTA owning some of those rows has
-// published the tiles that hold them.
-__device__ __forceinline__ bool wait_inputs(const Geo& g, const unsigned* progress, int* err, int l,
-                                            int m0, int len, int halo) {
-    const int lo = max(m0 - halo, 0);
-    const int hi = min(m0 + len + halo, g.m_total) - 1;
-    for (int c = lo / g.span; c <= hi / g.span; ++c) {
-        const int start = c * g.span;
-        const int nt = cta_tiles(g, c);
-        const int j0 = (max(lo, start) - start) / g.npx;
-        const int j1 = (min(hi, start + g.span - 1) - start) / g.npx;
-        const int last = (c & 1) ? order_of(c, j0, nt) : order_of(c, j1, nt);
-        if (!wait_counter(&progress[c], (unsigned)((l - 1) * nt + last + 1), err, kErrWaitDep))
-            return false;
-    }
-    return true;
 }
 
 // One layer of the epilogue for one warp (see the kernel's epilogue): t

@@ -33,6 +33,7 @@
 // records an error code, drains its in-flight copies and frees TMEM.
 #include "kernels.cuh"
 #include "ptx_sm100.cuh"
+#include "trunk_schedule.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -46,7 +47,11 @@ namespace {
 
 constexpr int kBM = 128;  // rows per tile (TMEM lanes)
 constexpr int kBK = 64;   // K elements per stage (128 bytes of 16-bit data)
-constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
+// weight producer, MMA, 8 epilogue warps, slab producer
+constexpr int kEpiWarps = 8;
+constexpr int kSlabWarp = 2 + kEpiWarps;
+constexpr int kThreads = 32 * (kSlabWarp + 1);
+constexpr int kMaxLayers = 44;  // layers per launch (kernel parameter space)
 
 template <int BN>
 struct TcConfig {
@@ -56,32 +61,56 @@ struct TcConfig {
     static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 8 : 12);
     static constexpr uint32_t kBBytes = BN * kBK * 2;
     static constexpr uint32_t kTmemCols = 2 * BN;
-    // B ring + barriers and tmem slot (512) + bias (256 floats) + head weights
-    // (3 x 256 floats) + head exchange (2 x 128 x 3 floats) + 1 KB alignment
-    // slack; the two slabs come on top (slab_bytes).
-    static constexpr int kSmemFixed = kStages * kBBytes + 512 + 1024 + 3072 + 3072 + 1024;
+    // B ring + barriers, tmem slot and tile counters (512) + head weights
+    // (3 x 256 floats) + head exchange (2 x 128 x 3 floats) + two layers'
+    // biases (2 x 256 floats, 16-byte aligned) + 1 KB alignment slack; the
+    // two slabs come on top (slab_bytes).
+    static constexpr int kSmemFixed = kStages * kBBytes + 512 + 3072 + 3072 + 2048 + 16 + 1024;
 };
 
 // Rows of an activation slab: the tile's 128 rows plus RS + 1 on each side,
 // rounded up to 16.
 __host__ __device__ constexpr int tc_slab_rows(int rs) { return (kBM + 2 * (rs + 1) + 15) / 16 * 16; }
 
-struct TcArgs {
-    int m_total;
-    int num_tiles;
-    int nsplit;  // cout / BN
-    int cin;
-    int cout;
-    int rs, is, board;
-    const float* bias;
-    const uint16_t* res_hi;  // residual stream x = hi + lo, pixel-major [m_total][cout]
+// One layer of a launch.
+struct TcLayer {
+    const float* bias;       // [cout]
+    const uint16_t* res_hi;  // residual stream x = hi + lo, pixel-major [m_total][cout], or nullptr
     const uint16_t* res_lo;
     uint16_t* out16;         // output hi plane (operand type) or nullptr
     uint16_t* out_lo;        // output lo plane (fp16 remainder) or nullptr
-    const float* head_w;
+    int cin;
+    int xmap;                // activation tensor map of the input slabs (0..2)
+    int wmap;                // weight tensor map (0 or 1)
+    int wrow;                // first row of this layer's weights in that map
+    int head;                // fused head projection (last trunk layer)
+    int pad[1];
+};
+static_assert(sizeof(TcLayer) == 64, "TcLayer layout");
+
+// Work units: unit u is row tile u / nsplit (rows [128 * (u / nsplit), +128))
+// and column tile u % nsplit (output channels [BN * (u % nsplit), +BN)).
+// CTA c owns units [c * upc, (c + 1) * upc).  With several layers per
+// launch nsplit is 1, and the units are the row tiles of the schedule of
+// trunk_schedule.cuh (span = 128 * upc, npx = 128).
+struct RowSpan {
+    int m_total, span, npx;
+};
+
+struct TcArgs {
+    int m_total;
+    int units, upc;  // work units in all, per CTA
+    int nsplit;      // cout / BN column tiles per row tile (one layer per launch only)
+    int cout;
+    int rs, is, board;
+    int n_layers;
+    int* err;
+    unsigned* progress;  // [grid] tiles finished per CTA (several layers), else nullptr
+    int withhold_cta;    // test hook: this CTA never publishes its progress (-1: none)
+    const float* head_w;  // [3][cout] or nullptr (fused head projection, last layer)
     const float* head_b;
     float* feat;
-    int* err;
+    TcLayer layer[kMaxLayers];
 };
 
 template <bool FP16>
@@ -113,8 +142,11 @@ struct Act16<true> {
 
 template <int BN, bool FP16>
 __global__ void __launch_bounds__(kThreads, 1)
-    conv3x3_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                      const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
+    conv3x3_tc_kernel(const __grid_constant__ CUtensorMap tmA0,
+                      const __grid_constant__ CUtensorMap tmA1,
+                      const __grid_constant__ CUtensorMap tmA2,
+                      const __grid_constant__ CUtensorMap tmB0,
+                      const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ TcArgs a) {
     using Cfg = TcConfig<BN>;
     using P = Act16<FP16>;
     constexpr int S = Cfg::kStages;
@@ -134,13 +166,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* done = bars + 2 * S + 4;
     uint64_t* sfull = bars + 2 * S + 5;
     uint64_t* sempty = sfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + 2);
-    float* sbias = reinterpret_cast<float*>(tmem_slot + 4);
-    float* shead = sbias + 256;  // [3][cout] fused head projection weights
+    uint64_t* bfull = sempty + 2;   // [2] a layer's bias has landed in sbias[l & 1]
+    uint64_t* bempty = bfull + 2;   // [2] the epilogue is done with sbias[l & 1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bempty + 2);
+    uint32_t* tcount = tmem_slot + 1;  // [2] epilogue warps done, per accumulator buffer
+    float* shead = reinterpret_cast<float*>(tmem_slot + 4);  // [3][cout] fused head projection weights
     float* sxchg = shead + 768;  // [2][128][3] head partial-sum exchange
+    // [2][256] folded-BN biases of layers l and l + 1 (bulk copies)
+    float* sbias = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(sxchg + 768) + 15) & ~uintptr_t(15));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int u0 = blockIdx.x * a.upc;
+    const int nt = max(0, min(a.upc, a.units - u0));  // this CTA's units per layer
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -149,9 +187,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&tfull[i]), 1);
-            mbar_init(smem_u32(&tempty[i]), 8);
+            mbar_init(smem_u32(&tempty[i]), kEpiWarps);
             mbar_init(smem_u32(&sfull[i]), 1);
             mbar_init(smem_u32(&sempty[i]), 1);
+            mbar_init(smem_u32(&bfull[i]), 1);
+            mbar_init(smem_u32(&bempty[i]), kEpiWarps);
+            tcount[i] = 0;
         }
         mbar_init(smem_u32(done), 1);
         fence_barrier_init();
@@ -160,7 +201,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
         tmem_relinquish();
     }
-    for (int i = threadIdx.x; i < a.cout; i += kThreads) sbias[i] = a.bias[i];
     if (a.head_w != nullptr)
         for (int i = threadIdx.x; i < 3 * a.cout; i += kThreads) shead[i] = a.head_w[i];
     tc_fence_before();
@@ -172,48 +212,93 @@ __global__ void __launch_bounds__(kThreads, 1)
     griddep_launch_dependents();
     griddep_wait();
 
-    const int cblocks = a.cin / kBK;
-
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- weight (B) producer ----------------
         if (lane == 0) {
-            prefetch_tensormap(&tmA);
-            prefetch_tensormap(&tmB);
-            int it = 0, is = 0;
+            prefetch_tensormap(&tmB0);
+            prefetch_tensormap(&tmB1);
+            int it = 0, nb = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
-                const int mt = tile / a.nsplit;
-                const int n0 = (tile - mt * a.nsplit) * BN;
-                const int m0 = mt * kBM;
-                for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
-                    // the tile's halo slab of this channel block (rows before
-                    // the first or past the last come back as zeros)
-                    const int sb = is & 1;
-                    if (!mbar_wait(smem_u32(&sempty[sb]), ((is >> 1) & 1) ^ 1, a.err,
-                                   kErrWaitProducer)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(smem_u32(&sfull[sb]), slab_bytes);
-                    tma_load_2d(smem_u32(sSlab + sb * slab_bytes), &tmA, smem_u32(&sfull[sb]),
-                                cb * kBK, m0 - halo);
-                    for (int tap = 0; tap < 9; ++tap, ++it) {
-                        const int s = it % S;
-                        const uint32_t ph = ((it / S) & 1) ^ 1;
-                        if (!mbar_wait(smem_u32(&empty[s]), ph, a.err, kErrWaitProducer)) {
-                            ok = false;
-                            break;
+            for (int l = 0; l < a.n_layers && ok; ++l) {
+                const int cin = a.layer[l].cin, wrow = a.layer[l].wrow;
+                const CUtensorMap* map = a.layer[l].wmap ? &tmB1 : &tmB0;
+                // the layer's bias into sbias[l & 1], once the epilogue is
+                // done with layer l - 2's
+                const int bb = l & 1;
+                if (l >= 2 && !mbar_wait(smem_u32(&bempty[bb]), ((l >> 1) - 1) & 1, a.err,
+                                         kErrWaitProducer)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(smem_u32(&bfull[bb]), (uint32_t)a.cout * 4u);
+                bulk_load(smem_u32(sbias + bb * 256), a.layer[l].bias, (uint32_t)a.cout * 4u,
+                          smem_u32(&bfull[bb]));
+                ++nb;
+                for (int q = 0; q < nt && ok; ++q) {
+                    const int n0 = ((u0 + tile_at(blockIdx.x, q, nt)) % a.nsplit) * BN;
+                    for (int cb = 0; cb < cin / kBK && ok; ++cb) {
+                        for (int tap = 0; tap < 9; ++tap, ++it) {
+                            const int s = it % S;
+                            if (!mbar_wait(smem_u32(&empty[s]), ((it / S) & 1) ^ 1, a.err,
+                                           kErrWaitProducer)) {
+                                ok = false;
+                                break;
+                            }
+                            const uint32_t fb = smem_u32(&full[s]);
+                            mbar_arrive_expect_tx(fb, Cfg::kBBytes);
+                            tma_load_2d(smem_u32(sB + s * Cfg::kBBytes), map, fb,
+                                        tap * cin + cb * kBK, wrow + n0);
                         }
-                        const uint32_t fb = smem_u32(&full[s]);
-                        mbar_arrive_expect_tx(fb, Cfg::kBBytes);
-                        tma_load_2d(smem_u32(sB + s * Cfg::kBBytes), &tmB, fb,
-                                    tap * a.cin + cb * kBK, n0);
                     }
                 }
             }
             // Drain: every copy issued has landed before exit.
             for (int j = (it > S ? it - S : 0); j < it; ++j)
                 mbar_wait(smem_u32(&full[j % S]), (j / S) & 1, a.err, kErrWaitDrain);
+            for (int j = (nb > 2 ? nb - 2 : 0); j < nb; ++j)
+                mbar_wait(smem_u32(&bfull[j & 1]), (j >> 1) & 1, a.err, kErrWaitDrain);
+        }
+        __syncwarp();
+    } else if (warp == kSlabWarp) {
+        // ---------------- activation slab producer ----------------
+        // Separate from the weight producer, so the wait for the previous
+        // layer's tiles never holds back the weight ring.
+        if (lane == 0) {
+            prefetch_tensormap(&tmA0);
+            prefetch_tensormap(&tmA1);
+            prefetch_tensormap(&tmA2);
+            int is = 0;
+            bool ok = true;
+            for (int l = 0; l < a.n_layers && ok; ++l) {
+                const int cin = a.layer[l].cin, xmap = a.layer[l].xmap;
+                const CUtensorMap* map = xmap == 0 ? &tmA0 : (xmap == 1 ? &tmA1 : &tmA2);
+                for (int q = 0; q < nt && ok; ++q) {
+                    const int m0 = ((u0 + tile_at(blockIdx.x, q, nt)) / a.nsplit) * kBM;
+                    if (l > 0 && a.progress != nullptr) {
+                        const RowSpan g{a.m_total, a.upc * kBM, kBM};
+                        if (!wait_inputs(g, a.progress, a.err, l, m0, min(kBM, a.m_total - m0),
+                                         halo)) {
+                            ok = false;
+                            break;
+                        }
+                        // the rows were written through the generic proxy
+                        fence_proxy_async_global();
+                    }
+                    for (int cb = 0; cb < cin / kBK; ++cb, ++is) {
+                        // the tile's halo slab of this channel block (rows
+                        // before the first or past the last read as zeros)
+                        const int sb = is & 1;
+                        if (!mbar_wait(smem_u32(&sempty[sb]), ((is >> 1) & 1) ^ 1, a.err,
+                                       kErrWaitProducer)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(smem_u32(&sfull[sb]), slab_bytes);
+                        tma_load_2d(smem_u32(sSlab + sb * slab_bytes), map, smem_u32(&sfull[sb]),
+                                    cb * kBK, m0 - halo);
+                    }
+                }
+            }
             for (int j = (is > 2 ? is - 2 : 0); j < is; ++j)
                 mbar_wait(smem_u32(&sfull[j & 1]), (j >> 1) & 1, a.err, kErrWaitDrain);
         }
@@ -224,50 +309,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc = idesc_f16(kBM, BN, !FP16);
             int it = 0, is = 0, t = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++t) {
-                const int acc = t & 1;
-                if (!mbar_wait(smem_u32(&tempty[acc]), ((t >> 1) & 1) ^ 1, a.err, kErrWaitMma)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-                for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
-                    const int sb = is & 1;
-                    if (!mbar_wait(smem_u32(&sfull[sb]), (is >> 1) & 1, a.err, kErrWaitMma)) {
+            for (int l = 0; l < a.n_layers && ok; ++l) {
+                const int cblocks = a.layer[l].cin / kBK;
+                for (int q = 0; q < nt && ok; ++q, ++t) {
+                    const int acc = t & 1;
+                    if (!mbar_wait(smem_u32(&tempty[acc]), ((t >> 1) & 1) ^ 1, a.err, kErrWaitMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    // Descriptor of the slab's first row; a tap's shifted
-                    // start adds its byte offset / 16 to the address field
-                    // (no carry: every start lies inside shared memory).
-                    const uint64_t ad0 = smem_desc_sw128(smem_u32(sSlab + sb * slab_bytes));
-                    // compile-time trip count: no per-tap index arithmetic
-                    // between the MMA groups
-#pragma unroll
-                    for (int tap = 0; tap < 9; ++tap, ++it) {
-                        const int s = it % S;
-                        if (!mbar_wait(smem_u32(&full[s]), (it / S) & 1, a.err, kErrWaitMma)) {
+                    const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                    for (int cb = 0; cb < cblocks && ok; ++cb, ++is) {
+                        const int sb = is & 1;
+                        if (!mbar_wait(smem_u32(&sfull[sb]), (is >> 1) & 1, a.err, kErrWaitMma)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        // A: the slab from the tap's shifted start row (whole
-                        // 128-byte rows, so no descriptor base offset)
-                        const int r0 = halo + (tap / 3 - 1) * a.rs + (tap % 3 - 1);
-                        const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * Cfg::kBBytes));
-                        const uint64_t ad = ad0 + (uint64_t)(r0 * 8);  // r0 * 128 B / 16
-                        // advance 16 elements (32 bytes) along K inside the swizzle atom
+                        // Descriptor of the slab's first row; a tap's shifted
+                        // start adds its byte offset / 16 to the address field
+                        // (no carry: every start lies inside shared memory).
+                        const uint64_t ad0 = smem_desc_sw128(smem_u32(sSlab + sb * slab_bytes));
+                        // compile-time trip count: no per-tap index arithmetic
+                        // between the MMA groups
 #pragma unroll
-                        for (int k = 0; k < kBK / 16; ++k)
-                            mma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
-                                    (cb | tap | k) != 0);
-                        mma_commit(smem_u32(&empty[s]));
+                        for (int tap = 0; tap < 9; ++tap, ++it) {
+                            const int s = it % S;
+                            if (!mbar_wait(smem_u32(&full[s]), (it / S) & 1, a.err, kErrWaitMma)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            // A: the slab from the tap's shifted start row (whole
+                            // 128-byte rows, so no descriptor base offset)
+                            const int r0 = halo + (tap / 3 - 1) * a.rs + (tap % 3 - 1);
+                            const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * Cfg::kBBytes));
+                            const uint64_t ad = ad0 + (uint64_t)(r0 * 8);  // r0 * 128 B / 16
+                            // advance 16 elements (32 bytes) along K inside the swizzle atom
+#pragma unroll
+                            for (int k = 0; k < kBK / 16; ++k)
+                                mma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                                        (cb | tap | k) != 0);
+                            mma_commit(smem_u32(&empty[s]));
+                        }
+                        if (ok) mma_commit(smem_u32(&sempty[sb]));
                     }
-                    if (ok) mma_commit(smem_u32(&sempty[sb]));
+                    if (ok) mma_commit(smem_u32(&tfull[acc]));
                 }
-                if (ok) mma_commit(smem_u32(&tfull[acc]));
             }
             // All MMAs complete before TMEM is released.
             mma_commit(smem_u32(done));
@@ -284,134 +372,180 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int kCols = BN / 2;
         constexpr int kChunks = kCols / 32;
         const int row = quarter * 32 + lane;
-        using T = typename P::T;
         int t = 0;
-        for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++t) {
-            const int mt = tile / a.nsplit;
-            const int n0 = (tile - mt * a.nsplit) * BN;
-            const int cbase = n0 + half * kCols;
-            const int acc = t & 1;
-            const int m = mt * kBM + row;
-            const bool in_range = m < a.m_total;
-            bool board_px = false;
-            int pos = 0, pix = 0;
-            if (in_range) {
-                pos = m / a.is;
-                const int q = m - pos * a.is;
-                const int y = q / a.rs;
-                const int x = q - y * a.rs;
-                board_px = (y < a.board) && (x < a.board);
-                pix = y * a.board + x;
+        bool ok = true;
+        for (int l = 0; l < a.n_layers && ok; ++l) {
+            // the layer's bias (bulk-copied by the weight producer)
+            const int bb = l & 1;
+            ok = mbar_wait(smem_u32(&bfull[bb]), (l >> 1) & 1, a.err, kErrWaitEpilogue);
+            if (bar_any(1, 32 * kEpiWarps, !ok)) {
+                ok = false;
+                break;
             }
-            const size_t off = (size_t)m * a.cout + cbase;
-            const bool has_res = a.res_hi != nullptr && in_range;
-            // The first chunk's residual (32 hi and 32 lo values, 4 + 4
-            // 16-byte loads) is requested before the accumulator is ready;
-            // each later chunk's one chunk ahead.  Ordinary L1-cached loads:
-            // a lane's 16 bytes are half a sector whose other half the
-            // next load reads (each row is read before it is overwritten in
-            // place, and never read again by this kernel).
-            uint4 rh[4], rl[4];
-            if (has_res) {
-                const uint4* ph = reinterpret_cast<const uint4*>(a.res_hi + off);
-                const uint4* pl = reinterpret_cast<const uint4*>(a.res_lo + off);
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    rh[q4] = ph[q4];
-                    rl[q4] = pl[q4];
+            const float* const bias = sbias + bb * 256;
+            // the layer's parameters, read once
+            const uint16_t* const res_hi = a.layer[l].res_hi;
+            const uint16_t* const res_lo = a.layer[l].res_lo;
+            uint16_t* const out16 = a.layer[l].out16;
+            uint16_t* const out_lo = a.layer[l].out_lo;
+            const bool head = a.layer[l].head != 0;
+            for (int q = 0; q < nt; ++q, ++t) {
+                const int u = u0 + tile_at(blockIdx.x, q, nt);
+                const int m0 = (u / a.nsplit) * kBM;
+                const int len = min(kBM, a.m_total - m0);
+                const int n0 = (u % a.nsplit) * BN;
+                const int cbase = n0 + half * kCols;
+                const int acc = t & 1;
+                const int use = t >> 1;  // earlier tiles of this accumulator buffer
+                const int m = m0 + row;
+                const bool in_range = row < len;
+                bool board_px = false;
+                int pos = 0, pix = 0;
+                if (in_range) {
+                    pos = m / a.is;
+                    const int qq = m - pos * a.is;
+                    const int y = qq / a.rs;
+                    const int x = qq - y * a.rs;
+                    board_px = (y < a.board) && (x < a.board);
+                    pix = y * a.board + x;
                 }
-            }
-            const bool ok = mbar_wait(smem_u32(&tfull[acc]), (t >> 1) & 1, a.err, kErrWaitEpilogue);
-            // Leave together: no epilogue warp may be left at a named barrier.
-            if (bar_any(1, 256, !ok)) break;
-            tc_fence_after();
-            float h0 = 0.f, h1 = 0.f, h2 = 0.f;  // fused head projection partial sums
-            const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) +
-                                   (uint32_t)(acc * BN + half * kCols);
-#pragma unroll 1
-            for (int c = 0; c < kChunks; ++c) {
-                const int c0 = c * 32;
-                uint32_t v[32];
-                tmem_ld_32cols(tbase + (uint32_t)c0, v);
-                tmem_ld_wait();
-                if (!in_range) continue;
-                float f[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + sbias[cbase + c0 + j];
+                const size_t off = (size_t)m * a.cout + cbase;
+                const bool has_res = res_hi != nullptr && in_range;
+                // The first chunk's residual (32 hi and 32 lo values, 4 + 4
+                // 16-byte loads) is requested before the accumulator is ready;
+                // each later chunk's one chunk ahead.  Ordinary L1-cached loads:
+                // a lane's 16 bytes are half a sector whose other half the
+                // next load reads (each row is read before it is overwritten in
+                // place, and never read again by this layer).
+                uint4 rh[4], rl[4];
                 if (has_res) {
+                    const uint4* ph = reinterpret_cast<const uint4*>(res_hi + off);
+                    const uint4* pl = reinterpret_cast<const uint4*>(res_lo + off);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
-                        const uint32_t hw4[4] = {rh[q4].x, rh[q4].y, rh[q4].z, rh[q4].w};
-                        const uint32_t lw4[4] = {rl[q4].x, rl[q4].y, rl[q4].z, rl[q4].w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 hv = P::unpack(hw4[e]);
-                            const float2 lv = __half22float2(*reinterpret_cast<const __half2*>(&lw4[e]));
-                            f[q4 * 8 + 2 * e] += hv.x + lv.x;
-                            f[q4 * 8 + 2 * e + 1] += hv.y + lv.y;
-                        }
+                        rh[q4] = ph[q4];
+                        rl[q4] = pl[q4];
                     }
-                    if (c + 1 < kChunks) {
-                        const uint4* ph = reinterpret_cast<const uint4*>(a.res_hi + off + c0 + 32);
-                        const uint4* pl = reinterpret_cast<const uint4*>(a.res_lo + off + c0 + 32);
+                }
+                ok = mbar_wait(smem_u32(&tfull[acc]), use & 1, a.err, kErrWaitEpilogue);
+                // Leave together: no epilogue warp may be left at a named barrier.
+                if (bar_any(1, 32 * kEpiWarps, !ok)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                float h0 = 0.f, h1 = 0.f, h2 = 0.f;  // fused head projection partial sums
+                const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                       (uint32_t)(acc * BN + half * kCols);
+#pragma unroll 1
+                for (int c = 0; c < kChunks; ++c) {
+                    const int c0 = c * 32;
+                    uint32_t v[32];
+                    tmem_ld_32cols(tbase + (uint32_t)c0, v);
+                    tmem_ld_wait();
+                    if (!in_range) continue;
+                    float f[32];
+                    // the layer's folded-BN bias (the same 32 values in every lane)
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + bias[cbase + c0 + j];
+                    if (has_res) {
 #pragma unroll
                         for (int q4 = 0; q4 < 4; ++q4) {
-                            rh[q4] = ph[q4];
-                            rl[q4] = pl[q4];
+                            const uint32_t hw4[4] = {rh[q4].x, rh[q4].y, rh[q4].z, rh[q4].w};
+                            const uint32_t lw4[4] = {rl[q4].x, rl[q4].y, rl[q4].z, rl[q4].w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float2 hv = P::unpack(hw4[e]);
+                                const float2 lv =
+                                    __half22float2(*reinterpret_cast<const __half2*>(&lw4[e]));
+                                f[q4 * 8 + 2 * e] += hv.x + lv.x;
+                                f[q4 * 8 + 2 * e + 1] += hv.y + lv.y;
+                            }
+                        }
+                        if (c + 1 < kChunks) {
+                            const uint4* ph = reinterpret_cast<const uint4*>(res_hi + off + c0 + 32);
+                            const uint4* pl = reinterpret_cast<const uint4*>(res_lo + off + c0 + 32);
+#pragma unroll
+                            for (int q4 = 0; q4 < 4; ++q4) {
+                                rh[q4] = ph[q4];
+                                rl[q4] = pl[q4];
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) f[j] = board_px ? fmaxf(f[j], 0.0f) : 0.0f;
+                    if (out16 != nullptr) {
+                        uint4* oh = reinterpret_cast<uint4*>(out16 + off + c0);
+                        uint4* ol = reinterpret_cast<uint4*>(out_lo + off + c0);
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            uint32_t hw4[4], lw4[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float x0 = f[q4 * 8 + 2 * e], x1 = f[q4 * 8 + 2 * e + 1];
+                                hw4[e] = P::pack(x0, x1);
+                                const float2 hv = P::unpack(hw4[e]);
+                                const __half2 lv = __floats2half2_rn(x0 - hv.x, x1 - hv.y);
+                                lw4[e] = *reinterpret_cast<const uint32_t*>(&lv);
+                            }
+                            oh[q4] = make_uint4(hw4[0], hw4[1], hw4[2], hw4[3]);
+                            if (out_lo != nullptr) ol[q4] = make_uint4(lw4[0], lw4[1], lw4[2], lw4[3]);
+                        }
+                    }
+                    if (head) {
+                        const float* w0 = shead + cbase + c0;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            h0 = fmaf(f[j], w0[j], h0);
+                            h1 = fmaf(f[j], w0[a.cout + j], h1);
+                            h2 = fmaf(f[j], w0[2 * a.cout + j], h2);
                         }
                     }
                 }
-#pragma unroll
-                for (int j = 0; j < 32; ++j) f[j] = board_px ? fmaxf(f[j], 0.0f) : 0.0f;
-                if (a.out16 != nullptr) {
-                    uint4* oh = reinterpret_cast<uint4*>(a.out16 + off + c0);
-                    uint4* ol = reinterpret_cast<uint4*>(a.out_lo + off + c0);
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        uint32_t hw4[4], lw4[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float x0 = f[q4 * 8 + 2 * e], x1 = f[q4 * 8 + 2 * e + 1];
-                            hw4[e] = P::pack(x0, x1);
-                            const float2 hv = P::unpack(hw4[e]);
-                            const __half2 lv = __floats2half2_rn(x0 - hv.x, x1 - hv.y);
-                            lw4[e] = *reinterpret_cast<const uint32_t*>(&lv);
+                if (head) {
+                    // Half 1 hands its partial sums to half 0 through a
+                    // double-buffered exchange (indexed by accumulator).
+                    float* xs = sxchg + acc * (kBM * 3) + row * 3;
+                    if (half == 1) {
+                        xs[0] = h0;
+                        xs[1] = h1;
+                        xs[2] = h2;
+                    }
+                    named_barrier_sync(1, 32 * kEpiWarps);
+                    if (half == 0 && board_px) {
+                        const int hw = a.board * a.board;
+                        float* fr = a.feat + (size_t)pos * 3 * hw;
+                        fr[pix] = fmaxf(h0 + xs[0] + a.head_b[0], 0.f);
+                        fr[hw + pix] = fmaxf(h1 + xs[1] + a.head_b[1], 0.f);
+                        fr[2 * hw + pix] = fmaxf(h2 + xs[2] + a.head_b[2], 0.f);
+                    }
+                }
+                // The accumulator has been read: hand it back to the MMA warp.
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+                if (a.progress != nullptr) {
+                    // This warp's stores of the tile are done (the warp
+                    // barrier orders every lane's stores before lane 0's
+                    // release).  The epilogue warps count themselves in at CTA
+                    // scope; the last one alone pays for the GPU-scope fences
+                    // and publishes the CTA's count of finished tiles.
+                    __syncwarp();
+                    if (lane == 0) {
+                        const unsigned before = atom_add_acq_rel_cta(smem_u32(&tcount[acc]), 1u);
+                        if (before == (unsigned)(kEpiWarps * use + kEpiWarps - 1) &&
+                            (int)blockIdx.x != a.withhold_cta) {
+                            fence_proxy_async_global();
+                            __threadfence();
+                            red_max_release_gpu(&a.progress[blockIdx.x], (unsigned)(l * nt + q + 1));
                         }
-                        oh[q4] = make_uint4(hw4[0], hw4[1], hw4[2], hw4[3]);
-                        if (a.out_lo != nullptr) ol[q4] = make_uint4(lw4[0], lw4[1], lw4[2], lw4[3]);
                     }
-                }
-                if (a.head_w != nullptr) {
-                    const float* w0 = shead + cbase + c0;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        h0 = fmaf(f[j], w0[j], h0);
-                        h1 = fmaf(f[j], w0[a.cout + j], h1);
-                        h2 = fmaf(f[j], w0[2 * a.cout + j], h2);
-                    }
+                    __syncwarp();
                 }
             }
-            if (a.head_w != nullptr) {
-                // Half 1 hands its partial sums to half 0 through a
-                // double-buffered exchange (indexed by accumulator).
-                float* xs = sxchg + acc * (kBM * 3) + row * 3;
-                if (half == 1) {
-                    xs[0] = h0;
-                    xs[1] = h1;
-                    xs[2] = h2;
-                }
-                named_barrier_sync(1, 256);
-                if (half == 0 && board_px) {
-                    const int hw = a.board * a.board;
-                    float* fr = a.feat + (size_t)pos * 3 * hw;
-                    fr[pix] = fmaxf(h0 + xs[0] + a.head_b[0], 0.f);
-                    fr[hw + pix] = fmaxf(h1 + xs[1] + a.head_b[1], 0.f);
-                    fr[2 * hw + pix] = fmaxf(h2 + xs[2] + a.head_b[2], 0.f);
-                }
-            }
-            tc_fence_before();
+            // this warp is done with the layer's bias
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+            if (ok && lane == 0) mbar_arrive(smem_u32(&bempty[bb]));
         }
     }
 
@@ -421,51 +555,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem_base, Cfg::kTmemCols);
     }
-}
-
-template <int BN, bool FP16>
-cudaError_t launch_bn(const ConvLayer& L, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                      int grid_limit, cudaStream_t stream) {
-    using Cfg = TcConfig<BN>;
-    // The fused head projection needs every output channel of a row in one tile.
-    if (L.head_w != nullptr && L.cout != BN) return cudaErrorInvalidValue;
-    TcArgs a;
-    a.m_total = L.m_total;
-    a.nsplit = L.cout / BN;
-    a.num_tiles = ((L.m_total + kBM - 1) / kBM) * a.nsplit;
-    a.cin = L.cin;
-    a.cout = L.cout;
-    a.rs = L.g.rs;
-    a.is = L.g.is;
-    a.board = L.g.board;
-    a.bias = L.bias;
-    // The residual stream is the hi / lo pair (16-bit operands only).
-    if (L.res32 != nullptr || L.out32 != nullptr || (L.res_hi == nullptr) != (L.res_lo == nullptr) ||
-        (L.out_lo != nullptr && L.out16 == nullptr))
-        return cudaErrorInvalidValue;
-    a.res_hi = static_cast<const uint16_t*>(L.res_hi);
-    a.res_lo = L.res_lo;
-    a.out16 = static_cast<uint16_t*>(L.out16);
-    a.out_lo = L.out_lo;
-    a.head_w = L.head_w;
-    a.head_b = L.head_b;
-    a.feat = L.feat;
-    a.err = L.err;
-    int grid = a.num_tiles < grid_limit ? a.num_tiles : grid_limit;
-    if (grid < 1) grid = 1;
-    // Programmatic dependent launch (see griddep_wait in the kernel).
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = (size_t)Cfg::kSmemFixed + 2 * tc_slab_rows(L.g.rs) * 128;
-    if (cfg.dynamicSmemBytes > 227 * 1024 || tc_slab_rows(L.g.rs) > 256) return cudaErrorInvalidValue;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, conv3x3_tc_kernel<BN, FP16>, tmA, tmB, a);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -509,6 +598,91 @@ cudaError_t configure_one() {
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
 }
 
+// The residual stream is the hi / lo pair (16-bit operands only).
+bool tc_layer_ok(const ConvLayer& L) {
+    return L.res32 == nullptr && L.out32 == nullptr && (L.res_hi == nullptr) == (L.res_lo == nullptr) &&
+           (L.out_lo == nullptr || L.out16 != nullptr) && L.cin % kBK == 0 && L.g.is <= 1200;
+}
+
+TcLayer tc_layer(const ConvLayer& L) {
+    TcLayer t{};
+    t.bias = L.bias;
+    t.res_hi = static_cast<const uint16_t*>(L.res_hi);
+    t.res_lo = L.res_lo;
+    t.out16 = static_cast<uint16_t*>(L.out16);
+    t.out_lo = L.out_lo;
+    t.cin = L.cin;
+    t.head = L.head_w != nullptr ? 1 : 0;
+    return t;
+}
+
+// The launch's common fields; returns the grid (units spread evenly over at
+// most grid_limit CTAs).
+int tc_args(const ConvLayer& F, int nsplit, int grid_limit, TcArgs& a) {
+    a.m_total = F.m_total;
+    a.nsplit = nsplit;
+    a.units = ((F.m_total + kBM - 1) / kBM) * nsplit;
+    int grid = a.units < grid_limit ? a.units : grid_limit;
+    if (grid < 1) grid = 1;
+    a.upc = (a.units + grid - 1) / grid;
+    grid = (a.units + a.upc - 1) / a.upc;
+    a.cout = F.cout;
+    a.rs = F.g.rs;
+    a.is = F.g.is;
+    a.board = F.g.board;
+    a.err = F.err;
+    a.progress = nullptr;
+    a.withhold_cta = -1;
+    a.head_w = nullptr;
+    a.head_b = nullptr;
+    a.feat = nullptr;
+    return grid;
+}
+
+template <int BN, bool FP16>
+cudaError_t launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmB, const TcArgs& a, int grid,
+                      bool cooperative, cudaStream_t stream) {
+    using Cfg = TcConfig<BN>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)Cfg::kSmemFixed + 2 * tc_slab_rows(a.rs) * 128;
+    if (cfg.dynamicSmemBytes > 227 * 1024 || tc_slab_rows(a.rs) > 256) return cudaErrorInvalidValue;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (cooperative) {
+        // CTAs wait on one another's progress: all of them must be resident.
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+    } else {
+        // Programmatic dependent launch (see griddep_wait in the kernel).
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, conv3x3_tc_kernel<BN, FP16>, tmA[0], tmA[1], tmA[2], tmB[0],
+                              tmB[1], a);
+}
+
+cudaError_t launch_tc_any(int bn, bool fp16, const CUtensorMap* tmA, const CUtensorMap* tmB,
+                          const TcArgs& a, int grid, bool cooperative, cudaStream_t stream) {
+    if (fp16) {
+        switch (bn) {
+            case 64: return launch_tc<64, true>(tmA, tmB, a, grid, cooperative, stream);
+            case 128: return launch_tc<128, true>(tmA, tmB, a, grid, cooperative, stream);
+            case 256: return launch_tc<256, true>(tmA, tmB, a, grid, cooperative, stream);
+        }
+    } else {
+        switch (bn) {
+            case 64: return launch_tc<64, false>(tmA, tmB, a, grid, cooperative, stream);
+            case 128: return launch_tc<128, false>(tmA, tmB, a, grid, cooperative, stream);
+            case 256: return launch_tc<256, false>(tmA, tmB, a, grid, cooperative, stream);
+        }
+    }
+    return cudaErrorInvalidValue;
+}
+
 }  // namespace
 
 cudaError_t configure_conv_tc() {
@@ -550,20 +724,97 @@ bool make_conv_tensor_maps(const ConvLayer& L, int bn, bool fp16, CUtensorMap* t
 
 cudaError_t launch_conv_tc(const ConvLayer& L, const CUtensorMap& tmA, const CUtensorMap& tmB,
                            int bn, bool fp16, int grid_limit, cudaStream_t stream) {
-    if (fp16) {
-        switch (bn) {
-            case 64: return launch_bn<64, true>(L, tmA, tmB, grid_limit, stream);
-            case 128: return launch_bn<128, true>(L, tmA, tmB, grid_limit, stream);
-            case 256: return launch_bn<256, true>(L, tmA, tmB, grid_limit, stream);
+    // The fused head projection needs every output channel of a row in one tile.
+    if (!tc_layer_ok(L) || bn <= 0 || L.cout % bn != 0 || (L.head_w != nullptr && L.cout != bn))
+        return cudaErrorInvalidValue;
+    TcArgs a;
+    const int grid = tc_args(L, L.cout / bn, grid_limit, a);
+    a.n_layers = 1;
+    a.layer[0] = tc_layer(L);
+    a.head_w = L.head_w;
+    a.head_b = L.head_b;
+    a.feat = L.feat;
+    const CUtensorMap A[3] = {tmA, tmA, tmA};
+    const CUtensorMap B[2] = {tmB, tmB};
+    return launch_tc_any(bn, fp16, A, B, a, grid, false, stream);
+}
+
+bool trunk_tc_supported(const ConvLayer* layers, int n) {
+    if (n < 1 || n > kMaxLayers) return false;
+    const ConvLayer& F = layers[0];
+    const int bn = F.cout;
+    if (bn != 64 && bn != 128 && bn != 256) return false;
+    if (conv_tc_smem_bytes(bn, F.g.rs) > 227 * 1024 || tc_slab_rows(F.g.rs) > 256) return false;
+    const size_t wstride = (size_t)bn * 9 * bn;  // elements per cin == cout layer
+    for (int l = 0; l < n; ++l) {
+        const ConvLayer& L = layers[l];
+        if (!tc_layer_ok(L) || L.cout != bn || L.m_total != F.m_total || L.g.rs != F.g.rs ||
+            (L.head_w != nullptr && l != n - 1))
+            return false;
+        if (l > 0 && (L.cin != bn ||
+                      L.weight != static_cast<const uint16_t*>(layers[1].weight) + (l - 1) * wstride))
+            return false;
+    }
+    return true;
+}
+
+cudaError_t launch_trunk_tc(const ConvLayer* layers, int n, bool fp16, int grid_limit,
+                            unsigned* progress, cudaStream_t stream, int withhold_cta) {
+    if (!trunk_tc_supported(layers, n) || (n > 1 && progress == nullptr)) return cudaErrorInvalidValue;
+    const ConvLayer& F = layers[0];
+    const int bn = F.cout;
+    TcArgs a;
+    const int grid = tc_args(F, 1, grid_limit, a);
+    a.n_layers = n;
+    a.progress = n > 1 ? progress : nullptr;
+    a.withhold_cta = n > 1 ? withhold_cta : -1;
+    // Up to three distinct input buffers, each with its own tensor map.
+    const void* xin[3] = {nullptr, nullptr, nullptr};
+    int xcin[3] = {0, 0, 0};
+    int nx = 0;
+    for (int l = 0; l < n; ++l) {
+        const ConvLayer& L = layers[l];
+        TcLayer& P = a.layer[l];
+        P = tc_layer(L);
+        int xm = 0;
+        while (xm < nx && xin[xm] != L.in) ++xm;
+        if (xm == nx) {
+            if (nx == 3) return cudaErrorInvalidValue;
+            xin[nx] = L.in;
+            xcin[nx] = L.cin;
+            ++nx;
+        } else if (xcin[xm] != L.cin) {
+            return cudaErrorInvalidValue;
         }
-    } else {
-        switch (bn) {
-            case 64: return launch_bn<64, false>(L, tmA, tmB, grid_limit, stream);
-            case 128: return launch_bn<128, false>(L, tmA, tmB, grid_limit, stream);
-            case 256: return launch_bn<256, false>(L, tmA, tmB, grid_limit, stream);
+        P.xmap = xm;
+        P.wmap = l == 0 ? 0 : 1;
+        P.wrow = l == 0 ? 0 : (l - 1) * bn;
+        if (L.head_w != nullptr) {
+            a.head_w = L.head_w;
+            a.head_b = L.head_b;
+            a.feat = L.feat;
         }
     }
-    return cudaErrorInvalidValue;
+    const char* why = "";
+    CUtensorMap A[3], B[2];
+    for (int i = 0; i < 3; ++i) {
+        const int k = i < nx ? i : 0;  // maps a launch does not use describe a valid dummy
+        if (!encode_2d(&A[i], fp16, xin[k], (uint64_t)xcin[k], (uint64_t)F.m_total, kBK,
+                       (uint32_t)tc_slab_rows(F.g.rs), &why))
+            return cudaErrorInvalidValue;
+    }
+    if (!encode_2d(&B[0], fp16, F.weight, (uint64_t)9 * F.cin, (uint64_t)bn, kBK, (uint32_t)bn, &why) ||
+        !encode_2d(&B[1], fp16, n > 1 ? layers[1].weight : F.weight,
+                   n > 1 ? (uint64_t)9 * bn : (uint64_t)9 * F.cin,
+                   n > 1 ? (uint64_t)(n - 1) * bn : (uint64_t)bn, kBK, (uint32_t)bn, &why))
+        return cudaErrorInvalidValue;
+    if (n > 1) {
+        cudaError_t e = cudaMemsetAsync(progress, 0, (size_t)grid * sizeof(unsigned), stream);
+        if (e != cudaSuccess) return e;
+    }
+    return launch_tc_any(bn, fp16, A, B, a, grid, n > 1, stream);
 }
+
+int trunk_tc_max_layers() { return kMaxLayers; }
 
 }  // namespace mgb

@@ -83,6 +83,11 @@ struct mg_engine {
     int pix_npx = 0;       // pixels per tile override (0 = heuristic)
     int pix_trunk = 1;     // 1: all 128-channel trunk layers as one persistent launch
     int pix_trunk_min_tiles = 3;  // ... when every CTA gets at least this many tiles
+    // 1: 64/256-channel trunk layers as persistent launches.  Off by default:
+    // measured no faster than one launch per layer (19x19 b20c256 batch
+    // 1024: equal within noise; 9x9 b6c64 batch 16, one tile per CTA: 7%
+    // slower, the cross-CTA publish and poll cost more than a launch).
+    int tc_trunk = 0;
     int withhold_cta = -1;  // test hook (MG_TEST_WITHHOLD_PROGRESS): see launch_trunk_pix
     bool use_graphs = true;
     cudaStream_t stream = nullptr;
@@ -548,8 +553,15 @@ struct mg_engine {
                 "the bf16/fp16 modes support networks of up to 256 filters; use fp32");
     }
 
-    // All trunk convolutions of a forward pass (the persistent trunk kernel
-    // on the 128-channel 16-bit path, else one launch per layer).
+    // Whether the 64/256-channel 16-bit trunk runs as persistent launches
+    // (one tile spans every output channel).
+    bool use_tc_trunk() const {
+        return precision != MG_PREC_FP32 && !use_pix() && tc_trunk != 0 && n_convs > 1 && cpad <= 256;
+    }
+
+    // All trunk convolutions of a forward pass: persistent launches of the
+    // 128-channel or the 64/256-channel tensor-core kernel, else one launch
+    // per layer.
     void enqueue_trunk(int bucket) {
         if (use_pix() && pix_trunk) {
             std::vector<ConvLayer> layers(n_convs);
@@ -558,6 +570,18 @@ struct mg_engine {
                                 precision == MG_PREC_FP16, num_sms, d_progress, stream,
                                 withhold_cta, pix_trunk_min_tiles),
                "conv3x3_pix trunk launch");
+        } else if (use_tc_trunk()) {
+            std::vector<ConvLayer> layers(n_convs);
+            for (int li = 0; li < n_convs; ++li) layers[li] = layer_desc(li, bucket);
+            // Runs of at most trunk_tc_max_layers() layers; a run's first
+            // layer takes its weights through its own tensor map.
+            const int run = trunk_tc_max_layers();
+            for (int l0 = 0; l0 < n_convs; l0 += run) {
+                const int cnt = std::min(run, n_convs - l0);
+                ck(launch_trunk_tc(layers.data() + l0, cnt, precision == MG_PREC_FP16, num_sms,
+                                   d_progress, stream, withhold_cta),
+                   "conv3x3_tc trunk launch");
+            }
         } else {
             for (int li = 0; li < n_convs; ++li) launch_conv(li, bucket);
         }
@@ -567,6 +591,7 @@ struct mg_engine {
         if (use_pix() && pix_trunk)
             return trunk_pix_launches(bucket * g.is, n_convs, choose_npx(bucket * g.is), num_sms,
                                       pix_trunk_min_tiles);
+        if (use_tc_trunk()) return (n_convs + trunk_tc_max_layers() - 1) / trunk_tc_max_layers();
         return n_convs;
     }
 
@@ -727,6 +752,7 @@ mg_engine* mg_create(int device, int flags) {
     if (const char* s = std::getenv("MG_PIX")) e->pix_mode = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_NPX")) e->pix_npx = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_TRUNK")) e->pix_trunk = std::atoi(s);
+    if (const char* s = std::getenv("MG_TC_TRUNK")) e->tc_trunk = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_TRUNK_MIN_TILES"))
         e->pix_trunk_min_tiles = std::max(1, std::atoi(s));
     if (const char* s = std::getenv("MG_TEST_WITHHOLD_PROGRESS")) e->withhold_cta = std::atoi(s);

@@ -81,6 +81,18 @@ struct ConvLayer {
 cudaError_t launch_conv_tc(const ConvLayer& layer, const CUtensorMap& tmA, const CUtensorMap& tmB,
                            int bn, bool fp16, int grid_limit, cudaStream_t stream);
 
+// The trunk layers of a 64/128/256-channel network (input conv first) as one
+// persistent cooperative launch of the tensor-core kernel, with the schedule
+// and cross-CTA progress counters of launch_trunk_pix (one tile spans every
+// output channel; 128-row tiles).  Layers 1..n-1 must have cin == cout and
+// their weights back to back from layers[1].weight; n <= trunk_tc_max_layers();
+// progress points at grid_limit counters of scratch.  withhold_cta is the
+// same failure-path test hook as launch_trunk_pix's.
+bool trunk_tc_supported(const ConvLayer* layers, int n);
+cudaError_t launch_trunk_tc(const ConvLayer* layers, int n, bool fp16, int grid_limit,
+                            unsigned* progress, cudaStream_t stream, int withhold_cta = -1);
+int trunk_tc_max_layers();
+
 // Host-side encoding of the two TMA descriptors of a layer.
 bool make_conv_tensor_maps(const ConvLayer& layer, int bn, bool fp16, CUtensorMap* tmA,
                            CUtensorMap* tmB, const char** why);

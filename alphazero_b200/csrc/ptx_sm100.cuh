@@ -178,6 +178,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Bulk copy global -> shared of `bytes` (a multiple of 16; both addresses
+// 16-byte aligned), completion counted on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(dst),
+        "l"((uint64_t)src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
 // Bulk prefetch of [addr, addr + bytes) into L2 (both 16-byte aligned).
 __device__ __forceinline__ void prefetch_l2(const void* addr, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)addr), "r"(bytes)

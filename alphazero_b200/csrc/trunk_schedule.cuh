@@ -1,0 +1,69 @@
+// Work split and cross-CTA ordering of a persistent trunk launch (several
+// 3x3 convolution layers in one cooperative launch), shared by the
+// 128-channel kernel (conv_pix.cu) and the 64/256-channel kernel (conv_tc.cu).
+//
+// CTA c owns the rows [c * span, min((c + 1) * span, m_total)) in every
+// layer, cut into tiles of npx rows (the last may be shorter).  Even CTAs
+// take their tiles left to right, odd CTAs right to left.  A tile of layer l
+// reads layer l-1's rows [m0 - halo, m0 + len + halo): the CTA's own
+// neighbouring tiles and, at the ends of its range, the nearest tiles of
+// the neighbouring CTAs.  After its epilogue has stored a tile, a CTA
+// publishes its count of finished tiles (release, GPU scope); before loading
+// a tile's input of layer l, the slab producer waits (acquire, bounded) until
+// every CTA owning some of those rows has published the tiles of layer l-1
+// that hold them.  The same wait covers the reverse hazard: a tile's outputs
+// overwrite rows that only those tiles of the layer before read.  Because
+// neighbouring CTAs run in opposite directions, the first tile of layer l
+// needs only tiles that were among the first finished in layer l-1.
+//
+// The geometry type G has int fields m_total, span and npx.
+#pragma once
+
+#include "ptx_sm100.cuh"
+
+namespace mgb {
+
+// Number of tiles of CTA c (those of the last CTA may be fewer).
+template <typename G>
+__device__ __forceinline__ int cta_tiles(const G& g, int c) {
+    const int start = c * g.span;
+    const int end = min(start + g.span, g.m_total);
+    return end > start ? (end - start + g.npx - 1) / g.npx : 0;
+}
+
+// Rows [m0, m0 + len) of CTA c's tile j.
+template <typename G>
+__device__ __forceinline__ void tile_rows(const G& g, int c, int j, int& m0, int& len) {
+    const int start = c * g.span;
+    const int end = min(start + g.span, g.m_total);
+    m0 = start + j * g.npx;
+    len = min(g.npx, end - m0);
+}
+
+// The tile CTA c takes q-th in each layer, and the position of tile j in
+// that order: even CTAs left to right, odd CTAs right to left.
+__device__ __forceinline__ int tile_at(int c, int q, int nt) { return (c & 1) ? nt - 1 - q : q; }
+__device__ __forceinline__ int order_of(int c, int j, int nt) { return (c & 1) ? nt - 1 - j : j; }
+
+// Before a tile of layer l (>= 1) reads rows [m0 - halo, m0 + len + halo)
+// of layer l-1's output: waits until every CTA owning some of those rows has
+// published the tiles that hold them.  False (with kErrWaitDep recorded in
+// *err) if a wait gave up.
+template <typename G>
+__device__ __forceinline__ bool wait_inputs(const G& g, const unsigned* progress, int* err, int l,
+                                            int m0, int len, int halo) {
+    const int lo = max(m0 - halo, 0);
+    const int hi = min(m0 + len + halo, g.m_total) - 1;
+    for (int c = lo / g.span; c <= hi / g.span; ++c) {
+        const int start = c * g.span;
+        const int nt = cta_tiles(g, c);
+        const int j0 = (max(lo, start) - start) / g.npx;
+        const int j1 = (min(hi, start + g.span - 1) - start) / g.npx;
+        const int last = (c & 1) ? order_of(c, j0, nt) : order_of(c, j1, nt);
+        if (!wait_counter(&progress[c], (unsigned)((l - 1) * nt + last + 1), err, kErrWaitDep))
+            return false;
+    }
+    return true;
+}
+
+}  // namespace mgb

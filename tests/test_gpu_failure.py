@@ -42,3 +42,27 @@ def test_withheld_progress_is_reported_and_the_context_recovers(gpu_engine_facto
     _, ov, ol = orc.predict_batch(x[rows], oracle.CANONICAL, threads=min(8, os.cpu_count() or 1))
     assert np.abs(l[rows] - ol).max() < 2e-2
     assert np.abs(v[rows] - ov).max() < 2e-2
+
+
+def test_withheld_progress_in_the_64_256_channel_trunk(gpu_engine_factory, monkeypatch):
+    """The same failure path in the persistent trunk launch of the 64/256-
+    channel kernel (conv_tc.cu, MG_TC_TRUNK=1): 19x19, 256 filters, 2 blocks,
+    batch 64."""
+    sd = weights.make_state_dict(19, 256, 2, seed=4, variant="perturbed")
+    x = host_lib.random_positions(19, 64, 8, 250)
+    monkeypatch.setenv("MG_TC_TRUNK", "1")  # the persistent launch (off by default)
+    monkeypatch.setenv("MG_TEST_WITHHOLD_PROGRESS", "3")
+    stalled = gpu_engine_factory(sd, "bf16", max_batch=64)
+    for _ in range(2):
+        t0 = time.time()
+        with pytest.raises(RuntimeError, match=r"gave up waiting \(device status 5\)"):
+            stalled.forward(x)
+        assert time.time() - t0 < 60
+    monkeypatch.delenv("MG_TEST_WITHHOLD_PROGRESS")
+    healthy = gpu_engine_factory(sd, "bf16", max_batch=64)
+    p, v, l = healthy.forward(x)
+    rows = np.array([0, 31, 63])
+    orc = oracle.EigenOracle(sd)
+    _, ov, ol = orc.predict_batch(x[rows], oracle.CANONICAL, threads=min(8, os.cpu_count() or 1))
+    assert np.abs(l[rows] - ol).max() < 2e-2
+    assert np.abs(v[rows] - ov).max() < 2e-2

@@ -249,18 +249,28 @@ def test_packed_wire_format_matches_fp32_planes(gpu_engine_factory, eigen_compat
     assert np.array_equal(l1, l2) and np.array_equal(v1, v2) and np.array_equal(p1, p2)
 
 
-@pytest.mark.parametrize("board,n", [(19, 512), (19, 300), (9, 1024), (19, 24), (9, 5)])
-def test_persistent_trunk_matches_per_layer_launches(gpu_engine_factory, monkeypatch, board, n):
+@pytest.mark.parametrize("board,filters,blocks,n", [
+    (19, 128, 10, 512), (19, 128, 10, 300), (9, 128, 10, 1024), (19, 128, 10, 24), (9, 128, 10, 5),
+    (9, 64, 6, 16), (19, 64, 6, 200), (9, 256, 3, 17), (19, 256, 4, 64), (19, 256, 20, 1024)])
+def test_persistent_trunk_matches_per_layer_launches(gpu_engine_factory, monkeypatch, board, filters,
+                                                     blocks, n):
     """The all-layers persistent launch (per-CTA progress counters between
-    layers) against one launch per layer of the same kernel: bit-identical.
-    19x19 batch 512 / 300 and 9x9 batch 1024 run as one launch; the small
-    batches fall back to one launch per layer in both engines."""
-    sd = weights.make_state_dict(board, 128, 10, seed=5, variant="perturbed")
+    layers) against one launch per layer: bit-identical.  128 channels: the
+    same kernel (conv_pix.cu); 19x19 batch 512 / 300 and 9x9 batch 1024 run
+    as one launch, the small batches fall back to one launch per layer in
+    both engines.  64 / 256 channels (conv_tc.cu): the persistent launch
+    tiles every layer with all output channels, the per-layer launches may
+    split them (small batches); the sums do not depend on that."""
+    sd = weights.make_state_dict(board, filters, blocks, seed=5, variant="perturbed")
     x = host_lib.random_positions(board, n, 99, 250 if board == 19 else 60)
-    monkeypatch.setenv("MG_PIX_TRUNK", "0")
-    per_layer = gpu_engine_factory(sd, "bf16")
-    monkeypatch.delenv("MG_PIX_TRUNK")
-    trunk = gpu_engine_factory(sd, "bf16")
+    env = "MG_PIX_TRUNK" if filters == 128 else "MG_TC_TRUNK"
+    monkeypatch.setenv(env, "0")
+    per_layer = gpu_engine_factory(sd, "bf16", max_batch=max(n, 64))
+    monkeypatch.setenv(env, "1")
+    trunk = gpu_engine_factory(sd, "bf16", max_batch=max(n, 64))
+    monkeypatch.delenv(env)
+    if filters != 128:
+        assert trunk.launches_per_forward(n) < per_layer.launches_per_forward(n)
     p0, v0, l0 = per_layer.forward(x)
     for _ in range(3):  # repeated launches reuse the progress counters
         p1, v1, l1 = trunk.forward(x)
