@@ -4,8 +4,10 @@
 #include <cmath>
 #include <cstring>
 #include <exception>
+#include <new>
 #include <numeric>
 #include <stdexcept>
+#include <type_traits>
 
 namespace mgb {
 
@@ -20,10 +22,8 @@ struct FastSearch::Node {
     std::atomic<int32_t> value_bits{0};  // float total value
     float prior = 0.0f;
     int action = -1;
-    Node* children = nullptr;  // n_children nodes, legal actions ascending
+    Node* children = nullptr;  // n_children nodes, legal actions ascending (arena memory)
     int n_children = 0;
-
-    ~Node() { delete[] children; }
 
     // The total value as a float updated by compare-and-swap
     // (include/mcts.h:38-55).
@@ -45,6 +45,25 @@ struct FastSearch::Node {
     }
 };
 
+namespace {
+constexpr size_t kArenaBlockBytes = size_t(256) << 10;
+}
+
+// n default-constructed nodes from the arena (a fresh block when the
+// current one is full; blocks hold at least one 362-child array).
+FastSearch::Node* FastSearch::Arena::take(int n) {
+    const size_t bytes = (size_t)n * sizeof(Node);
+    if (block < blocks.size() && used + bytes > kArenaBlockBytes) {
+        ++block;
+        used = 0;
+    }
+    if (block == blocks.size()) blocks.emplace_back(new unsigned char[kArenaBlockBytes]);
+    Node* out = reinterpret_cast<Node*>(blocks[block].get() + used);
+    used += (bytes + alignof(Node) - 1) / alignof(Node) * alignof(Node);
+    for (int i = 0; i < n; ++i) new (&out[i]) Node();
+    return out;
+}
+
 FastSearch::FastSearch(PackedEvaluator* evaluator, int board_size, const SearchParams& params,
                        uint64_t seed)
     : evaluator_(evaluator),
@@ -55,8 +74,12 @@ FastSearch::FastSearch(PackedEvaluator* evaluator, int board_size, const SearchP
       rng_((std::mt19937::result_type)seed) {
     if (evaluator_ == nullptr || board_size < 2 || board_size > kMaxBoard || params_.simulations < 1)
         throw std::invalid_argument("FastSearch: bad arguments");
+    static_assert(std::is_trivially_destructible<Node>::value, "arena nodes are never destroyed");
+    if ((size_t)actions_ * sizeof(Node) > kArenaBlockBytes)
+        throw std::invalid_argument("FastSearch: arena block too small");
     const int extra = std::max(1, params_.threads) - 1;
-    for (int i = 0; i < extra; ++i) pool_.emplace_back(&FastSearch::worker_loop, this);
+    arenas_.resize(extra + 1);
+    for (int i = 0; i < extra; ++i) pool_.emplace_back(&FastSearch::worker_loop, this, i + 1);
 }
 
 FastSearch::~FastSearch() {
@@ -93,7 +116,7 @@ FastSearch::Node* FastSearch::select_child(Node* node) const {
 }
 
 // MCTS::mask_policy + MCTS::expand (src/mcts.cpp:43-73).
-void FastSearch::expand(Node* node, std::vector<float>& policy, const uint8_t* legal) {
+void FastSearch::expand(Node* node, std::vector<float>& policy, const uint8_t* legal, Arena& arena) {
     float sum = 0.0f;
     int k = 0;
     for (int a = 0; a < actions_; ++a) {
@@ -108,7 +131,7 @@ void FastSearch::expand(Node* node, std::vector<float>& policy, const uint8_t* l
         for (int a = 0; a < actions_; ++a) ls += (float)legal[a];
         for (int a = 0; a < actions_; ++a) policy[a] = (float)legal[a] / ls;
     }
-    Node* kids = new Node[k];
+    Node* kids = arena.take(k);
     for (int a = 0, i = 0; a < actions_; ++a) {
         if (!legal[a]) continue;
         kids[i].action = a;
@@ -155,7 +178,8 @@ void FastSearch::add_dirichlet_noise(Node* root) {
 }
 
 // MCTS::search_thread_loop (src/mcts.cpp:126-165) for one search thread.
-void FastSearch::playouts_from_root() {
+void FastSearch::playouts_from_root(int tid) {
+    Arena& arena = arenas_[tid];
     std::vector<Node*> path;
     path.reserve(64);
     std::vector<uint32_t> words(words_);
@@ -208,7 +232,7 @@ void FastSearch::playouts_from_root() {
             g.encode_bits(words.data());
             evaluator_->evaluate_packed(words.data(), words_, policy.data(), &value);
             g.legal_mask(legal.data());
-            expand(node, policy, legal.data());
+            expand(node, policy, legal.data(), arena);
             node->state.store(kExpanded, std::memory_order_release);
             backup(path, value);
             sims_done_.fetch_add(1, std::memory_order_relaxed);
@@ -223,7 +247,7 @@ void FastSearch::playouts_from_root() {
     }
 }
 
-void FastSearch::worker_loop() {
+void FastSearch::worker_loop(int tid) {
     uint64_t seen = 0;
     for (;;) {
         {
@@ -232,7 +256,7 @@ void FastSearch::worker_loop() {
             if (stop_) return;
             seen = generation_;
         }
-        playouts_from_root();
+        playouts_from_root(tid);
         {
             std::lock_guard<std::mutex> lock(mu_);
             ++finished_;
@@ -244,6 +268,9 @@ void FastSearch::worker_loop() {
 // MCTS::search (src/mcts.cpp:261-325).
 void FastSearch::search(const GoPosition& pos, std::vector<float>& visits, bool add_noise) {
     if (pos.size() != board_) throw std::invalid_argument("FastSearch: board size mismatch");
+    // The pool is idle between searches: every arena starts over (the
+    // previous search's tree is gone with its root).
+    for (Arena& a : arenas_) a.reset();
     std::unique_ptr<Node> root(new Node);
     {
         std::vector<uint32_t> words(words_);
@@ -253,7 +280,7 @@ void FastSearch::search(const GoPosition& pos, std::vector<float>& visits, bool 
         pos.encode_bits(words.data());
         evaluator_->evaluate_packed(words.data(), words_, policy.data(), &value);
         pos.legal_mask(legal.data());
-        expand(root.get(), policy, legal.data());
+        expand(root.get(), policy, legal.data(), arenas_[0]);
         root->state.store(kExpanded, std::memory_order_release);
         root->visits.store(1, std::memory_order_relaxed);
         root->add_value(value);
@@ -269,7 +296,7 @@ void FastSearch::search(const GoPosition& pos, std::vector<float>& visits, bool 
         ++generation_;
     }
     cv_.notify_all();
-    playouts_from_root();
+    playouts_from_root(0);
     std::exception_ptr err;
     {
         std::unique_lock<std::mutex> lock(mu_);

@@ -13,9 +13,11 @@
 //
 // What differs is the cost per visit, which bounds end-to-end self-play on
 // the host:
-//   * a node's children are one array of the legal moves only, allocated
-//     once at expansion (the reference makes one heap node per legal move,
-//     and scans all board^2 + 1 slots on every selection);
+//   * a node's children are one array of the legal moves only, carved at
+//     expansion out of the expanding thread's node arena, which is reset
+//     once per search and keeps its memory (the reference makes one heap
+//     node per legal move, frees the tree after every move, and scans all
+//     board^2 + 1 slots on every selection);
 //   * the square root of the parent's visits is taken once per selection,
 //     not once per child;
 //   * positions are encoded straight to the bit-packed wire format (768
@@ -71,10 +73,19 @@ public:
     struct Node;
 
 private:
-    void worker_loop();
-    void playouts_from_root();
+    // Bump allocator of child arrays, one per search thread: blocks are
+    // kept across searches and reused from the start of each search.
+    struct Arena {
+        std::vector<std::unique_ptr<unsigned char[]>> blocks;
+        size_t block = 0, used = 0;
+        Node* take(int n);
+        void reset() { block = used = 0; }
+    };
+
+    void worker_loop(int tid);
+    void playouts_from_root(int tid);
     Node* select_child(Node* node) const;
-    void expand(Node* node, std::vector<float>& policy, const uint8_t* legal);
+    void expand(Node* node, std::vector<float>& policy, const uint8_t* legal, Arena& arena);
     void backup(std::vector<Node*>& path, float value);
     static void revert(std::vector<Node*>& path);
     void add_dirichlet_noise(Node* root);
@@ -96,6 +107,7 @@ private:
     int finished_ = 0;         // pool threads done with the current search
     bool stop_ = false;
     std::exception_ptr error_;  // first evaluation failure of the current search
+    std::vector<Arena> arenas_;  // [0] the caller's thread, [1 + i] pool thread i
     std::vector<std::thread> pool_;
 };
 
