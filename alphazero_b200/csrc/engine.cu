@@ -21,6 +21,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -142,6 +143,13 @@ struct mg_engine {
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (bucket, precision)
     int last_bucket = 0;
 
+    // Submissions of mg_submit_packed: per ticket slot, an event recorded
+    // after the results' copies and the status word copied back.
+    static constexpr int kTickets = 4;
+    cudaEvent_t tick_ev[kTickets] = {};
+    int* h_tick_err = nullptr;  // pinned [kTickets]
+    std::atomic<int> next_ticket{0};  // read by mg_wait_submitted on another thread
+
     ~mg_engine() { release_all(); }
 
     void drop_graphs() {
@@ -158,6 +166,8 @@ struct mg_engine {
         d_progress = nullptr;
         if (h_states) cudaFreeHost(h_states);
         if (h_err) cudaFreeHost(h_err);
+        if (h_tick_err) cudaFreeHost(h_tick_err);
+        h_tick_err = nullptr;
         if (d_bits) cudaFree(d_bits);
         if (h_bits) cudaFreeHost(h_bits);
         if (d_hist) cudaFree(d_hist);
@@ -194,6 +204,11 @@ struct mg_engine {
         DeviceGuard dg(device);
         free_buffers();
         free_weights();
+        for (cudaEvent_t& ev : tick_ev)
+            if (ev) {
+                cudaEventDestroy(ev);
+                ev = nullptr;
+            }
         if (stream) cudaStreamDestroy(stream);
         stream = nullptr;
     }
@@ -396,6 +411,8 @@ struct mg_engine {
                           (size_t)max_batch * planes * hw * sizeof(float)),
            "cudaMallocHost(states)");
         ck(cudaMallocHost(reinterpret_cast<void**>(&h_err), sizeof(int)), "cudaMallocHost(err)");
+        ck(cudaMallocHost(reinterpret_cast<void**>(&h_tick_err), kTickets * sizeof(int)),
+           "cudaMallocHost(ticket status)");
         d_bits = dalloc<uint32_t>((size_t)max_batch * words_per_pos(), "cudaMalloc(bits)");
         ck(cudaMemset(d_bits, 0, (size_t)max_batch * words_per_pos() * 4), "cudaMemset(bits)");
         ck(cudaMallocHost(reinterpret_cast<void**>(&h_bits), (size_t)max_batch * words_per_pos() * 4),
@@ -1019,6 +1036,58 @@ int mg_forward_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_o
                       float* value_out, float* logits_out) {
     return forward_words(e, bits, n, policy_out, value_out, logits_out, &mg_engine::words_per_pos,
                          &mg_engine::d_bits, &mg_engine::h_bits, &mg_engine::forward_core_bits);
+}
+
+int mg_submit_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_out, float* value_out,
+                     int* ticket) {
+    if (e == nullptr) return MG_E_ARG;
+    if (ticket == nullptr || bits == nullptr || policy_out == nullptr || value_out == nullptr)
+        return fail(e, MG_E_ARG, "null buffer");
+    if (n < 1 || n > e->max_batch) return fail(e, MG_E_ARG, "batch size out of range");
+    if (!is_pinned(bits) || !is_pinned(policy_out) || !is_pinned(value_out))
+        return fail(e, MG_E_ARG, "mg_submit_packed needs page-locked input and output buffers");
+    return guarded(e, [&] {
+        e->check_ready();
+        e->prepare_weights();
+        e->ensure_buffers();
+        const int slot = e->next_ticket % mg_engine::kTickets;
+        if (e->tick_ev[slot] == nullptr)
+            ck(cudaEventCreateWithFlags(&e->tick_ev[slot], cudaEventDisableTiming), "cudaEventCreate");
+        // A ticket slot is reused kTickets submissions later: the caller has
+        // waited for that one long since (at most two are outstanding).
+        ck(cudaEventSynchronize(e->tick_ev[slot]), "cudaEventSynchronize");
+        const size_t words = (size_t)e->words_per_pos();
+        const int A = e->actions;
+        ck(cudaMemcpyAsync(e->d_bits, bits, (size_t)n * words * 4, cudaMemcpyHostToDevice, e->stream),
+           "cudaMemcpyAsync(H2D bits)");
+        e->forward_core_bits(e->d_bits, n);
+        ck(cudaMemcpyAsync(policy_out, e->d_probs, (size_t)n * A * sizeof(float), cudaMemcpyDeviceToHost,
+                           e->stream),
+           "cudaMemcpyAsync(D2H policy)");
+        ck(cudaMemcpyAsync(value_out, e->d_value, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost,
+                           e->stream),
+           "cudaMemcpyAsync(D2H value)");
+        ck(cudaMemcpyAsync(e->h_tick_err + slot, e->d_err, sizeof(int), cudaMemcpyDeviceToHost,
+                           e->stream),
+           "cudaMemcpyAsync(D2H status)");
+        ck(cudaEventRecord(e->tick_ev[slot], e->stream), "cudaEventRecord");
+        *ticket = e->next_ticket.fetch_add(1);
+    });
+}
+
+int mg_wait_submitted(mg_engine* e, int ticket) {
+    // Touches only the ticket's event and status word (not the engine's
+    // error message), so one thread may wait while another submits.
+    const int issued = e != nullptr ? e->next_ticket.load() : 0;
+    if (e == nullptr || ticket < 0 || ticket >= issued || ticket < issued - mg_engine::kTickets)
+        return MG_E_ARG;
+    const int slot = ticket % mg_engine::kTickets;
+    DeviceGuard dg(e->device);
+    if (cudaEventSynchronize(e->tick_ev[slot]) != cudaSuccess) {
+        cudaGetLastError();
+        return MG_E_CUDA;
+    }
+    return e->h_tick_err[slot] != 0 ? MG_E_DEVICE : MG_OK;
 }
 
 int mg_history_words(const mg_engine* e) {

@@ -55,6 +55,8 @@ def lib() -> ctypes.CDLL:
         L.mg_forward_packed.argtypes = [vp, fp, ci, fp, fp, fp]
         L.mg_forward_history.argtypes = [vp, fp, ci, fp, fp, fp]
         L.mg_history_words.argtypes = [vp]
+        L.mg_submit_packed.argtypes = [vp, fp, ci, fp, fp, ctypes.POINTER(ci)]
+        L.mg_wait_submitted.argtypes = [vp, ci]
         L.mg_words_per_position.argtypes = [vp]
         L.mg_pack_states.argtypes = [fp, ci, ci, fp]
         L.mg_synchronize.argtypes = [vp]
@@ -66,6 +68,7 @@ def lib() -> ctypes.CDLL:
         for f in ("mg_load_onnx", "mg_load_weights", "mg_get_info", "mg_set_precision",
                   "mg_set_max_batch", "mg_forward", "mg_forward_device", "mg_forward_device_noalloc",
                   "mg_forward_packed", "mg_forward_history", "mg_history_words",
+                  "mg_submit_packed", "mg_wait_submitted",
                   "mg_words_per_position", "mg_pack_states", "mg_synchronize",
                   "mg_launch_conv", "mg_launch_trunk", "mg_launches_per_forward"):
             getattr(L, f).restype = ci
@@ -203,6 +206,21 @@ class CudaEngine:
                                                    vals.ctypes.data,
                                                    logits.ctypes.data if want_logits else None))
         return probs, vals, logits
+
+    def submit_packed(self, bits, n: int, probs, values) -> int:
+        """mg_submit_packed: enqueues n bit-packed positions from page-locked
+        `bits` with results into the page-locked arrays probs [n, A] and
+        values [n]; returns a ticket for wait_submitted.  The arrays must
+        stay alive (and unread) until then."""
+        t = ctypes.c_int(-1)
+        self._check(self._L.mg_submit_packed(self._h, bits.ctypes.data, n, probs.ctypes.data,
+                                             values.ctypes.data, ctypes.byref(t)))
+        return t.value
+
+    def wait_submitted(self, ticket: int) -> None:
+        rc = self._L.mg_wait_submitted(self._h, ticket)
+        if rc != 0:
+            raise RuntimeError(f"mg_wait_submitted failed ({rc})")
 
     def history_words(self) -> int:
         return self._L.mg_history_words(self._h)

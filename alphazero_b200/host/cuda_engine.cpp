@@ -23,7 +23,11 @@ CudaEngine::CudaEngine(int device, Precision precision, bool eigen_compat, int m
     check(mg_set_precision(h_, (int)precision), "mg_set_precision");
 }
 
-CudaEngine::~CudaEngine() { mg_destroy(h_); }
+CudaEngine::~CudaEngine() {
+    mg_destroy(h_);
+    mg_host_free(submit_in_[0]);
+    mg_host_free(submit_in_[1]);
+}
 
 void CudaEngine::check(int rc, const char* what) const {
     if (rc != MG_OK) {
@@ -115,6 +119,31 @@ void CudaEngine::predict_bits(const uint32_t* const* bits, int n, float* policy,
               "mg_forward_packed");
         count_launches(m);
     }
+}
+
+int CudaEngine::submit_bits(const uint32_t* const* bits, int n, float* policy, float* value) {
+    const int words = words_per_position();
+    const int cap = mg_max_batch(h_);
+    if (n < 1 || n > cap) throw std::invalid_argument("submit_bits: batch size out of range");
+    uint32_t*& in = submit_in_[submit_next_];
+    if (in == nullptr) {
+        in = static_cast<uint32_t*>(mg_host_alloc((size_t)cap * words * sizeof(uint32_t)));
+        if (in == nullptr) throw std::runtime_error("page-locked input buffer could not be allocated");
+    }
+    for (int i = 0; i < n; ++i) std::memcpy(in + (size_t)i * words, bits[i], sizeof(uint32_t) * words);
+    int ticket = -1;
+    check(mg_submit_packed(h_, in, n, policy, value, &ticket), "mg_submit_packed");
+    submit_next_ ^= 1;
+    count_launches(n);
+    return ticket;
+}
+
+int CudaEngine::max_batch() const { return mg_max_batch(h_); }
+
+void CudaEngine::wait_submitted(int ticket) {
+    const int rc = mg_wait_submitted(h_, ticket);
+    if (rc == MG_E_DEVICE) throw std::runtime_error("mg_wait_submitted: a kernel gave up waiting");
+    if (rc != MG_OK) throw std::runtime_error("mg_wait_submitted failed (" + std::to_string(rc) + ")");
 }
 
 void CudaEngine::predict_raw(const float* const* states, int n, int state_size, float* policy,

@@ -56,6 +56,16 @@ public:
     // into the engine's pinned buffer (mg_host_bits) and shipped as is.
     void predict_bits(const uint32_t* const* bits, int n, float* policy, float* value);
 
+    // The same without waiting (mg_submit_packed): gathers n <= max batch
+    // positions into one of two page-locked input buffers of this object,
+    // enqueues the evaluation with results into policy / value (page-locked,
+    // e.g. mg_host_alloc) and returns a ticket for wait_submitted.  At most
+    // two submissions may be outstanding.  wait_submitted may run on another
+    // thread than submit_bits; it throws std::runtime_error if the
+    // evaluation failed.
+    int submit_bits(const uint32_t* const* bits, int n, float* policy, float* value);
+    void wait_submitted(int ticket);
+
     // Packs one state's binary planes (`size` floats, each 0 or 1) into
     // (size + 31) / 32 words, element j at bit j % 32 of word j / 32; false
     // if some value is neither 0 nor 1 (the words are then unspecified).
@@ -63,6 +73,7 @@ public:
     int words_per_position() const { return (input_channels * board_size * board_size + 31) / 32; }
 
     int device() const { return device_; }
+    int max_batch() const;  // positions per engine call (mg_max_batch)
     int action_size() const { return action_size_; }
     // Kernel launches of this library made by predict / predict_batch /
     // predict_raw so far (readable from any thread).
@@ -75,6 +86,8 @@ private:
     void count_launches(int n);
 
     mg_engine* h_ = nullptr;
+    uint32_t* submit_in_[2] = {nullptr, nullptr};  // page-locked inputs of submit_bits
+    int submit_next_ = 0;
     int device_ = 0;
     int action_size_ = 0;
     std::vector<float> policy_scratch_, value_scratch_;

@@ -6,6 +6,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cmath>
 #include <limits>
 #include <stdexcept>
@@ -18,6 +19,8 @@ GpuEvaluator::GpuEvaluator(InferenceEngine* engine, int max_batch_size)
     : engine_(engine), cuda_(dynamic_cast<CudaEngine*>(engine)), max_batch_(max_batch_size) {
     if (engine_ == nullptr || max_batch_ < 1) throw std::invalid_argument("GpuEvaluator: bad arguments");
     queue_.reserve(max_batch_);
+    if (const char* s = std::getenv("MG_EVAL_IN_FLIGHT")) max_in_flight_ = std::atoi(s) >= 2 ? 2 : 1;
+    if (const char* s = std::getenv("MG_EVAL_OVERLAP_MIN")) overlap_min_ = (size_t)std::max(0, std::atoi(s));
     server_ = std::thread(&GpuEvaluator::server_loop, this);
     completer_ = std::thread(&GpuEvaluator::completion_loop, this);
 }
@@ -246,30 +249,60 @@ void GpuEvaluator::fail_batch(std::vector<Pending>& batch) {
     batch.clear();
 }
 
+bool GpuEvaluator::submittable(const std::vector<Pending>& batch) const {
+    if (cuda_ == nullptr || batch.empty() || (int)batch.size() > max_batch_ ||
+        (int)batch.size() > cuda_->max_batch())
+        return false;
+    const int size = cuda_->input_channels * cuda_->board_size * cuda_->board_size;
+    for (const auto& p : batch)
+        if (p.bits == nullptr || p.buf->state_size != size) return false;
+    return true;
+}
+
 void GpuEvaluator::server_loop() {
     std::vector<Pending> batch;
     batch.reserve(max_batch_);
     for (uint64_t k = 0;; ++k) {
         {
             std::unique_lock<std::mutex> lock(mu_);
-            cv_.wait(lock, [this] { return !queue_.empty() || stop_; });
+            cv_.wait(lock, [&] {
+                if (stop_) return true;
+                if (queue_.empty() || in_flight_ >= max_in_flight_) return false;
+                return in_flight_ == 0 ||
+                       queue_.size() >= std::min((size_t)max_batch_,
+                                                 overlap_min_ > 0 ? overlap_min_ : last_batch_);
+            });
             if (stop_ && queue_.empty()) break;
             const int n = std::min((int)queue_.size(), max_batch_);
             batch.assign(queue_.begin(), queue_.begin() + n);
             queue_.erase(queue_.begin(), queue_.begin() + n);
+            ++in_flight_;  // until the completion thread has waited for it
+            last_batch_ = (size_t)n;
         }
-        const int si = (int)(k & 1);
+        const int si = (int)(k % kSlots);
         Slot& slot = slots_[si];
         {
             // The completion thread may still be handing back the batch
-            // that used this slot two batches ago.
+            // that used this slot kSlots batches ago.
             std::unique_lock<std::mutex> lock(cmu_);
             ccv_.wait(lock, [&] { return !slot.busy; });
         }
         slot.batch.swap(batch);
+        slot.ticket = -1;
         try {
-            run_batch(slot);
             const int n = (int)slot.batch.size();
+            if (submittable(slot.batch)) {
+                reserve(slot, (size_t)max_batch_, (size_t)cuda_->action_size());
+                const auto t0 = std::chrono::steady_clock::now();
+                bit_ptrs_.resize(n);
+                for (int i = 0; i < n; ++i) bit_ptrs_[i] = slot.batch[i].bits;
+                slot.ticket = cuda_->submit_bits(bit_ptrs_.data(), n, slot.policy, slot.value);
+                engine_ns_.fetch_add((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                         std::chrono::steady_clock::now() - t0)
+                                         .count());
+            } else {
+                run_batch(slot);  // synchronous (fp32 planes, mixed or other engines)
+            }
             batches_.fetch_add(1);
             positions_.fetch_add(n);
             int seen = largest_.load();
@@ -286,6 +319,7 @@ void GpuEvaluator::server_loop() {
             {
                 std::lock_guard<std::mutex> lock(mu_);
                 last_error_ = ex.what();
+                --in_flight_;
             }
             fail_batch(slot.batch);
         }
@@ -308,10 +342,35 @@ void GpuEvaluator::completion_loop() {
             si = posted_.front();
             posted_.erase(posted_.begin());
         }
-        hand_back(slots_[si]);
+        Slot& slot = slots_[si];
+        bool ok = true;
+        if (slot.ticket >= 0) {
+            // Submissions complete in order: wait for this one on the GPU.
+            const auto t0 = std::chrono::steady_clock::now();
+            try {
+                cuda_->wait_submitted(slot.ticket);
+            } catch (const std::exception& ex) {
+                ok = false;
+                failed_.fetch_add(1);
+                std::lock_guard<std::mutex> lock(mu_);
+                last_error_ = ex.what();
+            }
+            engine_ns_.fetch_add((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                     std::chrono::steady_clock::now() - t0)
+                                     .count());
+        }
+        {
+            // Its place in flight is free before the clients are woken, so
+            // the server can submit the next batch meanwhile.
+            std::lock_guard<std::mutex> lock(mu_);
+            --in_flight_;
+        }
+        cv_.notify_all();
+        if (ok) hand_back(slot);
+        else fail_batch(slot.batch);
         {
             std::lock_guard<std::mutex> lock(cmu_);
-            slots_[si].busy = false;
+            slot.busy = false;
         }
         ccv_.notify_all();
     }

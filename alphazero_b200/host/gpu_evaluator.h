@@ -20,9 +20,20 @@
 //   * handing results back is pipelined with the next engine call: the
 //     server thread forms batch k+1 and runs it on the engine while a
 //     completion thread copies batch k's results into the clients' buffers
-//     and wakes them (two result slots; waking a sleeping client is a
-//     futex call of a few microseconds, half the server's time at 19x19
-//     batch 512 when it was done inline);
+//     and wakes them (waking a sleeping client is a futex call of a few
+//     microseconds, half the server's time at 19x19 batch 512 when it was
+//     done inline);
+//   * with a CudaEngine, bit-packed batches are submitted without waiting
+//     (CudaEngine::submit_bits): the server gathers and submits the next
+//     batch while the GPU still computes the previous one, so the GPU does
+//     not idle through each batch's gather, copies and synchronisation.  A
+//     second batch is submitted while one is in flight only once at least
+//     as many requests are queued as that batch holds, so batches do not
+//     shrink (else the server waits for the GPU, then takes whatever is
+//     queued, as the reference's server does); the completion thread waits
+//     for each submission in order, frees its place in flight, then wakes
+//     its clients.  Measured on 2 GPUs with 24 host threads, FastSearch
+//     self-play 697k -> 763k visits/s;
 //   * a client is woken while its buffer's mutex is held: the reference
 //     notifies after unlocking (src/nn_evaluator.cpp:127-137), so a client
 //     that sees `done` can return and destroy its stack NNResultBuf while
@@ -93,7 +104,19 @@ private:
         size_t capacity = 0;               // positions policy / value hold
         std::vector<Result> results;       // other engines' results
         bool busy = false;                 // posted, not yet handed back
+        int ticket = -1;                   // submitted without waiting (CudaEngine), else -1
     };
+    static constexpr int kSlots = 4;       // in flight (2), being handed back, being formed
+    // Batches submitted and not yet waited for (1 or 2; MG_EVAL_IN_FLIGHT),
+    // and the queued requests that let a second one go in flight
+    // (MG_EVAL_OVERLAP_MIN; 0, the default, means the size of the batch in
+    // flight).
+    int max_in_flight_ = 2;
+    size_t overlap_min_ = 0;
+    size_t last_batch_ = 1;  // size of the last batch taken (guarded by mu_)
+    // True if this batch goes to the engine as a submission (bit-packed,
+    // CudaEngine, one chunk).
+    bool submittable(const std::vector<Pending>& batch) const;
     static void reserve(Slot& slot, size_t n, size_t actions);
     void server_loop();
     void completion_loop();
@@ -117,7 +140,8 @@ private:
     std::vector<const uint32_t*> bit_ptrs_;
     std::vector<float> unpacked_;  // fp32 planes of packed-only requests in a mixed batch
 
-    Slot slots_[2];
+    Slot slots_[kSlots];
+    int in_flight_ = 0;  // submitted batches not yet waited for (guarded by mu_)
     std::mutex cmu_;  // guards slots_[*].busy, posted_, done_
     std::condition_variable ccv_;
     std::vector<int> posted_;  // slots waiting for the completion thread

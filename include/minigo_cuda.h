@@ -121,6 +121,23 @@ int mg_pack_states(const float* states, int n, int state_size, uint32_t* out);
 int mg_forward_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_out,
                       float* value_out, float* logits_out);
 
+/* Asynchronous form of mg_forward_packed for a batching server that
+ * overlaps the host work of one batch (gathering its inputs, waking the
+ * clients of the last one) with the GPU work of another: enqueues the copy
+ * of n (<= mg_max_batch) bit-packed positions, the forward pass and the
+ * copies of the results into policy_out / value_out on the engine's stream,
+ * and returns at once with a ticket.  All three buffers must be page-locked
+ * (mg_host_alloc); the input may be reused, and the outputs read, only after
+ * mg_wait_submitted(ticket).  At most two submissions may be outstanding;
+ * submissions complete in order.  mg_wait_submitted blocks until that
+ * submission's results are in the output buffers and returns MG_OK,
+ * MG_E_DEVICE if a kernel gave up waiting, or MG_E_ARG / MG_E_CUDA; it does
+ * not set mg_last_error, and one thread may call it while another submits.
+ * No counterpart in the reference, whose engines are synchronous. */
+int mg_submit_packed(mg_engine* e, const uint32_t* bits, int n, float* policy_out,
+                     float* value_out, int* ticket);
+int mg_wait_submitted(mg_engine* e, int ticket);
+
 /* History wire format: a position travels as the board-history ring that
  * GoGame::encode reads (src/game.cpp:213-256), and the 17 input planes are
  * expanded on the device.  mg_history_words(e) = 1 + 8 * ceil(board^2 / 16)

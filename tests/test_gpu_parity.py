@@ -279,3 +279,36 @@ def test_persistent_trunk_matches_per_layer_launches(gpu_engine_factory, monkeyp
     _, ov, ol = _oracle_rows(sd, x, rows)
     assert np.abs(l1[rows] - ol).max() < TOL["bf16"]
     assert np.abs(v1[rows] - ov).max() < TOL["bf16"]
+
+
+def test_submitted_batches_match_synchronous_calls(gpu_engine_factory):
+    """mg_submit_packed / mg_wait_submitted (the batching server's pipelined
+    path): two submissions in flight on one engine, waited for in order,
+    give exactly mg_forward_packed's results; pageable buffers are refused."""
+    import torch
+    from alphazero_b200.engine import pack_states
+
+    _, sd = load_golden("b19c128x10_pert")
+    e = gpu_engine_factory(sd, "bf16", max_batch=256)
+    xs = [host_lib.random_positions(19, n, 60 + n, 250) for n in (256, 100, 7, 256)]
+    ref = [e.forward_packed(pack_states(x), len(x)) for x in xs]
+
+    def pinned(shape, dtype):
+        t = torch.empty(shape, dtype=dtype).pin_memory()
+        return t.numpy()
+
+    bufs = []
+    for x in xs:
+        b = pinned((len(x), e.words_per_position()), torch.int32).view(np.uint32)
+        b[:] = pack_states(x)
+        bufs.append((b, pinned((len(x), 362), torch.float32), pinned((len(x),), torch.float32)))
+    tickets = [e.submit_packed(bufs[0][0], len(xs[0]), bufs[0][1], bufs[0][2])]
+    for i in range(1, len(xs)):
+        tickets.append(e.submit_packed(bufs[i][0], len(xs[i]), bufs[i][1], bufs[i][2]))
+        e.wait_submitted(tickets[i - 1])  # at most two outstanding
+    e.wait_submitted(tickets[-1])
+    for (p0, v0, _), (_, p1, v1) in zip(ref, bufs):
+        assert np.array_equal(p0, p1) and np.array_equal(v0, v1)
+    with pytest.raises(RuntimeError):
+        e.submit_packed(pack_states(xs[2]), len(xs[2]), np.empty((7, 362), np.float32),
+                        np.empty((7,), np.float32))
