@@ -77,8 +77,24 @@ FastSearch::FastSearch(PackedEvaluator* evaluator, int board_size, const SearchP
     static_assert(std::is_trivially_destructible<Node>::value, "arena nodes are never destroyed");
     if ((size_t)actions_ * sizeof(Node) > kArenaBlockBytes)
         throw std::invalid_argument("FastSearch: arena block too small");
-    const int extra = std::max(1, params_.threads) - 1;
+    const int extra = params_.grouped ? 0 : std::max(1, params_.threads) - 1;
     arenas_.resize(extra + 1);
+    if (params_.grouped) {
+        const int t = std::max(1, params_.threads);
+        group_.paths.resize(t);
+        for (auto& p : group_.paths) p.reserve(64);
+        group_.leaves.resize(t);
+        group_.words.resize((size_t)t * words_);
+        group_.policy.resize((size_t)t * actions_);
+        group_.values.resize(t);
+        group_.legal.resize((size_t)t * actions_);
+        group_.word_ptrs.resize(t);
+        group_.policy_ptrs.resize(t);
+        for (int i = 0; i < t; ++i) {
+            group_.word_ptrs[i] = group_.words.data() + (size_t)i * words_;
+            group_.policy_ptrs[i] = group_.policy.data() + (size_t)i * actions_;
+        }
+    }
     for (int i = 0; i < extra; ++i) pool_.emplace_back(&FastSearch::worker_loop, this, i + 1);
 }
 
@@ -116,7 +132,7 @@ FastSearch::Node* FastSearch::select_child(Node* node) const {
 }
 
 // MCTS::mask_policy + MCTS::expand (src/mcts.cpp:43-73).
-void FastSearch::expand(Node* node, std::vector<float>& policy, const uint8_t* legal, Arena& arena) {
+void FastSearch::expand(Node* node, float* policy, const uint8_t* legal, Arena& arena) {
     float sum = 0.0f;
     int k = 0;
     for (int a = 0; a < actions_; ++a) {
@@ -232,7 +248,7 @@ void FastSearch::playouts_from_root(int tid) {
             g.encode_bits(words.data());
             evaluator_->evaluate_packed(words.data(), words_, policy.data(), &value);
             g.legal_mask(legal.data());
-            expand(node, policy, legal.data(), arena);
+            expand(node, policy.data(), legal.data(), arena);
             node->state.store(kExpanded, std::memory_order_release);
             backup(path, value);
             sims_done_.fetch_add(1, std::memory_order_relaxed);
@@ -245,6 +261,74 @@ void FastSearch::playouts_from_root(int tid) {
         std::lock_guard<std::mutex> lock(mu_);
         if (!error_) error_ = std::current_exception();
     }
+}
+
+// The params.threads concurrent playouts of MCTS::search as rounds on the
+// calling thread (SearchParams::grouped): the descent, collision rule,
+// terminal valuation, masking, expansion and backup of playouts_from_root,
+// with the leaves of a round evaluated as one group.
+void FastSearch::grouped_playouts() {
+    const int t = std::max(1, params_.threads);
+    const int target = params_.simulations;
+    Arena& arena = arenas_[0];
+    int done = 0;
+    while (done < target) {
+        int n = 0;
+        const int want = std::min(t, target - done);
+        while (n < want && done < target) {
+            std::vector<Node*>& path = group_.paths[n];
+            Node* node = root_;
+            GoPosition g = *pos_;
+            path.clear();
+            path.push_back(node);
+            node->vloss.fetch_add(1, std::memory_order_relaxed);
+            bool collision = false;
+            for (;;) {
+                const int st = node->state.load(std::memory_order_relaxed);
+                if (st == kExpanded) {
+                    Node* child = select_child(node);
+                    if (child == nullptr) break;
+                    child->vloss.fetch_add(1, std::memory_order_relaxed);
+                    path.push_back(child);
+                    g.play(child->action);
+                    node = child;
+                } else if (st == kExpanding) {
+                    collision = true;  // already a leaf of this round
+                    break;
+                } else {
+                    break;  // an unevaluated leaf
+                }
+            }
+            if (collision) {
+                revert(path);
+                break;  // the round is complete
+            }
+            if (g.over()) {
+                const float v = g.winner() == 0 ? 0.0f : (g.winner() == g.to_move() ? 1.0f : -1.0f);
+                backup(path, v);
+                ++done;
+                playouts_.fetch_add(1, std::memory_order_relaxed);
+                continue;
+            }
+            node->state.store(kExpanding, std::memory_order_relaxed);
+            g.encode_bits(group_.words.data() + (size_t)n * words_);
+            g.legal_mask(group_.legal.data() + (size_t)n * actions_);
+            group_.leaves[n] = node;
+            ++n;
+        }
+        if (n == 0) continue;
+        evaluator_->evaluate_packed_group(group_.word_ptrs.data(), n, words_, group_.policy_ptrs.data(),
+                                          group_.values.data());
+        for (int i = 0; i < n; ++i) {
+            expand(group_.leaves[i], group_.policy_ptrs[i], group_.legal.data() + (size_t)i * actions_,
+                   arena);
+            group_.leaves[i]->state.store(kExpanded, std::memory_order_relaxed);
+            backup(group_.paths[i], group_.values[i]);
+            ++done;
+            playouts_.fetch_add(1, std::memory_order_relaxed);
+        }
+    }
+    sims_done_.store(done, std::memory_order_relaxed);
 }
 
 void FastSearch::worker_loop(int tid) {
@@ -280,7 +364,7 @@ void FastSearch::search(const GoPosition& pos, std::vector<float>& visits, bool 
         pos.encode_bits(words.data());
         evaluator_->evaluate_packed(words.data(), words_, policy.data(), &value);
         pos.legal_mask(legal.data());
-        expand(root.get(), policy, legal.data(), arenas_[0]);
+        expand(root.get(), policy.data(), legal.data(), arenas_[0]);
         root->state.store(kExpanded, std::memory_order_release);
         root->visits.store(1, std::memory_order_relaxed);
         root->add_value(value);
@@ -289,6 +373,16 @@ void FastSearch::search(const GoPosition& pos, std::vector<float>& visits, bool 
     pos_ = &pos;
     root_ = root.get();
     sims_done_.store(0, std::memory_order_relaxed);
+    if (params_.grouped) {
+        grouped_playouts();
+        root_ = nullptr;
+        pos_ = nullptr;
+        visits.assign(actions_, 0.0f);
+        for (int i = 0; i < root->n_children; ++i)
+            visits[root->children[i].action] =
+                (float)root->children[i].visits.load(std::memory_order_relaxed);
+        return;
+    }
     {
         std::lock_guard<std::mutex> lock(mu_);
         finished_ = 0;

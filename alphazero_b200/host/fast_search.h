@@ -49,6 +49,15 @@ struct SearchParams {
     float dirichlet_alpha = 0.03f;  // Config::dirichlet_alpha
     float dirichlet_epsilon = 0.25f;
     int threads = 16;               // Config::num_search_threads
+    // false: `threads` search threads (a pool), as the reference runs them.
+    // true: the same number of concurrent playouts as one group on the
+    // calling thread: each round selects up to `threads` leaves with virtual
+    // loss (a leaf already in the round ends the round early), evaluates
+    // them through one evaluate_packed_group call, then expands them and
+    // backs them up.  The arithmetic is the same; what changes is that a
+    // round's playouts start together, and the host pays one sleep and one
+    // wake-up per round instead of one per playout.
+    bool grouped = false;
 };
 
 class FastSearch {
@@ -84,8 +93,9 @@ private:
 
     void worker_loop(int tid);
     void playouts_from_root(int tid);
+    void grouped_playouts();
     Node* select_child(Node* node) const;
-    void expand(Node* node, std::vector<float>& policy, const uint8_t* legal, Arena& arena);
+    void expand(Node* node, float* policy, const uint8_t* legal, Arena& arena);
     void backup(std::vector<Node*>& path, float value);
     static void revert(std::vector<Node*>& path);
     void add_dirichlet_noise(Node* root);
@@ -109,6 +119,17 @@ private:
     std::exception_ptr error_;  // first evaluation failure of the current search
     std::vector<Arena> arenas_;  // [0] the caller's thread, [1 + i] pool thread i
     std::vector<std::thread> pool_;
+
+    // Per-member storage of a grouped round (grouped mode only).
+    struct Group {
+        std::vector<std::vector<Node*>> paths;
+        std::vector<Node*> leaves;
+        std::vector<uint32_t> words;
+        std::vector<float> policy, values;
+        std::vector<uint8_t> legal;
+        std::vector<const uint32_t*> word_ptrs;
+        std::vector<float*> policy_ptrs;
+    } group_;
 };
 
 }  // namespace mgb

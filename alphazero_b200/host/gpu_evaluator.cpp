@@ -123,6 +123,49 @@ void GpuEvaluator::evaluate_packed(const uint32_t* words, int n_words, float* po
     *value = buf.value;
 }
 
+void GpuEvaluator::evaluate_packed_group(const uint32_t* const* words, int n, int n_words,
+                                         float* const* policies, float* values) {
+    if (cuda_ == nullptr) throw std::logic_error("evaluate_packed_group needs a CudaEngine");
+    if (n <= 0) return;
+    const int size = cuda_->input_channels * cuda_->board_size * cuda_->board_size;
+    if (n_words != (size + 31) / 32)
+        throw std::invalid_argument("packed state has " + std::to_string(n_words) + " words, expected " +
+                                    std::to_string((size + 31) / 32));
+    // One buffer per group member, kept per client thread.
+    thread_local std::vector<std::unique_ptr<NNResultBuf>> bufs;
+    thread_local std::vector<Pending> items;
+    while ((int)bufs.size() < n) bufs.push_back(std::make_unique<NNResultBuf>());
+    items.resize(n);
+    for (int i = 0; i < n; ++i) {
+        NNResultBuf& b = *bufs[i];
+        b.done = false;
+        b.state_data = nullptr;
+        b.state_size = size;
+        items[i] = {&b, words[i]};
+    }
+    enqueue(items.data(), (size_t)n);
+    bool failed = false;
+    for (int i = 0; i < n; ++i) {
+        NNResultBuf& b = *bufs[i];
+        {
+            // Usually only the first wait sleeps: the group is served by one
+            // or two batches.
+            std::unique_lock<std::mutex> lock(b.mu);
+            b.cv.wait(lock, [&] { return b.done; });
+        }
+        if (b.policy.empty()) {
+            failed = true;
+            continue;
+        }
+        std::copy(b.policy.begin(), b.policy.end(), policies[i]);
+        values[i] = b.value;
+    }
+    if (failed) {
+        std::lock_guard<std::mutex> lock(mu_);
+        throw std::runtime_error("batched evaluation failed: " + last_error_);
+    }
+}
+
 BatchEvaluator::Result GpuEvaluator::evaluate_single(const std::vector<float>& state) {
     NNResultBuf buf;
     return evaluate_with_buf(buf, state);
@@ -425,6 +468,11 @@ BatchEvaluator::Result ShardedEvaluator::evaluate_with_buf(NNResultBuf& buf,
 
 void ShardedEvaluator::evaluate_packed(const uint32_t* words, int n_words, float* policy, float* value) {
     shards_[shard_of_this_thread()]->evaluate_packed(words, n_words, policy, value);
+}
+
+void ShardedEvaluator::evaluate_packed_group(const uint32_t* const* words, int n, int n_words,
+                                             float* const* policies, float* values) {
+    shards_[shard_of_this_thread()]->evaluate_packed_group(words, n, n_words, policies, values);
 }
 
 BatchEvaluator::Result ShardedEvaluator::evaluate_single(const std::vector<float>& state) {

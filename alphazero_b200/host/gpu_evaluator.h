@@ -75,6 +75,10 @@ public:
     // A position already in the bit-packed wire format (CudaEngine only):
     // queued like evaluate_with_buf, with no fp32 planes at all.
     void evaluate_packed(const uint32_t* words, int n_words, float* policy, float* value) override;
+    // A group of packed positions queued together (one lock, one wake-up of
+    // the server); the calling thread sleeps once for the whole group.
+    void evaluate_packed_group(const uint32_t* const* words, int n, int n_words,
+                               float* const* policies, float* values) override;
 
     // Counters (for batching statistics and tests).
     uint64_t batches() const { return batches_.load(); }
@@ -172,6 +176,8 @@ public:
     Result evaluate_with_buf(NNResultBuf& buf, const std::vector<float>& state) override;
     Result evaluate_single(const std::vector<float>& state) override;
     void evaluate_packed(const uint32_t* words, int n_words, float* policy, float* value) override;
+    void evaluate_packed_group(const uint32_t* const* words, int n, int n_words,
+                               float* const* policies, float* values) override;
 
     size_t shards() const { return shards_.size(); }
     GpuEvaluator& shard(size_t i) { return *shards_[i]; }

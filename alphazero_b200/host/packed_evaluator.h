@@ -18,6 +18,15 @@ public:
     // value.  Throws std::runtime_error if the evaluation failed.
     virtual void evaluate_packed(const uint32_t* words, int n_words, float* policy,
                                  float* value) = 0;
+
+    // Evaluates n positions (words[i], n_words words each) as one group and
+    // blocks until every one is done: policies[i] receives position i's
+    // probabilities, values[i] its value.  Throws std::runtime_error if an
+    // evaluation failed.  The default evaluates them one after another.
+    virtual void evaluate_packed_group(const uint32_t* const* words, int n, int n_words,
+                                       float* const* policies, float* values) {
+        for (int i = 0; i < n; ++i) evaluate_packed(words[i], n_words, policies[i], &values[i]);
+    }
 };
 
 }  // namespace mgb

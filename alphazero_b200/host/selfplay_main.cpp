@@ -11,11 +11,14 @@
 //   selfplay_cuda --model M.onnx [--gpus N] [--workers 64] [--search-threads 16]
 //                 [--sims 800] [--max-batch 512] [--warmup-seconds 10]
 //                 [--seconds 30] [--precision bf16|fp16|fp32]
-//                 [--servers-per-gpu K] [--search reference|fast]
+//                 [--servers-per-gpu K] [--search reference|fast|grouped]
 //
 // --search fast replaces the reference's search with FastSearch
 // (fast_search.h: the same algorithm at a lower host cost per visit, boards
-// encoded straight to the bit-packed wire format).
+// encoded straight to the bit-packed wire format).  --search grouped runs
+// FastSearch's grouped mode: each game worker's search-threads concurrent
+// playouts as rounds on the worker's own thread, a round's leaves evaluated
+// as one group (SearchParams::grouped).
 //
 //   selfplay_cuda --model M.onnx --search fast --games N [--records DIR] ...
 //
@@ -52,7 +55,7 @@ int main(int argc, char** argv) {
     int gpus = 1, workers = 64, search_threads = 16, sims = 800, max_batch = 512, per_gpu = 1;
     double warmup_s = 10.0, measure_s = 30.0;
     CudaEngine::Precision prec = CudaEngine::kBf16;
-    bool fast = false;
+    bool fast = false, grouped = false;
     int games = 0;
     std::string records_dir;
     for (int i = 1; i < argc; ++i) {
@@ -75,11 +78,12 @@ int main(int argc, char** argv) {
         else if (a == "--records") records_dir = next();
         else if (a == "--search") {
             const std::string v = next();
-            if (v != "fast" && v != "reference") {
-                std::fprintf(stderr, "--search takes reference or fast\n");
+            if (v != "fast" && v != "reference" && v != "grouped") {
+                std::fprintf(stderr, "--search takes reference, fast or grouped\n");
                 return 2;
             }
-            fast = v == "fast";
+            fast = v != "reference";
+            grouped = v == "grouped";
         }
         else if (a == "--warmup-seconds") warmup_s = std::atof(next());
         else if (a == "--seconds") measure_s = std::atof(next());
@@ -141,6 +145,7 @@ int main(int argc, char** argv) {
             sp.dirichlet_alpha = config.dirichlet_alpha;
             sp.dirichlet_epsilon = config.dirichlet_epsilon;
             sp.threads = search_threads;
+            sp.grouped = grouped;
             std::atomic<int> next_game{0};
             std::atomic<uint64_t> moves{0}, records{0};
             const auto t0 = std::chrono::steady_clock::now();
@@ -180,6 +185,7 @@ int main(int argc, char** argv) {
             fp.search.dirichlet_alpha = config.dirichlet_alpha;
             fp.search.dirichlet_epsilon = config.dirichlet_epsilon;
             fp.search.threads = search_threads;
+            fp.search.grouped = grouped;
             w = mgb_selfplay::run_fast(&evaluator, fp, workers, warmup_s, measure_s, nn);
         } else {
             w = mgb_selfplay::run(&evaluator, config, workers, warmup_s, measure_s, nn);
@@ -198,7 +204,7 @@ int main(int argc, char** argv) {
             "\"host_threads\": %u, \"failed_batches\": %llu, \"gpu_launches\": %llu, "
             "\"server_engine_frac\": %.3f, \"server_pack_frac\": %.3f, \"server_scatter_frac\": %.3f}\n",
             moves * sims / w.seconds, pos / w.seconds, moves / w.seconds, bat > 0 ? pos / bat : 0.0,
-            w.seconds, moves, (unsigned long long)(w.end.games - w.begin.games), fast ? "fast" : "reference",
+            w.seconds, moves, (unsigned long long)(w.end.games - w.begin.games), grouped ? "grouped" : (fast ? "fast" : "reference"),
             gpus, per_gpu, workers,
             search_threads, sims, max_batch, config.board_size, config.num_filters,
             config.num_res_blocks, std::thread::hardware_concurrency(),

@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                     [--workload b19c128x10_bs512|b19c256x20_bs1024|b9c128x10_bs256|b9c64x6_bs16
-                                |selfplay_b19c128x10|selfplay_b19c128x10_fast]
+                                |selfplay_b19c128x10|selfplay_b19c128x10_fast|selfplay_b19c128x10_grouped]
 
 A step is one forward pass of the network over one batch of seeded random-
 playout positions.  Under torchrun each rank drives its own GPU with its own
@@ -30,9 +30,9 @@ JSON line.  Numbers:
              quoted on), 9x9 b10c128 batch 256 and 9x9 b6c64 batch 16;
   selfplay   (every N, default workload only) end-to-end self-play MCTS
              visits/s over all N GPUs after the per-rank engines are closed:
-             rank 0 runs alphazero_b200/lib/selfplay_cuda with FastSearch and
-             with the reference's own search (the selfplay_b19c128x10*
-             workloads below) for a bounded window each.
+             rank 0 runs alphazero_b200/lib/selfplay_cuda with FastSearch
+             (threaded and grouped) and with the reference's own search (the
+             selfplay_b19c128x10* workloads below) for a bounded window each.
 --impl reference times that CPU implementation alone as the reference arm.
 
 selfplay_b19c128x10 is end-to-end self-play instead: the reference's own
@@ -40,7 +40,10 @@ search (src/mcts.cpp, compiled unmodified) with 64 game workers x 16 search
 threads, 800 simulations per move, max batch 512, over one batching server
 and engine per GPU (alphazero_b200/lib/selfplay_cuda); selfplay_b19c128x10_fast
 is the same with FastSearch (alphazero_b200/host/fast_search.h, the
-reference's algorithm at a lower host cost per visit).  One process drives
+reference's algorithm at a lower host cost per visit), and
+selfplay_b19c128x10_grouped with FastSearch's grouped mode (each worker's 16
+concurrent playouts as rounds on its own thread, a round's leaves evaluated
+as one group: one sleep and wake-up per round instead of per playout).  One process drives
 all N GPUs (under torchrun rank 0 runs it, the other ranks wait).  A step is
 one second of the measured window (at least 10), a warm-up step two seconds
 (at least 6).  value = MCTS visits/s = searches completed in the window x 800
@@ -80,11 +83,15 @@ SELFPLAY_WORKLOADS = {
     #        simulations per move, max batch per evaluator)
     "selfplay_b19c128x10": (19, 128, 10, 64, 16, 800, 512),
     "selfplay_b19c128x10_fast": (19, 128, 10, 64, 16, 800, 512),
+    "selfplay_b19c128x10_grouped": (19, 128, 10, 64, 16, 800, 512),
 }
 
 
 def selfplay_search(wl):
-    return "fast" if wl.endswith("_fast") else "reference"
+    for s in ("fast", "grouped"):
+        if wl.endswith("_" + s):
+            return s
+    return "reference"
 DEFAULT_WORKLOAD = "b19c128x10_bs512"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
@@ -509,7 +516,8 @@ def selfplay_records(world, args):
     recs = {}
     with tempfile.TemporaryDirectory(prefix="mgb_selfplay_") as tmp:
         model = selfplay_model("selfplay_b19c128x10", tmp)
-        for search, wl in (("fast", "selfplay_b19c128x10_fast"), ("reference", "selfplay_b19c128x10")):
+        for search, wl in (("fast", "selfplay_b19c128x10_fast"), ("grouped", "selfplay_b19c128x10_grouped"),
+                           ("reference", "selfplay_b19c128x10")):
             with ClockSampler(0) as clocks:
                 out = run_selfplay_binary(build.SELFPLAY_BIN, model, wl, args, world, search=search,
                                           window=(args.selfplay_warmup, args.selfplay_seconds))
@@ -566,8 +574,12 @@ def selfplay_config(wl):
                         f"{threads} search threads, {sims} simulations per move, max batch {max_batch}",
             "board": board, "filters": filters, "blocks": blocks, "workers": workers,
             "search_threads": threads, "simulations": sims, "max_batch": max_batch,
-            "search": ("FastSearch (the reference's MCTS algorithm, own implementation)"
-                       if selfplay_search(wl) == "fast" else "reference src/mcts.cpp compiled unmodified"),
+            "search": {"fast": "FastSearch (the reference's MCTS algorithm, own implementation; "
+                               f"{threads} search threads per game worker)",
+                       "grouped": "FastSearch, grouped mode (the reference's MCTS algorithm; each "
+                                  f"worker's {threads} concurrent playouts as rounds on its own "
+                                  "thread, a round's leaves evaluated as one group)",
+                       "reference": "reference src/mcts.cpp compiled unmodified"}[selfplay_search(wl)],
             "weights": "seeded random init (export_onnx --init distributions)",
             "parallelism": "one batching server + engine per GPU, search threads round-robin, "
                            "weights replicated, no collective"}
@@ -619,7 +631,8 @@ def run_selfplay(args, wl):
     if rank == 0:
         metric = (f"MCTS visits/sec (self-play {board}x{board} b{blocks}c{filters}, {workers} workers x "
                   f"{threads} search threads, {sims} sims"
-                  + (", FastSearch)" if selfplay_search(wl) == "fast" else ")"))
+                  + {"fast": ", FastSearch)", "grouped": ", FastSearch grouped)",
+                     "reference": ")"}[selfplay_search(wl)])
         if args.impl == "reference":
             out, why = oracle_selfplay(wl, args)
             if out is None:

@@ -10,7 +10,11 @@
 //      children hold between sims and sims + 7 visits) over repeated
 //      searches;
 //   4. an evaluation failure surfaces as an exception from search() and the
-//      searcher keeps working.
+//      searcher keeps working;
+//   5. the grouped mode (the playouts of a round evaluated as one group on
+//      the calling thread): with one playout per round it visits exactly
+//      what the reference's single-threaded search does; with 16 it
+//      completes exactly the requested playouts; failures surface as in 4.
 // Exit code 0 = pass.
 #include "fast_search.h"
 #include "go_positions.h"
@@ -137,7 +141,7 @@ void check_rules(int board, int games, uint32_t seed) {
     }
 }
 
-void check_search_parity(int board, int sims, uint32_t seed) {
+void check_search_parity(int board, int sims, uint32_t seed, bool grouped = false) {
     const int actions = board * board + 1;
     std::mt19937 rng(seed);
     FakeBatch ref_eval(actions);
@@ -150,6 +154,7 @@ void check_search_parity(int board, int sims, uint32_t seed) {
     mgb::SearchParams sp;
     sp.simulations = sims;
     sp.threads = 1;
+    sp.grouped = grouped;
     mgb::FastSearch fast(&fast_eval, board, sp, 7);
     minigo::GoGame ref(board, 7.5f);
     mgb::GoPosition pos(board, 7.5f);
@@ -180,12 +185,13 @@ void check_search_parity(int board, int sims, uint32_t seed) {
     CHECK(compared > 0);
 }
 
-void check_pool(int board, int sims, int threads) {
+void check_pool(int board, int sims, int threads, bool grouped = false) {
     FakePacked ev(board);
     ev.delay_us = 20;
     mgb::SearchParams sp;
     sp.simulations = sims;
     sp.threads = threads;
+    sp.grouped = grouped;
     mgb::FastSearch fast(&ev, board, sp, 11);
     mgb::GoPosition pos(board, 7.5f);
     for (int m = 0; m < 6; ++m) {
@@ -193,18 +199,20 @@ void check_pool(int board, int sims, int threads) {
         fast.search(pos, visits, true);
         double total = 0;
         for (float v : visits) total += v;
-        CHECK(total >= sims && total <= sims + threads - 1);
+        if (grouped) CHECK(total == sims);  // a round never overshoots
+        else CHECK(total >= sims && total <= sims + threads - 1);
         const int a = fast.get_action(pos, pi, 1.0f, true);
         CHECK(a >= 0 && a <= board * board && pos.legal(a));
         pos.play(a);
     }
 }
 
-void check_failure(int board) {
+void check_failure(int board, bool grouped = false) {
     FakePacked ev(board, 40);
     mgb::SearchParams sp;
     sp.simulations = 100;
     sp.threads = 4;
+    sp.grouped = grouped;
     mgb::FastSearch fast(&ev, board, sp, 3);
     mgb::GoPosition pos(board, 7.5f);
     std::vector<float> visits;
@@ -235,6 +243,12 @@ int main() {
     std::printf("pool ok\n");
     check_failure(9);
     std::printf("failure ok\n");
+    check_search_parity(9, 300, 5, true);
+    check_search_parity(19, 200, 6, true);
+    check_pool(9, 400, 16, true);
+    check_pool(19, 300, 16, true);
+    check_failure(9, true);
+    std::printf("grouped ok\n");
     std::printf("fast search tests passed\n");
     return 0;
 }
