@@ -91,6 +91,7 @@ struct mg_engine {
     int tc_trunk = 0;
     int withhold_cta = -1;  // test hook (MG_TEST_WITHHOLD_PROGRESS): see launch_trunk_pix
     bool use_graphs = true;
+    int l2_policy = 1;  // keep the residual lo plane resident in L2 (MG_L2_POLICY=0: off)
     cudaStream_t stream = nullptr;
     std::string err;
 
@@ -423,6 +424,43 @@ struct mg_engine {
            "cudaMallocHost(history)");
         alloc_batch = max_batch;
         alloc_elem = elem;
+        if (l2_policy != 0 && precision != MG_PREC_FP32) apply_l2_policy(rows * cpad * 2);
+    }
+
+    // The 16-bit paths' residual lo plane (in d_x's storage) is written by
+    // one block's conv2 and read back by the next block's, two layers later;
+    // the activations streamed in between (t and the hi plane) exceed the
+    // 126 MB L2 and evict it.  An L2 access-policy window on the engine's
+    // stream marks it persisting, in a set-aside of the L2 for persisting
+    // lines (a limit of this process's CUDA context, released with it).
+    // Measured at 19x19, 128 filters, batch 512: trunk 1015 -> 994 us.  Only
+    // when the whole plane fits the set-aside: a window persisting 82 MB of
+    // the 20-block 256-filter net's 210 MB plane at batch 1024 made its trunk
+    // 26% slower.  Graphs captured on the stream keep the window in their
+    // kernel nodes.
+    void apply_l2_policy(size_t lo_bytes) {
+        int max_persist = 0, max_window = 0;
+        if (cudaDeviceGetAttribute(&max_persist, cudaDevAttrMaxPersistingL2CacheSize, device) !=
+                cudaSuccess ||
+            cudaDeviceGetAttribute(&max_window, cudaDevAttrMaxAccessPolicyWindowSize, device) !=
+                cudaSuccess ||
+            max_persist <= 0 || max_window <= 0) {
+            cudaGetLastError();
+            return;  // no persisting L2 on this device: nothing to do
+        }
+        if (lo_bytes > (size_t)max_persist || lo_bytes > (size_t)max_window) return;
+        const size_t window = std::min(lo_bytes, (size_t)max_window);
+        const size_t set_aside = std::min(window, (size_t)max_persist);
+        ck(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, set_aside),
+           "cudaDeviceSetLimit(persisting L2)");
+        cudaStreamAttrValue attr = {};
+        attr.accessPolicyWindow.base_ptr = d_x;
+        attr.accessPolicyWindow.num_bytes = window;
+        attr.accessPolicyWindow.hitRatio = (float)((double)set_aside / (double)window);
+        attr.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
+        attr.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
+        ck(cudaStreamSetAttribute(stream, cudaStreamAttributeAccessPolicyWindow, &attr),
+           "cudaStreamSetAttribute(access policy window)");
     }
 
     int bucket_for(int n) const {
@@ -766,6 +804,7 @@ mg_engine* mg_create(int device, int flags) {
     }
     if (const char* s = std::getenv("MG_CONV_BN")) e->conv_bn_override = std::atoi(s);
     if (const char* s = std::getenv("MG_NO_GRAPHS")) e->use_graphs = std::atoi(s) == 0;
+    if (const char* s = std::getenv("MG_L2_POLICY")) e->l2_policy = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX")) e->pix_mode = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_NPX")) e->pix_npx = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_TRUNK")) e->pix_trunk = std::atoi(s);
