@@ -140,19 +140,6 @@ __device__ __forceinline__ Geo geo_of(const PixArgs& a) {
 }
 
 template <bool FP16>
-__device__ __forceinline__ uint16_t to16(float v);
-template <>
-__device__ __forceinline__ uint16_t to16<false>(float v) {
-    __nv_bfloat16 h = __float2bfloat16_rn(v);
-    return *reinterpret_cast<uint16_t*>(&h);
-}
-template <>
-__device__ __forceinline__ uint16_t to16<true>(float v) {
-    __half h = __float2half_rn(v);
-    return *reinterpret_cast<uint16_t*>(&h);
-}
-
-template <bool FP16>
 __device__ __forceinline__ float from16(uint16_t h);
 template <>
 __device__ __forceinline__ float from16<false>(uint16_t h) {
@@ -180,7 +167,6 @@ __device__ __forceinline__ uint32_t lo_bits2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 __device__ __forceinline__ float lo_value(uint16_t l) { return __half2float(__ushort_as_half(l)); }
-__device__ __forceinline__ uint16_t lo_bits(float r) { return __half_as_ushort(__float2half_rn(r)); }
 
 // The lo plane is read and written only by the epilogue, one channel per
 // lane and 16 pixels at a time, so it is stored in 16-pixel blocks:
@@ -227,7 +213,6 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
     // store or wait).
     const uint16_t* const res_hi = a.layer[l].res_hi;
     const uint16_t* const res_lo = a.layer[l].res_lo;
-    uint16_t* const out16 = a.layer[l].out16;
     uint16_t* const out_lo = a.layer[l].out_lo;
     const float bias = a.layer[l].bias[co];
     const bool has_res = res_hi != nullptr;
