@@ -108,6 +108,7 @@ struct PixArgs {
     int nbuf;                     // TMEM accumulator buffers, npx columns each
     uint64_t is_magic, rs_magic;  // ceil(2^40 / is), ceil(2^40 / rs)
     int n_layers;
+    int own_frames;      // 1: CTA ranges are whole frames; a tile waits only on its own CTA
     int* err;
     unsigned* progress;  // [grid] tiles finished per CTA (several layers), else nullptr
     int withhold_cta;    // test hook: this CTA never publishes its progress (-1: none)
@@ -124,6 +125,23 @@ struct Geo {
     int m_total, span, npx, rs, is, board, nbuf;
     uint64_t is_magic, rs_magic;
 };
+
+// The rows of the previous layer a tile reads, as wait_inputs takes them.
+// With CTA ranges of whole frames (own_frames), only the CTA's own rows: the
+// halo rows past either end of its range are either zero padding rows of a
+// neighbouring frame (the frame stride is padded to whole 16-row chunks, and
+// every layer writes frame rows as zero) or inputs of frame pixels, whose
+// outputs are masked to zero whatever they read.
+__device__ __forceinline__ bool wait_tile_inputs(const Geo& G, const PixArgs& a, int l, int m0,
+                                                 int len, int halo) {
+    if (!a.own_frames) return wait_inputs(G, a.progress, a.err, l, m0, len, halo);
+    // Tiles of whole frames read no other tile's rows at all.
+    if (G.npx % G.is == 0) halo = 0;
+    const int start = blockIdx.x * G.span;
+    const int end = min(start + G.span, G.m_total);
+    const int lo = max(m0 - halo, start), hi = min(m0 + len + halo, end);
+    return wait_inputs(G, a.progress, a.err, l, lo, hi - lo, 0);
+}
 
 __device__ __forceinline__ Geo geo_of(const PixArgs& a) {
     Geo g;
@@ -544,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int m0, len;
                     tile_rows(G, blockIdx.x, tile_at(blockIdx.x, q, nt), m0, len);
                     if (l > 0 && a.progress != nullptr) {
-                        if (!wait_inputs(G, a.progress, err, l, m0, len, halo)) {
+                        if (!wait_tile_inputs(G, a, l, m0, len, halo)) {
                             ok = false;
                             break;
                         }
@@ -717,16 +735,25 @@ bool layer_ok(const ConvLayer& L, const ConvLayer& first) {
 // any supported cin; layers 1.. must have cin 128 and weights laid out back
 // to back from layers[1].weight.  With several layers, progress must point
 // at grid_limit counters.
+// Whether CTA ranges can be whole frames: frames of whole 16-row chunks that
+// fit one tile.
+bool frames_fit(const FrameGeom& g, int m_total) {
+    return g.is % kChunk == 0 && g.is <= kMaxPx && m_total % g.is == 0;
+}
+
 cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16, int grid_limit,
-                          unsigned* progress, cudaStream_t stream, int withhold_cta = -1) {
+                          unsigned* progress, cudaStream_t stream, int withhold_cta = -1,
+                          bool own_frames = false) {
     if (n < 1 || n > kMaxLayers || (n > 1 && progress == nullptr)) return cudaErrorInvalidValue;
     const ConvLayer& F = layers[0];
-    // Balanced ranges: each CTA takes span pixels (a multiple of 16) cut into
-    // equal tiles of at most max_npx.
-    const int units = (F.m_total + 15) / 16;
+    if (own_frames && !frames_fit(F.g, F.m_total)) return cudaErrorInvalidValue;
+    // Balanced ranges: each CTA takes span pixels (a multiple of 16, or of
+    // whole frames) cut into equal tiles of at most max_npx.
+    const int unit = own_frames ? F.g.is : 16;
+    const int units = (F.m_total + unit - 1) / unit;
     int grid = units < grid_limit ? units : grid_limit;
     if (grid < 1) grid = 1;
-    const int span = (((F.m_total + grid - 1) / grid) + 15) / 16 * 16;
+    const int span = (units + grid - 1) / grid * unit;
     grid = (F.m_total + span - 1) / span;
     const int tiles = (span + max_npx - 1) / max_npx;
     const int npx = ((span + tiles - 1) / tiles + 15) / 16 * 16;
@@ -746,6 +773,7 @@ cudaError_t launch_layers(const ConvLayer* layers, int n, int max_npx, bool fp16
     a.is_magic = ((1ull << kMagicShift) + (uint64_t)F.g.is - 1) / (uint64_t)F.g.is;
     a.rs_magic = ((1ull << kMagicShift) + (uint64_t)F.g.rs - 1) / (uint64_t)F.g.rs;
     a.n_layers = n;
+    a.own_frames = own_frames ? 1 : 0;
     a.err = F.err;
     a.progress = n > 1 ? progress : nullptr;
     a.withhold_cta = n > 1 ? withhold_cta : -1;
@@ -876,8 +904,10 @@ bool trunk_in_one_launch(int m_total, int max_npx, int grid_limit, int min_tiles
 
 }  // namespace
 
-int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit, int min_tiles) {
+int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit, int min_tiles,
+                       bool own_frames) {
     if (n <= 0) return 0;
+    if (own_frames) return (n + kMaxLayers - 1) / kMaxLayers;
     if (!trunk_in_one_launch(m_total, max_npx, grid_limit, min_tiles)) return n;
     return (n + kMaxLayers - 1) / kMaxLayers;
 }
@@ -905,7 +935,19 @@ cudaError_t launch_conv_pix(const ConvLayer& L, int max_npx, bool fp16, int grid
 
 cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool fp16,
                              int grid_limit, unsigned* progress, cudaStream_t stream,
-                             int withhold_cta, int min_tiles) {
+                             int withhold_cta, int min_tiles, bool own_frames) {
+    // CTA ranges of whole frames: no tile waits on another CTA, so the
+    // layers run as one launch whatever the batch (each CTA goes through
+    // them at its own pace).
+    if (own_frames && n > 0 && frames_fit(layers[0].g, layers[0].m_total)) {
+        for (int l0 = 0; l0 < n; l0 += kMaxLayers) {
+            const int cnt = n - l0 < kMaxLayers ? n - l0 : kMaxLayers;
+            cudaError_t e = launch_layers(layers + l0, cnt, max_npx, fp16, grid_limit,
+                                          cnt > 1 ? progress : nullptr, stream, withhold_cta, true);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
     // With few tiles per CTA a tile of the next layer depends on most of the
     // CTA's range and its neighbours' of the layer before, so one launch per
     // layer (programmatic dependent launches) is faster than the cross-CTA

@@ -89,6 +89,14 @@ struct mg_engine {
     // 1024: equal within noise; 9x9 b6c64 batch 16, one tile per CTA: 7%
     // slower, the cross-CTA publish and poll cost more than a launch).
     int tc_trunk = 0;
+    // 1: on boards whose frame fits one tile of the 128-channel kernel, pad
+    // the frame stride to whole 16-row chunks and run the trunk as one
+    // launch of CTAs that own whole frames (MG_FRAME_TRUNK=1).  Off by
+    // default: bit-identical, and measured no faster at 9x9 batch 256
+    // (trunk 250 us either way; 255 us with one frame per tile), where each
+    // layer is bound by streaming its 288 KB of weights per tile through the
+    // 4-stage ring, not by the launches or the cross-CTA waits it removes.
+    int frame_trunk = 0;
     int withhold_cta = -1;  // test hook (MG_TEST_WITHHOLD_PROGRESS): see launch_trunk_pix
     bool use_graphs = true;
     int l2_policy = 1;  // keep the residual lo plane resident in L2 (MG_L2_POLICY=0: off)
@@ -238,10 +246,11 @@ struct mg_engine {
         free_weights();
         free_buffers();
         net = std::move(n);
-        g = make_frame(net.board);
         hw = net.board * net.board;
         planes = net.input_channels;
         cpad = round_up(net.filters, 64);
+        g = make_frame(net.board);
+        if (frame_trunk != 0 && cpad == 128 && g.is <= 256) g = make_frame(net.board, 16);
         actions = net.actions;
         n_convs = 1 + 2 * net.blocks;
 
@@ -396,6 +405,12 @@ struct mg_engine {
         d_x = dalloc<float>(rows * cpad, "cudaMalloc(act x)");
         d_x16 = dalloc<uint16_t>(rows * cpad, "cudaMalloc(act x16)");
         d_t = dalloc<uint8_t>(rows * cpad * elem, "cudaMalloc(act t)");
+        // Frame rows start out zero (every layer keeps them so); the
+        // whole-frame trunk schedule reads other CTAs' frame rows unordered.
+        ck(cudaMemset(d_stage, 0, rows * kStagedChannels * elem), "cudaMemset(stage)");
+        ck(cudaMemset(d_x, 0, rows * cpad * sizeof(float)), "cudaMemset(act x)");
+        ck(cudaMemset(d_x16, 0, rows * cpad * 2), "cudaMemset(act x16)");
+        ck(cudaMemset(d_t, 0, rows * cpad * elem), "cudaMemset(act t)");
         d_feat = dalloc<float>((size_t)max_batch * 3 * hw, "cudaMalloc(feat)");
         d_fc = dalloc<float>((size_t)kHeadsFcSplits * max_batch * (actions + net.hidden),
                              "cudaMalloc(fc)");
@@ -608,6 +623,10 @@ struct mg_engine {
                 "the bf16/fp16 modes support networks of up to 256 filters; use fp32");
     }
 
+    // Whether the 128-channel trunk's CTAs own whole frames (frame stride of
+    // whole 16-row chunks, one frame per tile at most).
+    bool own_frames() const { return frame_trunk != 0 && g.is % 16 == 0 && g.is <= 256; }
+
     // Whether the 64/256-channel 16-bit trunk runs as persistent launches
     // (one tile spans every output channel).
     bool use_tc_trunk() const {
@@ -623,7 +642,7 @@ struct mg_engine {
             for (int li = 0; li < n_convs; ++li) layers[li] = layer_desc(li, bucket);
             ck(launch_trunk_pix(layers.data(), n_convs, choose_npx(bucket * g.is),
                                 precision == MG_PREC_FP16, num_sms, d_progress, stream,
-                                withhold_cta, pix_trunk_min_tiles),
+                                withhold_cta, pix_trunk_min_tiles, own_frames()),
                "conv3x3_pix trunk launch");
         } else if (use_tc_trunk()) {
             std::vector<ConvLayer> layers(n_convs);
@@ -645,7 +664,7 @@ struct mg_engine {
     int trunk_launches(int bucket) const {
         if (use_pix() && pix_trunk)
             return trunk_pix_launches(bucket * g.is, n_convs, choose_npx(bucket * g.is), num_sms,
-                                      pix_trunk_min_tiles);
+                                      pix_trunk_min_tiles, own_frames());
         if (use_tc_trunk()) return (n_convs + trunk_tc_max_layers() - 1) / trunk_tc_max_layers();
         return n_convs;
     }
@@ -809,6 +828,7 @@ mg_engine* mg_create(int device, int flags) {
     if (const char* s = std::getenv("MG_PIX_NPX")) e->pix_npx = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_TRUNK")) e->pix_trunk = std::atoi(s);
     if (const char* s = std::getenv("MG_TC_TRUNK")) e->tc_trunk = std::atoi(s);
+    if (const char* s = std::getenv("MG_FRAME_TRUNK")) e->frame_trunk = std::atoi(s);
     if (const char* s = std::getenv("MG_PIX_TRUNK_MIN_TILES"))
         e->pix_trunk_min_tiles = std::max(1, std::atoi(s));
     if (const char* s = std::getenv("MG_TEST_WITHHOLD_PROGRESS")) e->withhold_cta = std::atoi(s);

@@ -3,7 +3,7 @@
 // Activation layout ("framed NHWC"): a batch of positions on a board of side
 // B is stored as rows of channel vectors, one row per pixel of a
 // (B+1) x (B+1) frame per position: row = n*IS + y*RS + x with RS = B + 1,
-// IS = RS * RS.  Column x = B and row y = B of every frame are zero, so the
+// IS = RS * RS, or more (rows past RS * RS are zero padding).  Column x = B and row y = B of every frame are zero, so the
 // 3x3 neighbour (y+dy, x+dx) of any board pixel is the row
 // row + dy*RS + dx and reads zero whenever it falls off the board (the
 // zero padding of src/eigen_engine.cpp:139-168); the rows before the first
@@ -23,11 +23,14 @@ struct FrameGeom {
     int is;     // (B + 1)^2
 };
 
-inline FrameGeom make_frame(int board) {
+// pad_to > 1: the frame stride rounded up to a multiple of pad_to rows; the
+// extra rows at the end of each frame are frame pixels (zero) like the
+// frame's last row and column.
+inline FrameGeom make_frame(int board, int pad_to = 1) {
     FrameGeom g;
     g.board = board;
     g.rs = board + 1;
-    g.is = (board + 1) * (board + 1);
+    g.is = ((board + 1) * (board + 1) + pad_to - 1) / pad_to * pad_to;
     return g;
 }
 
@@ -122,15 +125,19 @@ cudaError_t configure_conv_pix();
 // stored.  Layers 1..n-1 must have cin 128 and their weights back to back
 // from layers[1].weight; progress points at grid_limit counters of scratch.
 // When CTAs get fewer than min_tiles tiles the layers go out as one launch
-// each.
+// each.  With own_frames (frames of whole 16-row chunks that fit one tile,
+// FrameGeom padded) each CTA takes whole frames and waits only on its own
+// tiles: the layers go out as one launch at any batch.  Needs every
+// activation buffer's frame rows zero from allocation on.
 // withhold_cta >= 0 is a test hook for the failure path: that CTA never
 // publishes its progress, so the CTAs waiting on it (itself included) give up
 // after the bounded wait and report kErrWaitDep in the status word.
 cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool fp16,
                              int grid_limit, unsigned* progress, cudaStream_t stream,
-                             int withhold_cta = -1, int min_tiles = 3);
+                             int withhold_cta = -1, int min_tiles = 3, bool own_frames = false);
 // Number of kernel launches launch_trunk_pix makes for n layers of m_total rows.
-int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit, int min_tiles = 3);
+int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit, int min_tiles = 3,
+                       bool own_frames = false);
 
 // fp32 SIMT path used by the fp32 verification mode.
 cudaError_t launch_conv_simt(const ConvLayer& layer, cudaStream_t stream);

@@ -312,3 +312,27 @@ def test_submitted_batches_match_synchronous_calls(gpu_engine_factory):
     with pytest.raises(RuntimeError):
         e.submit_packed(pack_states(xs[2]), len(xs[2]), np.empty((7, 362), np.float32),
                         np.empty((7,), np.float32))
+
+
+@pytest.mark.parametrize("board,n", [(9, 256), (9, 1024), (9, 17), (9, 5), (5, 64), (13, 100)])
+def test_whole_frame_trunk_matches_the_unpadded_layout(gpu_engine_factory, monkeypatch, board, n):
+    """MG_FRAME_TRUNK=1 on small boards (frame of at most 256 rows): the
+    engine pads the frame stride to whole 16-row chunks and runs the
+    128-channel trunk as one launch of CTAs that own whole frames and wait
+    only on their own tiles.  Against the unpadded layout with the usual
+    schedule: bit-identical, on repeated calls."""
+    sd = weights.make_state_dict(board, 128, 10, seed=8, variant="perturbed")
+    x = host_lib.random_positions(board, n, 31, 60 if board < 19 else 250)
+    monkeypatch.setenv("MG_FRAME_TRUNK", "0")
+    plain = gpu_engine_factory(sd, "bf16", max_batch=max(n, 64))
+    monkeypatch.setenv("MG_FRAME_TRUNK", "1")  # an option, off by default
+    framed = gpu_engine_factory(sd, "bf16", max_batch=max(n, 64))
+    monkeypatch.delenv("MG_FRAME_TRUNK")
+    assert framed.launches_per_forward(n) == 4  # staging, trunk, FC, finish
+    p0, v0, l0 = plain.forward(x)
+    for _ in range(3):
+        p1, v1, l1 = framed.forward(x)
+        assert np.array_equal(l0, l1) and np.array_equal(v0, v1) and np.array_equal(p0, p1)
+    rows = np.array([0, n // 2, n - 1])
+    _, ov, ol = _oracle_rows(sd, x, rows)
+    assert np.abs(l1[rows] - ol).max() < TOL["bf16"]
