@@ -93,9 +93,10 @@ struct mg_engine {
     // the frame stride to whole 16-row chunks and run the trunk as one
     // launch of CTAs that own whole frames (MG_FRAME_TRUNK=1).  Off by
     // default: bit-identical, and measured no faster at 9x9 batch 256
-    // (trunk 250 us either way; 255 us with one frame per tile), where each
-    // layer is bound by streaming its 288 KB of weights per tile through the
-    // 4-stage ring, not by the launches or the cross-CTA waits it removes.
+    // (trunk 250 us either way; 255 us with one frame per tile): with one
+    // tile per CTA each layer's MMA, epilogue and publish run one after
+    // another on every SM, and the launches and cross-CTA waits this
+    // removes were not what that costs.
     int frame_trunk = 0;
     int withhold_cta = -1;  // test hook (MG_TEST_WITHHOLD_PROGRESS): see launch_trunk_pix
     bool use_graphs = true;
