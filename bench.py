@@ -13,9 +13,11 @@ JSON line.  Numbers:
              (256 MB write) before every timed step, CUDA-event timed on the
              engine's stream, max over ranks;
   e2e        the same through the host API with pinned host buffers: H2D of
-             the inputs in the bit-packed wire format (mg_forward_packed),
-             forward, D2H of policy and value, wall-clock timed, max over
-             ranks (e2e_fp32_planes: the same with fp32 planes, mg_forward);
+             the inputs in the bit-packed wire format, forward, D2H of policy
+             and value every step, wall-clock timed, max over ranks; through
+             mg_submit_packed with two steps in flight, as the batching server
+             runs (e2e_sync: one synchronous mg_forward_packed per step;
+             e2e_fp32_planes: fp32 planes through mg_forward);
   roofline   the trunk (all 3x3 convolution layers; the dominant kernel,
              one persistent launch) timed alone with CUDA events:
              algorithmic FLOPs per launch / average launch time, against the
@@ -449,7 +451,42 @@ def measure_predict(wl, args, ranks, world, rank, local, planes_e2e=True):
         barrier()
         return aggregate_rate(world, batch, args.steps, ranks.max(dt))
 
-    e2e = e2e_loop(lambda: eng.forward_packed(bits, batch, out=outs))
+    e2e_sync = e2e_loop(lambda: eng.forward_packed(bits, batch, out=outs))
+
+    # The same through the submission API the batching server uses
+    # (mg_submit_packed / mg_wait_submitted): each step still copies its
+    # bit-packed inputs from pinned host memory and its policy and value back
+    # into pinned host memory, but step k+1's copies and launch are queued
+    # while step k computes (two steps in flight, two sets of pinned buffers).
+    pin_bits = [torch.from_numpy(pack_states(x).view(np.int32)).pin_memory().numpy().view(np.uint32)
+                for _ in range(2)]
+    pin_out = [(torch.empty((batch, actions)).pin_memory().numpy(),
+                torch.empty((batch,)).pin_memory().numpy()) for _ in range(2)]
+    pending = []
+
+    def submitted_step():
+        k = len(pending)
+        b = k & 1
+        pending.append(eng.submit_packed(pin_bits[b], batch, pin_out[b][0], pin_out[b][1]))
+        if len(pending) >= 2:
+            eng.wait_submitted(pending[-2])
+
+    def e2e_submitted():
+        pending.clear()
+        for _ in range(args.warmup):
+            submitted_step()
+        eng.wait_submitted(pending[-1])
+        barrier()
+        pending.clear()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            submitted_step()
+        eng.wait_submitted(pending[-1])  # the last step's results are in host memory
+        dt = time.perf_counter() - t0
+        barrier()
+        return aggregate_rate(world, batch, args.steps, ranks.max(dt))
+
+    e2e = e2e_submitted()
     e2e_planes = None
     if planes_e2e:
         xin = torch.from_numpy(x).pin_memory().numpy()
@@ -479,7 +516,13 @@ def measure_predict(wl, args, ranks, world, rank, local, planes_e2e=True):
         "e2e": {"value": e2e, "unit": "positions/s",
                 "h2d_bytes_per_step": world * batch * words * 4,
                 "d2h_bytes_per_step": world * batch * (actions + 1) * 4,
-                "api": "mg_forward_packed (bit-packed planes, pinned host buffers)"},
+                "api": "mg_submit_packed / mg_wait_submitted (bit-packed planes, pinned host "
+                       "buffers; two steps in flight, as the batching server runs)"},
+        "e2e_sync": {"value": e2e_sync, "unit": "positions/s",
+                     "h2d_bytes_per_step": world * batch * words * 4,
+                     "d2h_bytes_per_step": world * batch * (actions + 1) * 4,
+                     "api": "mg_forward_packed (bit-packed planes, pinned host buffers; one "
+                            "synchronous call per step)"},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
