@@ -308,14 +308,16 @@ void GpuEvaluator::server_loop() {
     for (uint64_t k = 0;; ++k) {
         {
             std::unique_lock<std::mutex> lock(mu_);
+            // The in-flight limit holds even while stopping (two pinned input
+            // buffers); a stop only drops the wait for a full second batch.
             cv_.wait(lock, [&] {
-                if (stop_) return true;
-                if (queue_.empty() || in_flight_ >= max_in_flight_) return false;
-                return in_flight_ == 0 ||
+                if (queue_.empty()) return stop_;
+                if (in_flight_ >= max_in_flight_) return false;
+                return in_flight_ == 0 || stop_ ||
                        queue_.size() >= std::min((size_t)max_batch_,
                                                  overlap_min_ > 0 ? overlap_min_ : last_batch_);
             });
-            if (stop_ && queue_.empty()) break;
+            if (queue_.empty()) break;  // stopping, nothing left
             const int n = std::min((int)queue_.size(), max_batch_);
             batch.assign(queue_.begin(), queue_.begin() + n);
             queue_.erase(queue_.begin(), queue_.begin() + n);
