@@ -100,7 +100,10 @@ struct mg_engine {
     int frame_trunk = 0;
     int withhold_cta = -1;  // test hook (MG_TEST_WITHHOLD_PROGRESS): see launch_trunk_pix
     bool use_graphs = true;
-    int l2_policy = 1;  // keep the residual lo plane resident in L2 (MG_L2_POLICY=0: off)
+    // 1: keep the residual lo plane resident in L2 where it fits (default);
+    // 2: mark it streaming (evict-first) instead; 0: no window
+    // (MG_L2_POLICY).
+    int l2_policy = 1;
     cudaStream_t stream = nullptr;
     std::string err;
 
@@ -464,11 +467,13 @@ struct mg_engine {
             cudaGetLastError();
             return;  // no persisting L2 on this device: nothing to do
         }
-        if (lo_bytes > (size_t)max_persist || lo_bytes > (size_t)max_window) return;
+        const bool streaming = l2_policy == 2;  // evict-first, no set-aside
+        if (!streaming && (lo_bytes > (size_t)max_persist || lo_bytes > (size_t)max_window)) return;
         const size_t window = std::min(lo_bytes, (size_t)max_window);
-        const size_t set_aside = std::min(window, (size_t)max_persist);
-        ck(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, set_aside),
-           "cudaDeviceSetLimit(persisting L2)");
+        const size_t set_aside = streaming ? 0 : std::min(window, (size_t)max_persist);
+        if (set_aside > 0)
+            ck(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, set_aside),
+               "cudaDeviceSetLimit(persisting L2)");
         cudaStreamAttrValue attr = {};
         attr.accessPolicyWindow.base_ptr = d_x;
         attr.accessPolicyWindow.num_bytes = window;
