@@ -67,9 +67,14 @@ namespace {
 constexpr int kCo = 128;        // output channels (MMA M)
 constexpr int kBK = 64;         // K per stage / slab channel block
 constexpr int kMaxPx = 256;     // MMA N limit
-// Weight ring depth, measured: 4 beats 3 and 5 by about 1.5%; 6 and 7 take
-// the kernel past 196 KB of shared memory, where the carve-out leaves the
-// epilogue's residual loads much less L1, and lose 5-10%.
+// Weight ring depth, measured: 4 beats 3 and every deeper ring.  With the
+// ring index advanced incrementally (no division) and the head layer's
+// slots aliased onto the store staging, 5, 6 and 8 stages ran the 19x19
+// batch-512 trunk in 1040, 1045 and 1094 us against 1015 us, and the 9x9
+// batch-256 trunk in 254, 256 and 260 us against 252 us, though a stage's
+// round trip (about 1 us from its TMA load to the commit that frees it)
+// bounds a ring of 4 near the MMA's rate.  Weight loads further ahead take
+// L2 bandwidth from the slab and residual loads that the layer waits on.
 constexpr int kStages = 4;
 constexpr int kSlabs = 2;       // activation slab ring depth
 constexpr int kEpiWarps = 12;   // epilogue warps: kPar per TMEM lane quarter
@@ -409,16 +414,18 @@ __device__ __forceinline__ bool epilogue_layer(const PixArgs& a, const Geo G, in
             // This warp's stores of the tile are done (the warp barrier
             // orders every lane's stores before lane 0's release).  The
             // epilogue warps count themselves in at CTA scope; the last one,
-            // whose acquire sees the others' stores, alone pays for the
-            // GPU-scope fences and publishes the CTA's count of finished
-            // tiles (a full fence in every warp stalled the epilogue).
+            // whose acquire sees the others' stores, publishes the CTA's
+            // count of finished tiles with a GPU-scope release.  Causality
+            // order is transitive, so that release covers every warp's
+            // stores: no full fence is needed (one before it cost 0.5 us per
+            // tile, measured; a full fence in every warp stalled the
+            // epilogue).
             __syncwarp();
             if (lane == 0) {
                 const unsigned before = atom_add_acq_rel_cta(smem_u32(&tcount[acc]), 1u);
                 if (before == (unsigned)(kEpiWarps * use + kEpiWarps - 1) &&
                     (int)blockIdx.x != a.withhold_cta) {
                     fence_proxy_async_global();
-                    __threadfence();
                     red_max_release_gpu(&progress[blockIdx.x], (unsigned)(l * nt + q + 1));
                 }
             }
@@ -948,11 +955,11 @@ cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool f
         }
         return cudaSuccess;
     }
-    // With few tiles per CTA a tile of the next layer depends on most of the
-    // CTA's range and its neighbours' of the layer before, so one launch per
-    // layer (programmatic dependent launches) is faster than the cross-CTA
-    // handoff (measured: 19x19 batch 64 and 9x9 batch 256, one or two tiles
-    // per CTA).
+    // Below min_tiles tiles per CTA, one launch per layer (programmatic
+    // dependent launches).  The engine's default of 1 never takes this path:
+    // the persistent launch measured faster at every batch (19x19 batch 32
+    // to 384 and 9x9 batch 64 to 768, 1 to 4 tiles per CTA: 1-3% at one
+    // tile, 5-6% at two, 16-18% at three).
     if (n > 0 && !trunk_in_one_launch(layers[0].m_total, max_npx, grid_limit, min_tiles)) {
         for (int l = 0; l < n; ++l) {
             cudaError_t e = launch_layers(layers + l, 1, max_npx, fp16, grid_limit, nullptr, stream);

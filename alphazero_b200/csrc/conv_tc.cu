@@ -528,15 +528,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // This warp's stores of the tile are done (the warp
                     // barrier orders every lane's stores before lane 0's
                     // release).  The epilogue warps count themselves in at CTA
-                    // scope; the last one alone pays for the GPU-scope fences
-                    // and publishes the CTA's count of finished tiles.
+                    // scope; the last one, whose acquire sees the others'
+                    // stores, publishes the CTA's count of finished tiles with
+                    // a GPU-scope release, which (causality order being
+                    // transitive) covers every warp's stores.
                     __syncwarp();
                     if (lane == 0) {
                         const unsigned before = atom_add_acq_rel_cta(smem_u32(&tcount[acc]), 1u);
                         if (before == (unsigned)(kEpiWarps * use + kEpiWarps - 1) &&
                             (int)blockIdx.x != a.withhold_cta) {
                             fence_proxy_async_global();
-                            __threadfence();
                             red_max_release_gpu(&a.progress[blockIdx.x], (unsigned)(l * nt + q + 1));
                         }
                     }

@@ -83,11 +83,11 @@ struct mg_engine {
     int pix_mode = 1;      // 1: pixels-on-N kernel for 128-channel layers
     int pix_npx = 0;       // pixels per tile override (0 = heuristic)
     int pix_trunk = 1;     // 1: all 128-channel trunk layers as one persistent launch
-    int pix_trunk_min_tiles = 3;  // ... when every CTA gets at least this many tiles
+    int pix_trunk_min_tiles = 1;  // ... when every CTA gets at least this many tiles
     // 1: 64/256-channel trunk layers as persistent launches.  Off by default:
     // measured no faster than one launch per layer (19x19 b20c256 batch
-    // 1024: equal within noise; 9x9 b6c64 batch 16, one tile per CTA: 7%
-    // slower, the cross-CTA publish and poll cost more than a launch).
+    // 1024: 0-1% slower, within the power-capped clock's noise; 9x9 b6c64
+    // batch 16, one tile per CTA: 3% slower, 86 against 82 us per forward).
     int tc_trunk = 0;
     // 1: on boards whose frame fits one tile of the 128-channel kernel, pad
     // the frame stride to whole 16-row chunks and run the trunk as one

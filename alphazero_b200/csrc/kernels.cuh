@@ -134,9 +134,9 @@ cudaError_t configure_conv_pix();
 // after the bounded wait and report kErrWaitDep in the status word.
 cudaError_t launch_trunk_pix(const ConvLayer* layers, int n, int max_npx, bool fp16,
                              int grid_limit, unsigned* progress, cudaStream_t stream,
-                             int withhold_cta = -1, int min_tiles = 3, bool own_frames = false);
+                             int withhold_cta = -1, int min_tiles = 1, bool own_frames = false);
 // Number of kernel launches launch_trunk_pix makes for n layers of m_total rows.
-int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit, int min_tiles = 3,
+int trunk_pix_launches(int m_total, int n, int max_npx, int grid_limit, int min_tiles = 1,
                        bool own_frames = false);
 
 // fp32 SIMT path used by the fp32 verification mode.

@@ -256,11 +256,11 @@ def test_persistent_trunk_matches_per_layer_launches(gpu_engine_factory, monkeyp
                                                      blocks, n):
     """The all-layers persistent launch (per-CTA progress counters between
     layers) against one launch per layer: bit-identical.  128 channels: the
-    same kernel (conv_pix.cu); 19x19 batch 512 / 300 and 9x9 batch 1024 run
-    as one launch, the small batches fall back to one launch per layer in
-    both engines.  64 / 256 channels (conv_tc.cu): the persistent launch
-    tiles every layer with all output channels, the per-layer launches may
-    split them (small batches); the sums do not depend on that."""
+    same kernel (conv_pix.cu), as one launch at every batch, down to a
+    single tile on a few CTAs (9x9 batch 5).  64 / 256 channels
+    (conv_tc.cu): the persistent launch tiles every layer with all output
+    channels, the per-layer launches may split them (small batches); the
+    sums do not depend on that."""
     sd = weights.make_state_dict(board, filters, blocks, seed=5, variant="perturbed")
     x = host_lib.random_positions(board, n, 99, 250 if board == 19 else 60)
     env = "MG_PIX_TRUNK" if filters == 128 else "MG_TC_TRUNK"
@@ -269,8 +269,7 @@ def test_persistent_trunk_matches_per_layer_launches(gpu_engine_factory, monkeyp
     monkeypatch.setenv(env, "1")
     trunk = gpu_engine_factory(sd, "bf16", max_batch=max(n, 64))
     monkeypatch.delenv(env)
-    if filters != 128:
-        assert trunk.launches_per_forward(n) < per_layer.launches_per_forward(n)
+    assert trunk.launches_per_forward(n) < per_layer.launches_per_forward(n)
     p0, v0, l0 = per_layer.forward(x)
     for _ in range(3):  # repeated launches reuse the progress counters
         p1, v1, l1 = trunk.forward(x)
