@@ -24,8 +24,10 @@
 //   warps 2-9  epilogue: tcgen05.ld of the accumulator, folded-BN bias,
 //              residual add (the stream is a 16-bit hi plane, the operand,
 //              plus an fp16 remainder plane lo, both pixel-major), ReLU,
-//              frame masking, the sum re-split into hi and lo and stored
-//              with 16-byte accesses, and optionally the fused policy/value 1x1 head
+//              frame masking, the sum re-split into hi and lo, each plane
+//              staged per warp in shared memory ([32 rows][32 channels],
+//              64-byte swizzle) and written by one TMA store, and
+//              optionally the fused policy/value 1x1 head
 //              projection (one thread owns one pixel row, so when a tile
 //              spans all output channels it sees the whole channel vector).
 // The epilogue of tile t overlaps the main loop of tile t+1.
@@ -61,11 +63,13 @@ struct TcConfig {
     static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 8 : 12);
     static constexpr uint32_t kBBytes = BN * kBK * 2;
     static constexpr uint32_t kTmemCols = 2 * BN;
-    // B ring + barriers, tmem slot and tile counters (512) + head weights
-    // (3 x 256 floats) + head exchange (2 x 128 x 3 floats) + two layers'
-    // biases (2 x 256 floats, 16-byte aligned) + 1 KB alignment slack; the
-    // two slabs come on top (slab_bytes).
-    static constexpr int kSmemFixed = kStages * kBBytes + 512 + 3072 + 3072 + 2048 + 16 + 1024;
+    // B ring + output staging (kStageBytes per epilogue warp) + barriers,
+    // tmem slot and tile counters (512) + head weights (3 x 256 floats) +
+    // head exchange (2 x 128 x 3 floats) + two layers' biases (2 x 256
+    // floats, 16-byte aligned) + 1 KB alignment slack; the two slabs come
+    // on top (slab_bytes).
+    static constexpr int kSmemFixed =
+        kStages * kBBytes + kEpiWarps * 4096 + 512 + 3072 + 3072 + 2048 + 16 + 1024;
 };
 
 // Rows of an activation slab: the tile's 128 rows plus RS + 1 on each side,
@@ -84,7 +88,7 @@ struct TcLayer {
     int wmap;                // weight tensor map (0 or 1)
     int wrow;                // first row of this layer's weights in that map
     int head;                // fused head projection (last trunk layer)
-    int pad[1];
+    int omap;                // output tensor maps: hi plane (bits 0-1), lo plane (bits 2-3)
 };
 static_assert(sizeof(TcLayer) == 64, "TcLayer layout");
 
@@ -146,7 +150,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tmA1,
                       const __grid_constant__ CUtensorMap tmA2,
                       const __grid_constant__ CUtensorMap tmB0,
-                      const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ TcArgs a) {
+                      const __grid_constant__ CUtensorMap tmB1,
+                      const __grid_constant__ CUtensorMap tmO0,
+                      const __grid_constant__ CUtensorMap tmO1,
+                      const __grid_constant__ CUtensorMap tmO2, const __grid_constant__ TcArgs a) {
     using Cfg = TcConfig<BN>;
     using P = Act16<FP16>;
     constexpr int S = Cfg::kStages;
@@ -158,7 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t slab_bytes = (uint32_t)tc_slab_rows(a.rs) * 128u;
     uint8_t* sSlab = smem;                   // 2 slabs (multiples of 2 KB: atoms stay aligned)
     uint8_t* sB = smem + 2 * slab_bytes;     // S B stages
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+    // Output staging, 4 KB per epilogue warp: two [32 rows][64 B] blocks in
+    // the 64-byte swizzle of the output tensor maps (1 KB aligned).
+    uint8_t* sOut = sB + S * Cfg::kBBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kEpiWarps * 4096);
     uint64_t* full = bars;
     uint64_t* empty = bars + S;
     uint64_t* tfull = bars + 2 * S;
@@ -372,7 +382,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int kCols = BN / 2;
         constexpr int kChunks = kCols / 32;
         const int row = quarter * 32 + lane;
-        int t = 0;
+        uint8_t* const stg = sOut + (warp - 2) * 4096;
+        const bool l1_res = a.n_layers == 1;  // see the residual loads
+        const CUtensorMap* const omaps[3] = {&tmO0, &tmO1, &tmO2};
+        if (lane == 0)
+            for (int i = 0; i < 3; ++i) prefetch_tensormap(omaps[i]);
+        int t = 0, sc = 0;
         bool ok = true;
         for (int l = 0; l < a.n_layers && ok; ++l) {
             // the layer's bias (bulk-copied by the weight producer)
@@ -389,6 +404,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint16_t* const out16 = a.layer[l].out16;
             uint16_t* const out_lo = a.layer[l].out_lo;
             const bool head = a.layer[l].head != 0;
+            const CUtensorMap* const map_hi = omaps[a.layer[l].omap & 3];
+            const CUtensorMap* const map_lo = omaps[(a.layer[l].omap >> 2) & 3];
+            // The staging buffers change roles between layers (two hi
+            // buffers without a lo plane, one each with it): every store
+            // of the layer before has read its buffer first.
+            if (lane == 0) bulk_wait_read();
+            __syncwarp();
             for (int q = 0; q < nt; ++q, ++t) {
                 const int u = u0 + tile_at(blockIdx.x, q, nt);
                 const int m0 = (u / a.nsplit) * kBM;
@@ -413,18 +435,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool has_res = res_hi != nullptr && in_range;
                 // The first chunk's residual (32 hi and 32 lo values, 4 + 4
                 // 16-byte loads) is requested before the accumulator is ready;
-                // each later chunk's one chunk ahead.  Ordinary L1-cached loads:
-                // a lane's 16 bytes are half a sector whose other half the
-                // next load reads (each row is read before it is overwritten in
-                // place, and never read again by this layer).
+                // each later chunk's one chunk ahead.  With one layer per
+                // launch, ordinary L1-cached loads: a lane's 16 bytes are half
+                // a sector whose other half the next load reads (each row is
+                // read before it is overwritten in place, and never read
+                // again by this launch).  A launch of several layers reads
+                // the rows again two layers on, after its own TMA stores
+                // (which bypass L1) rewrote them: there the loads skip L1.
                 uint4 rh[4], rl[4];
                 if (has_res) {
                     const uint4* ph = reinterpret_cast<const uint4*>(res_hi + off);
                     const uint4* pl = reinterpret_cast<const uint4*>(res_lo + off);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
-                        rh[q4] = ph[q4];
-                        rl[q4] = pl[q4];
+                        rh[q4] = l1_res ? ph[q4] : __ldcg(ph + q4);
+                        rl[q4] = l1_res ? pl[q4] : __ldcg(pl + q4);
                     }
                 }
                 ok = mbar_wait(smem_u32(&tfull[acc]), use & 1, a.err, kErrWaitEpilogue);
@@ -443,7 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t v[32];
                     tmem_ld_32cols(tbase + (uint32_t)c0, v);
                     tmem_ld_wait();
-                    if (!in_range) continue;
+                    // Rows past the end go through with zeros (the warp
+                    // stages and stores together; the store clips them).
                     float f[32];
                     // the layer's folded-BN bias (the same 32 values in every lane)
 #pragma unroll
@@ -467,30 +493,70 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint4* pl = reinterpret_cast<const uint4*>(res_lo + off + c0 + 32);
 #pragma unroll
                             for (int q4 = 0; q4 < 4; ++q4) {
-                                rh[q4] = ph[q4];
-                                rl[q4] = pl[q4];
+                                rh[q4] = l1_res ? ph[q4] : __ldcg(ph + q4);
+                                rl[q4] = l1_res ? pl[q4] : __ldcg(pl + q4);
                             }
                         }
                     }
 #pragma unroll
                     for (int j = 0; j < 32; ++j) f[j] = board_px ? fmaxf(f[j], 0.0f) : 0.0f;
                     if (out16 != nullptr) {
-                        uint4* oh = reinterpret_cast<uint4*>(out16 + off + c0);
-                        uint4* ol = reinterpret_cast<uint4*>(out_lo + off + c0);
+                        // This warp's [32 rows][32 channels] block of each
+                        // plane goes through a shared-memory block and one
+                        // TMA store: 32 rows per instruction in 16-byte
+                        // pieces made 32 separate writes each (measured: the
+                        // hi/lo stores took 27% of the 256-filter trunk).
+                        // Lane = row; its 16-byte piece q4 sits at chunk
+                        // q4 ^ ((row >> 1) & 3) of the row (64-byte swizzle,
+                        // conflict-free for the 8 lanes of a store phase).
+                        // With a lo plane, hi uses block 0 and lo block 1;
+                        // without, the hi blocks alternate.  A block is
+                        // rewritten only after the store issued from it
+                        // has read it (at most one newer group pending).
+                        const int y0 = m0 + quarter * 32;
+                        const bool store = y0 < a.m_total;  // warp-uniform
+                        uint8_t* const sh = stg + (out_lo != nullptr ? 0 : (sc & 1)) * 2048 + lane * 64;
+                        uint8_t* const sl = stg + 2048 + lane * 64;
+                        const int swz = (lane >> 1) & 3;
+                        if (lane == 0) bulk_wait_read_n<1>();
+                        __syncwarp();
+                        uint32_t lw[16];
 #pragma unroll
                         for (int q4 = 0; q4 < 4; ++q4) {
-                            uint32_t hw4[4], lw4[4];
+                            uint32_t hw4[4];
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
                                 const float x0 = f[q4 * 8 + 2 * e], x1 = f[q4 * 8 + 2 * e + 1];
                                 hw4[e] = P::pack(x0, x1);
                                 const float2 hv = P::unpack(hw4[e]);
                                 const __half2 lv = __floats2half2_rn(x0 - hv.x, x1 - hv.y);
-                                lw4[e] = *reinterpret_cast<const uint32_t*>(&lv);
+                                lw[q4 * 4 + e] = *reinterpret_cast<const uint32_t*>(&lv);
                             }
-                            oh[q4] = make_uint4(hw4[0], hw4[1], hw4[2], hw4[3]);
-                            if (out_lo != nullptr) ol[q4] = make_uint4(lw4[0], lw4[1], lw4[2], lw4[3]);
+                            *reinterpret_cast<uint4*>(sh + ((q4 ^ swz) << 4)) =
+                                make_uint4(hw4[0], hw4[1], hw4[2], hw4[3]);
                         }
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0 && store) {
+                            tma_store_2d(map_hi, smem_u32(stg + (out_lo != nullptr ? 0 : (sc & 1)) * 2048),
+                                         cbase + c0, y0);
+                            bulk_commit();
+                        }
+                        if (out_lo != nullptr) {
+                            if (lane == 0) bulk_wait_read_n<1>();
+                            __syncwarp();
+#pragma unroll
+                            for (int q4 = 0; q4 < 4; ++q4)
+                                *reinterpret_cast<uint4*>(sl + ((q4 ^ swz) << 4)) =
+                                    make_uint4(lw[q4 * 4], lw[q4 * 4 + 1], lw[q4 * 4 + 2], lw[q4 * 4 + 3]);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0 && store) {
+                                tma_store_2d(map_lo, smem_u32(stg + 2048), cbase + c0, y0);
+                                bulk_commit();
+                            }
+                        }
+                        ++sc;
                     }
                     if (head) {
                         const float* w0 = shead + cbase + c0;
@@ -525,6 +591,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
                 if (a.progress != nullptr) {
+                    if (lane == 0) {
+                        // this warp's TMA stores of the tile have landed
+                        bulk_wait_all();
+                        fence_proxy_async_global();
+                    }
                     // This warp's stores of the tile are done (the warp
                     // barrier orders every lane's stores before lane 0's
                     // release).  The epilogue warps count themselves in at CTA
@@ -548,6 +619,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(smem_u32(&bempty[bb]));
         }
+        // every TMA store has landed before the CTA exits
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -572,7 +646,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 bool encode_2d(CUtensorMap* map, bool fp16, const void* base, uint64_t inner, uint64_t rows,
-               uint32_t box_inner, uint32_t box_rows, const char** why) {
+               uint32_t box_inner, uint32_t box_rows, const char** why,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     auto enc = tensor_map_encoder();
     if (enc == nullptr) {
         *why = "cuTensorMapEncodeTiled unavailable";
@@ -584,11 +659,47 @@ bool encode_2d(CUtensorMap* map, bool fp16, const void* base, uint64_t inner, ui
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                      2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         *why = "cuTensorMapEncodeTiled rejected the tensor map";
         return false;
+    }
+    return true;
+}
+
+// Output maps of a launch: up to three distinct 16-bit [m_total][cout]
+// buffers (hi planes and lo planes alike; a store copies bytes), box of 32
+// channels x 32 rows (one epilogue warp's chunk), 64-byte swizzle.  Sets
+// each layer's omap; unused maps describe a valid dummy that is never
+// written.
+bool output_maps(const ConvLayer* layers, int n, TcArgs& a, bool fp16, CUtensorMap* tmO,
+                 const char** why) {
+    const void* outs[3] = {nullptr, nullptr, nullptr};
+    int no = 0;
+    auto slot = [&](const void* p) {
+        if (p == nullptr) return 0;
+        for (int i = 0; i < no; ++i)
+            if (outs[i] == p) return i;
+        if (no == 3) return -1;
+        outs[no] = p;
+        return no++;
+    };
+    for (int l = 0; l < n; ++l) {
+        const int h = slot(layers[l].out16), lo = slot(layers[l].out_lo);
+        if (h < 0 || lo < 0) {
+            *why = "more than three output buffers in one launch";
+            return false;
+        }
+        a.layer[l].omap = h | (lo << 2);
+    }
+    const ConvLayer& F = layers[0];
+    for (int i = 0; i < 3; ++i) {
+        const void* base = i < no ? outs[i] : (no > 0 ? outs[0] : F.in);
+        const uint64_t inner = no > 0 ? (uint64_t)F.cout : (uint64_t)F.cin;
+        if (!encode_2d(&tmO[i], fp16, base, inner, (uint64_t)F.m_total, 32, 32, why,
+                       CU_TENSOR_MAP_SWIZZLE_64B))
+            return false;
     }
     return true;
 }
@@ -641,8 +752,8 @@ int tc_args(const ConvLayer& F, int nsplit, int grid_limit, TcArgs& a) {
 }
 
 template <int BN, bool FP16>
-cudaError_t launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmB, const TcArgs& a, int grid,
-                      bool cooperative, cudaStream_t stream) {
+cudaError_t launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUtensorMap* tmO,
+                      const TcArgs& a, int grid, bool cooperative, cudaStream_t stream) {
     using Cfg = TcConfig<BN>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -663,22 +774,23 @@ cudaError_t launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmB, const TcAr
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, conv3x3_tc_kernel<BN, FP16>, tmA[0], tmA[1], tmA[2], tmB[0],
-                              tmB[1], a);
+                              tmB[1], tmO[0], tmO[1], tmO[2], a);
 }
 
 cudaError_t launch_tc_any(int bn, bool fp16, const CUtensorMap* tmA, const CUtensorMap* tmB,
-                          const TcArgs& a, int grid, bool cooperative, cudaStream_t stream) {
+                          const CUtensorMap* tmO, const TcArgs& a, int grid, bool cooperative,
+                          cudaStream_t stream) {
     if (fp16) {
         switch (bn) {
-            case 64: return launch_tc<64, true>(tmA, tmB, a, grid, cooperative, stream);
-            case 128: return launch_tc<128, true>(tmA, tmB, a, grid, cooperative, stream);
-            case 256: return launch_tc<256, true>(tmA, tmB, a, grid, cooperative, stream);
+            case 64: return launch_tc<64, true>(tmA, tmB, tmO, a, grid, cooperative, stream);
+            case 128: return launch_tc<128, true>(tmA, tmB, tmO, a, grid, cooperative, stream);
+            case 256: return launch_tc<256, true>(tmA, tmB, tmO, a, grid, cooperative, stream);
         }
     } else {
         switch (bn) {
-            case 64: return launch_tc<64, false>(tmA, tmB, a, grid, cooperative, stream);
-            case 128: return launch_tc<128, false>(tmA, tmB, a, grid, cooperative, stream);
-            case 256: return launch_tc<256, false>(tmA, tmB, a, grid, cooperative, stream);
+            case 64: return launch_tc<64, false>(tmA, tmB, tmO, a, grid, cooperative, stream);
+            case 128: return launch_tc<128, false>(tmA, tmB, tmO, a, grid, cooperative, stream);
+            case 256: return launch_tc<256, false>(tmA, tmB, tmO, a, grid, cooperative, stream);
         }
     }
     return cudaErrorInvalidValue;
@@ -737,7 +849,10 @@ cudaError_t launch_conv_tc(const ConvLayer& L, const CUtensorMap& tmA, const CUt
     a.feat = L.feat;
     const CUtensorMap A[3] = {tmA, tmA, tmA};
     const CUtensorMap B[2] = {tmB, tmB};
-    return launch_tc_any(bn, fp16, A, B, a, grid, false, stream);
+    CUtensorMap O[3];
+    const char* why = "";
+    if (!output_maps(&L, 1, a, fp16, O, &why)) return cudaErrorInvalidValue;
+    return launch_tc_any(bn, fp16, A, B, O, a, grid, false, stream);
 }
 
 bool trunk_tc_supported(const ConvLayer* layers, int n) {
@@ -809,11 +924,13 @@ cudaError_t launch_trunk_tc(const ConvLayer* layers, int n, bool fp16, int grid_
                    n > 1 ? (uint64_t)9 * bn : (uint64_t)9 * F.cin,
                    n > 1 ? (uint64_t)(n - 1) * bn : (uint64_t)bn, kBK, (uint32_t)bn, &why))
         return cudaErrorInvalidValue;
+    CUtensorMap O[3];
+    if (!output_maps(layers, n, a, fp16, O, &why)) return cudaErrorInvalidValue;
     if (n > 1) {
         cudaError_t e = cudaMemsetAsync(progress, 0, (size_t)grid * sizeof(unsigned), stream);
         if (e != cudaSuccess) return e;
     }
-    return launch_tc_any(bn, fp16, A, B, a, grid, n > 1, stream);
+    return launch_tc_any(bn, fp16, A, B, O, a, grid, n > 1, stream);
 }
 
 int trunk_tc_max_layers() { return kMaxLayers; }
