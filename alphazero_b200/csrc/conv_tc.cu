@@ -383,7 +383,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int kChunks = kCols / 32;
         const int row = quarter * 32 + lane;
         uint8_t* const stg = sOut + (warp - 2) * 4096;
-        const bool l1_res = a.n_layers == 1;  // see the residual loads
         const CUtensorMap* const omaps[3] = {&tmO0, &tmO1, &tmO2};
         if (lane == 0)
             for (int i = 0; i < 3; ++i) prefetch_tensormap(omaps[i]);
@@ -433,24 +432,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const size_t off = (size_t)m * a.cout + cbase;
                 const bool has_res = res_hi != nullptr && in_range;
-                // The first chunk's residual (32 hi and 32 lo values, 4 + 4
-                // 16-byte loads) is requested before the accumulator is ready;
-                // each later chunk's one chunk ahead.  With one layer per
-                // launch, ordinary L1-cached loads: a lane's 16 bytes are half
-                // a sector whose other half the next load reads (each row is
-                // read before it is overwritten in place, and never read
-                // again by this launch).  A launch of several layers reads
-                // the rows again two layers on, after its own TMA stores
-                // (which bypass L1) rewrote them: there the loads skip L1.
-                uint4 rh[4], rl[4];
+                // The first chunk's residual (32 hi and 32 lo values: each
+                // plane's 64 contiguous bytes of the row as two 32-byte,
+                // whole-sector loads) is requested before the accumulator is
+                // ready; each later chunk's one chunk ahead.  L2-only: a
+                // launch of several layers reads the rows again two layers
+                // on, after its own TMA stores (which bypass L1) rewrote
+                // them.  Every address is 32-byte aligned: buffers are
+                // 256-byte aligned, rows are cout * 2 bytes and chunks start
+                // at multiples of 32 channels.
+                uint32_t rh[16], rl[16];
                 if (has_res) {
-                    const uint4* ph = reinterpret_cast<const uint4*>(res_hi + off);
-                    const uint4* pl = reinterpret_cast<const uint4*>(res_lo + off);
-#pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        rh[q4] = l1_res ? ph[q4] : __ldcg(ph + q4);
-                        rl[q4] = l1_res ? pl[q4] : __ldcg(pl + q4);
-                    }
+                    ld_cg_v8(res_hi + off, rh);
+                    ld_cg_v8(res_hi + off + 16, rh + 8);
+                    ld_cg_v8(res_lo + off, rl);
+                    ld_cg_v8(res_lo + off + 16, rl + 8);
                 }
                 ok = mbar_wait(smem_u32(&tfull[acc]), use & 1, a.err, kErrWaitEpilogue);
                 // Leave together: no epilogue warp may be left at a named barrier.
@@ -476,26 +472,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + bias[cbase + c0 + j];
                     if (has_res) {
 #pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) {
-                            const uint32_t hw4[4] = {rh[q4].x, rh[q4].y, rh[q4].z, rh[q4].w};
-                            const uint32_t lw4[4] = {rl[q4].x, rl[q4].y, rl[q4].z, rl[q4].w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float2 hv = P::unpack(hw4[e]);
-                                const float2 lv =
-                                    __half22float2(*reinterpret_cast<const __half2*>(&lw4[e]));
-                                f[q4 * 8 + 2 * e] += hv.x + lv.x;
-                                f[q4 * 8 + 2 * e + 1] += hv.y + lv.y;
-                            }
+                        for (int w = 0; w < 16; ++w) {
+                            const float2 hv = P::unpack(rh[w]);
+                            const float2 lv = __half22float2(*reinterpret_cast<const __half2*>(&rl[w]));
+                            f[2 * w] += hv.x + lv.x;
+                            f[2 * w + 1] += hv.y + lv.y;
                         }
                         if (c + 1 < kChunks) {
-                            const uint4* ph = reinterpret_cast<const uint4*>(res_hi + off + c0 + 32);
-                            const uint4* pl = reinterpret_cast<const uint4*>(res_lo + off + c0 + 32);
-#pragma unroll
-                            for (int q4 = 0; q4 < 4; ++q4) {
-                                rh[q4] = l1_res ? ph[q4] : __ldcg(ph + q4);
-                                rl[q4] = l1_res ? pl[q4] : __ldcg(pl + q4);
-                            }
+                            ld_cg_v8(res_hi + off + c0 + 32, rh);
+                            ld_cg_v8(res_hi + off + c0 + 48, rh + 8);
+                            ld_cg_v8(res_lo + off + c0 + 32, rl);
+                            ld_cg_v8(res_lo + off + c0 + 48, rl + 8);
                         }
                     }
 #pragma unroll

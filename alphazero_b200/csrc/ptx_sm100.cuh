@@ -209,6 +209,15 @@ __device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
+// 32-byte global load, L2 only (a whole sector per lane): r[0..7] are the
+// eight 32-bit words at p, which must be 32-byte aligned.
+__device__ __forceinline__ void ld_cg_v8(const void* p, uint32_t* r) {
+    asm volatile("ld.global.cg.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "l"(p));
+}
+
 // Waits until every committed bulk store has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
