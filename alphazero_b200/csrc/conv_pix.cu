@@ -701,31 +701,10 @@ size_t pix_smem_bytes(int npx, int rs) {
            (2 * kStages + 2 * kSlabs + 2 * kMaxBufs + 1) * 8 + 32 + 3 * kCo * 4 + 1024;
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (fn == nullptr) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
-    return fn;
-}
-
 // 2-D tensor map [rows][inner] of `esize`-byte elements.
 bool encode(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, uint64_t inner,
             uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
-    auto enc = encoder();
-    if (enc == nullptr) return false;
-    cuuint64_t dims[2] = {inner, rows};
-    cuuint64_t strides[1] = {inner * (uint64_t)esize};
-    cuuint32_t box[2] = {box_inner, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    return enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return encode_tiled_2d(map, dt, esize, base, inner, rows, box_inner, box_rows, sw);
 }
 
 bool layer_ok(const ConvLayer& L, const ConvLayer& first) {

@@ -619,37 +619,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (fn == nullptr) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
-    return fn;
-}
-
 bool encode_2d(CUtensorMap* map, bool fp16, const void* base, uint64_t inner, uint64_t rows,
                uint32_t box_inner, uint32_t box_rows, const char** why,
                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
-    auto enc = tensor_map_encoder();
-    if (enc == nullptr) {
-        *why = "cuTensorMapEncodeTiled unavailable";
-        return false;
-    }
-    cuuint64_t dims[2] = {inner, rows};
-    cuuint64_t strides[1] = {inner * 2};
-    cuuint32_t box[2] = {box_inner, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                     2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-        *why = "cuTensorMapEncodeTiled rejected the tensor map";
+    if (!encode_tiled_2d(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                         2, base, inner, rows, box_inner, box_rows, swizzle)) {
+        *why = "cuTensorMapEncodeTiled rejected the tensor map (or is unavailable)";
         return false;
     }
     return true;
@@ -784,6 +759,52 @@ cudaError_t launch_tc_any(int bn, bool fp16, const CUtensorMap* tmA, const CUten
 }
 
 }  // namespace
+
+bool encode_tiled_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base,
+                     uint64_t inner, uint64_t rows, uint32_t box_inner, uint32_t box_rows,
+                     CUtensorMapSwizzle swizzle) {
+    static PFN_cuTensorMapEncodeTiled_v12000 enc = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        return cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                           cudaSuccess &&
+                       q == cudaDriverEntryPointSuccess
+                   ? reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p)
+                   : nullptr;
+    }();
+    struct Entry {
+        const void* base;
+        uint64_t inner, rows;
+        uint32_t box_inner, box_rows;
+        int dt, esize, swizzle;
+        CUtensorMap map;
+    };
+    constexpr int kEntries = 64;  // a network's launches use a few dozen maps
+    thread_local Entry cache[kEntries];
+    thread_local int used = 0, next = 0;
+    for (int i = 0; i < used; ++i) {
+        const Entry& e = cache[i];
+        if (e.base == base && e.inner == inner && e.rows == rows && e.box_inner == box_inner &&
+            e.box_rows == box_rows && e.dt == (int)dt && e.esize == esize && e.swizzle == (int)swizzle) {
+            *map = e.map;
+            return true;
+        }
+    }
+    if (enc == nullptr) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {inner * (uint64_t)esize};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    Entry& e = cache[next];
+    e = Entry{base, inner, rows, box_inner, box_rows, (int)dt, esize, (int)swizzle, *map};
+    next = (next + 1) % kEntries;
+    if (used < kEntries) ++used;
+    return true;
+}
 
 cudaError_t configure_conv_tc() {
     cudaError_t e;

@@ -96,6 +96,15 @@ cudaError_t launch_trunk_tc(const ConvLayer* layers, int n, bool fp16, int grid_
                             unsigned* progress, cudaStream_t stream, int withhold_cta = -1);
 int trunk_tc_max_layers();
 
+// cuTensorMapEncodeTiled of a dense 2-D [rows][inner] tensor of esize-byte
+// elements, memoised per host thread.  The launchers encode the same maps
+// at every launch (an encode costs microseconds of host time, which made
+// launch-bound paths host-bound); a map depends only on these arguments, so
+// a remembered one is exact.
+bool encode_tiled_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base,
+                     uint64_t inner, uint64_t rows, uint32_t box_inner, uint32_t box_rows,
+                     CUtensorMapSwizzle swizzle);
+
 // Host-side encoding of the two TMA descriptors of a layer.
 bool make_conv_tensor_maps(const ConvLayer& layer, int bn, bool fp16, CUtensorMap* tmA,
                            CUtensorMap* tmB, const char** why);
