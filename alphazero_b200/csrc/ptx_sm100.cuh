@@ -119,6 +119,13 @@ __device__ __forceinline__ bool wait_counter(const unsigned* p, unsigned target,
     }
 }
 
+__device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 // 16-bit global load cached in L2 only, issued exactly where it is written
 // (volatile), so a load meant to run ahead of other work is not sunk next to
 // its use by the scheduler.

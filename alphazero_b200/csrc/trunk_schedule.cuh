@@ -54,16 +54,47 @@ __device__ __forceinline__ bool wait_inputs(const G& g, const unsigned* progress
                                             int m0, int len, int halo) {
     const int lo = max(m0 - halo, 0);
     const int hi = min(m0 + len + halo, g.m_total) - 1;
-    for (int c = lo / g.span; c <= hi / g.span; ++c) {
+    const int c0 = lo / g.span, n = hi / g.span - c0 + 1;
+    // The count each CTA must have published.
+    auto target = [&](int c) {
         const int start = c * g.span;
         const int nt = cta_tiles(g, c);
         const int j0 = (max(lo, start) - start) / g.npx;
         const int j1 = (min(hi, start + g.span - 1) - start) / g.npx;
         const int last = (c & 1) ? order_of(c, j0, nt) : order_of(c, j1, nt);
-        if (!wait_counter(&progress[c], (unsigned)((l - 1) * nt + last + 1), err, kErrWaitDep))
-            return false;
+        return (unsigned)((l - 1) * nt + last + 1);
+    };
+    constexpr int kPoll = 4;
+    if (n > kPoll) {  // many small ranges: one acquire wait per CTA
+        for (int c = c0; c < c0 + n; ++c)
+            if (!wait_counter(&progress[c], target(c), err, kErrWaitDep)) return false;
+        return true;
     }
-    return true;
+    // Up to kPoll counters (the CTA's own and its neighbours'), polled
+    // together with relaxed loads, all in flight at once; once every one has
+    // reached its target, one fence makes the reads an acquire of each
+    // (a strong read followed by fence.acq_rel).  Acquire loads one counter
+    // after another took a round trip to L2 each.
+    unsigned tgt[kPoll];
+#pragma unroll
+    for (int i = 0; i < kPoll; ++i) tgt[i] = i < n ? target(c0 + i) : 0u;
+    const uint64_t t0 = global_timer_ns();
+    for (int round = 0;; ++round) {
+        unsigned v[kPoll];
+#pragma unroll
+        for (int i = 0; i < kPoll; ++i) v[i] = i < n ? ld_relaxed_gpu(&progress[c0 + i]) : 0u;
+        bool all = true;
+#pragma unroll
+        for (int i = 0; i < kPoll; ++i) all = all && v[i] >= tgt[i];
+        if (all) {
+            fence_acq_rel_gpu();
+            return true;
+        }
+        if ((round & 7) == 7 && global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicCAS(err, 0, kErrWaitDep);
+            return false;
+        }
+    }
 }
 
 }  // namespace mgb
