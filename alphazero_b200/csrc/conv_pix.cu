@@ -17,16 +17,17 @@
 //
 // The accumulator is [co lanes][px columns] in TMEM, double-buffered across
 // tiles (2 x 256 columns).  Each epilogue warp works on its own: it owns 32
-// channels (its TMEM lanes) of every third 16-pixel chunk and moves them
-// straight between registers and global memory (lane = channel, so each
-// 16-bit access of a warp covers 64 contiguous bytes of a pixel row).  The
-// residual stream is a pair of 16-bit planes, x = hi + lo with hi = x
+// channels (its TMEM lanes) of every third 16-pixel chunk (lane = channel,
+// so each 16-bit load of a warp covers 64 contiguous bytes of a pixel row).
+// The residual stream is a pair of 16-bit planes, x = hi + lo with hi = x
 // rounded to the operand type (the next layer's input) and lo = x - hi
 // rounded to fp16.  A chunk's residual hi / lo values are loaded one chunk
 // ahead into registers; each thread adds bias and residual, applies ReLU and
-// the frame mask, and stores the sum re-split into hi and lo.  In the last
-// trunk layer the fp32 sums go through shared memory to the policy / value
-// 1x1 head projection instead.
+// the frame mask, and re-splits the sum into hi and lo.  The hi values go
+// through one of the warp's two 1 KB shared-memory staging buffers and one
+// TMA store per chunk; the lo values (16-pixel blocks, contiguous per warp)
+// are stored from registers.  In the last trunk layer the fp32 sums go
+// through shared memory to the policy / value 1x1 head projection instead.
 //
 // Warp roles (480 threads): warp 0 weight TMA producer, warp 1 TMEM
 // allocator + MMA issuer, warps 2-13 epilogue (warp w reads TMEM lanes
@@ -44,8 +45,9 @@
 // + RS + 1), i.e. the CTA's own neighbouring tiles and, at the ends of its
 // range, the nearest tiles of the neighbouring CTAs.  After all 12 epilogue
 // warps have stored a tile, the CTA publishes its count of finished tiles
-// (release, GPU scope); the slab producer waits (acquire) until the tiles
-// it needs are counted before loading a slab.  The same wait covers the
+// (release, GPU scope); the slab producer waits until the tiles it needs
+// are counted (relaxed polls of every counter it needs, then one acquire
+// fence) before loading a slab.  The same wait covers the
 // reverse hazard: a tile's outputs overwrite rows that only those tiles of
 // the layer before read.  Because neighbouring CTAs run in opposite
 // directions, the first tile of layer l needs only tiles that were among the

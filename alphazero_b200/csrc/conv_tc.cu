@@ -16,8 +16,8 @@
 // tap*cin + channel block; B stages stream through a ring.
 //
 // One persistent CTA per SM, warp-specialised:
-//   warp 0     TMA producer (one thread): two slab buffers and a
-//              STAGES-deep ring of B stages;
+//   warp 0     weight producer (one thread): a STAGES-deep ring of B
+//              stages by TMA, and each layer's bias by a bulk copy;
 //   warp 1     TMEM allocator and MMA issuer (one thread): 4 x
 //              tcgen05.mma.kind::f16 (128 x bn x 16) per K block, fp32
 //              accumulators in TMEM, double-buffered across tiles;
@@ -29,7 +29,10 @@
 //              64-byte swizzle) and written by one TMA store, and
 //              optionally the fused policy/value 1x1 head
 //              projection (one thread owns one pixel row, so when a tile
-//              spans all output channels it sees the whole channel vector).
+//              spans all output channels it sees the whole channel vector);
+//   warp 10    activation producer (one thread): the two halo-slab buffers
+//              by TMA, after waiting for the previous layer's tiles when
+//              one launch runs several layers.
 // The epilogue of tile t overlaps the main loop of tile t+1.
 // Every mbarrier wait is bounded (ptx_sm100.cuh); on expiry the kernel
 // records an error code, drains its in-flight copies and frees TMEM.
