@@ -23,27 +23,58 @@
 
 namespace mgb {
 
+// The index arithmetic below is host-callable too, so that the protocol can
+// be checked exhaustively on the CPU (tests/cpp/test_trunk_schedule.cu).
+
 // Number of tiles of CTA c (those of the last CTA may be fewer).
 template <typename G>
-__device__ __forceinline__ int cta_tiles(const G& g, int c) {
+__host__ __device__ __forceinline__ int cta_tiles(const G& g, int c) {
     const int start = c * g.span;
-    const int end = min(start + g.span, g.m_total);
+    const int end = start + g.span < g.m_total ? start + g.span : g.m_total;
     return end > start ? (end - start + g.npx - 1) / g.npx : 0;
 }
 
 // Rows [m0, m0 + len) of CTA c's tile j.
 template <typename G>
-__device__ __forceinline__ void tile_rows(const G& g, int c, int j, int& m0, int& len) {
+__host__ __device__ __forceinline__ void tile_rows(const G& g, int c, int j, int& m0, int& len) {
     const int start = c * g.span;
-    const int end = min(start + g.span, g.m_total);
+    const int end = start + g.span < g.m_total ? start + g.span : g.m_total;
     m0 = start + j * g.npx;
-    len = min(g.npx, end - m0);
+    len = end - m0 < g.npx ? end - m0 : g.npx;
 }
 
 // The tile CTA c takes q-th in each layer, and the position of tile j in
 // that order: even CTAs left to right, odd CTAs right to left.
-__device__ __forceinline__ int tile_at(int c, int q, int nt) { return (c & 1) ? nt - 1 - q : q; }
-__device__ __forceinline__ int order_of(int c, int j, int nt) { return (c & 1) ? nt - 1 - j : j; }
+__host__ __device__ __forceinline__ int tile_at(int c, int q, int nt) {
+    return (c & 1) ? nt - 1 - q : q;
+}
+__host__ __device__ __forceinline__ int order_of(int c, int j, int nt) {
+    return (c & 1) ? nt - 1 - j : j;
+}
+
+// Rows [lo, hi] (inclusive) of layer l-1's output that the tile [m0, m0 +
+// len) of layer l reads: its own rows and `halo` rows on either side,
+// clipped to the tensor.
+template <typename G>
+__host__ __device__ __forceinline__ void input_rows(const G& g, int m0, int len, int halo, int& lo,
+                                                    int& hi) {
+    lo = m0 - halo > 0 ? m0 - halo : 0;
+    hi = (m0 + len + halo < g.m_total ? m0 + len + halo : g.m_total) - 1;
+}
+
+// The count of finished tiles CTA c (which owns some of rows [lo, hi]) must
+// have published before a tile of layer l (>= 1) reads those rows: all its
+// tiles of layers before l-1, and its tiles of layer l-1 up to the last one,
+// in its order, that holds any of the rows.
+template <typename G>
+__host__ __device__ __forceinline__ unsigned wait_target(const G& g, int c, int lo, int hi, int l) {
+    const int start = c * g.span;
+    const int nt = cta_tiles(g, c);
+    const int j0 = ((lo > start ? lo : start) - start) / g.npx;
+    const int j1 = ((hi < start + g.span - 1 ? hi : start + g.span - 1) - start) / g.npx;
+    const int last = (c & 1) ? order_of(c, j0, nt) : order_of(c, j1, nt);
+    return (unsigned)((l - 1) * nt + last + 1);
+}
 
 // Before a tile of layer l (>= 1) reads rows [m0 - halo, m0 + len + halo)
 // of layer l-1's output: waits until every CTA owning some of those rows has
@@ -52,18 +83,10 @@ __device__ __forceinline__ int order_of(int c, int j, int nt) { return (c & 1) ?
 template <typename G>
 __device__ __forceinline__ bool wait_inputs(const G& g, const unsigned* progress, int* err, int l,
                                             int m0, int len, int halo) {
-    const int lo = max(m0 - halo, 0);
-    const int hi = min(m0 + len + halo, g.m_total) - 1;
+    int lo, hi;
+    input_rows(g, m0, len, halo, lo, hi);
     const int c0 = lo / g.span, n = hi / g.span - c0 + 1;
-    // The count each CTA must have published.
-    auto target = [&](int c) {
-        const int start = c * g.span;
-        const int nt = cta_tiles(g, c);
-        const int j0 = (max(lo, start) - start) / g.npx;
-        const int j1 = (min(hi, start + g.span - 1) - start) / g.npx;
-        const int last = (c & 1) ? order_of(c, j0, nt) : order_of(c, j1, nt);
-        return (unsigned)((l - 1) * nt + last + 1);
-    };
+    auto target = [&](int c) { return wait_target(g, c, lo, hi, l); };
     constexpr int kPoll = 4;
     if (n > kPoll) {  // many small ranges: one acquire wait per CTA
         for (int c = c0; c < c0 + n; ++c)
